@@ -1,0 +1,388 @@
+#!/usr/bin/env python3
+"""Benchmark: IQ2_XXS matmul weight GB/s at M=1 (decode GEMV) on Llama-3-8B-shaped projections.
+
+Workload (benchmark configuration 1 at M=1): the 7 projections of a Llama-3-8B layer
+(q 4096x4096, k/v 4096x1024, o 4096x4096, gate/up 4096x14336, down 14336x4096; K x N), IQ2_XXS
+weights with the benchmark block distribution, f32 N(0,1) activations, repeated over 32
+distinct layers (1.80 GB of packed weights, > 14x the 126 MB L2, so no step reads weights from
+L2). One step = the 224 projections, each through the library's public call. Synthetic data.
+
+  value   = packed weight bytes per step / device time per step (CUDA events on the launch stream
+            around K back-to-back replays of a CUDA graph holding one step; inputs resident)
+  e2e     = the same metric, each step also copying every projection's x host->device from
+            pinned memory and every output device->host (stream-ordered, inside the timed region)
+  roofline: the dominant kernel (the decode GEMV of a 4096x14336 gate/up projection) timed alone
+            with CUDA events (64 distinct matrices in rotation, > L2), against measured HBM BW.
+  cpu_baseline: the reference's own kernels (compiled from source for the host, all threads) on
+            a bounded sample of the same workload.
+
+--gpus N > 1 (launched by torchrun, one rank per GPU): every projection is column-sharded over
+the N ranks (rank r computes output columns [r*N/g, (r+1)*N/g) from its contiguous slice of the
+weight rows), and the output slices of the step are all-gathered with NCCL over NVLink and put
+back in [m, N] order -- strong scaling of the same workload; value = whole-job weight bytes/s.
+
+--impl reference: the reference's own kernels on the host cores (see above), same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "IQ2_XXS matmul: weight GB/s at M=1, TFLOPS at M=2048, % of roofline"
+LAYERS = 32
+
+
+def _peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 100 ms while active."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.file.name)
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------- ours
+class Workload:
+    """Device-resident weights, inputs, outputs and workspaces of one step, optionally sharded."""
+
+    def __init__(self, m: int, layers: int, rank: int, world: int, device: torch.device):
+        from candelora_metal_kernels_b200 import synth, workspace_bytes
+        self.m, self.device, self.rank, self.world = m, device, rank, world
+        self.calls = []  # (x_view, qs, sc, n_local, k, out_view, ws)
+        self.weight_bytes = 0        # whole-job packed bytes per step
+        self.local_weight_bytes = 0
+        x_elems = out_elems = 0
+        specs = []
+        for layer in range(layers):
+            for pi, (name, k, n) in enumerate(synth.LLAMA3_8B_PROJECTIONS):
+                n_loc = n // world
+                specs.append((layer, pi, name, k, n, n_loc, x_elems, out_elems))
+                x_elems += m * k
+                out_elems += m * n_loc
+                self.weight_bytes += synth.packed_bytes(n, k)
+                self.local_weight_bytes += synth.packed_bytes(n_loc, k)
+        self.x_dev = torch.empty(x_elems, dtype=torch.float32, device=device)
+        self.out_dev = torch.empty(out_elems, dtype=torch.float32, device=device)
+        self.x_host = torch.empty(x_elems, dtype=torch.float32, pin_memory=True)
+        self.out_host = torch.empty(out_elems, dtype=torch.float32, pin_memory=True)
+        ws_cache = {}
+        for (layer, pi, name, k, n, n_loc, xo, oo) in specs:
+            seed = layer * 16 + pi
+            qs, sc = synth.iq2xxs_weights(n, k, seed, device=device, row_begin=rank * n_loc,
+                                          row_end=(rank + 1) * n_loc)
+            x = synth.activations(m, k, seed=10_000 + seed)
+            self.x_host[xo:xo + m * k].copy_(x.reshape(-1))
+            key = (n_loc, k)
+            if key not in ws_cache:  # one workspace per shape is enough: calls are stream-ordered
+                ws_cache[key] = torch.empty(max(workspace_bytes(m, n_loc, k, torch.float32), 1),
+                                            dtype=torch.uint8, device=device)
+            self.calls.append((self.x_dev[xo:xo + m * k].view(m, k), qs, sc, n_loc, k,
+                               self.out_dev[oo:oo + m * n_loc].view(m, n_loc), ws_cache[key], name))
+        self.x_dev.copy_(self.x_host)
+        self.gathered = None
+        if world > 1:
+            self.gathered = torch.empty(world * out_elems, dtype=torch.float32, device=device)
+            self.full_out = torch.empty(world * out_elems, dtype=torch.float32, device=device)
+
+    def step(self):
+        from candelora_metal_kernels_b200 import iq2_xxs_matmul
+        for (x, qs, sc, n, k, out, ws, _) in self.calls:
+            iq2_xxs_matmul(x, qs, sc, n, k, out=out, workspace=ws)
+        if self.world > 1:
+            torch.distributed.all_gather_into_tensor(self.gathered, self.out_dev)
+
+    def launches_per_step(self) -> int:
+        return 2 * len(self.calls)  # x-limb prep + decode GEMV per projection
+
+
+def _time_graph(graph, steps: int, stream) -> float:
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+def run_ours(args, rank: int, world: int, local_rank: int):
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    import candelora_metal_kernels_b200 as c
+    from candelora_metal_kernels_b200 import synth
+    c._lib.load()
+    dist = world > 1
+    wl = Workload(args.m, args.layers, rank, world, device)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize()
+
+    # warm-up (eager), then capture one step
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            wl.step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        wl.step()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, barrier + sync on both sides, max over ranks
+    if dist:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(device.index) as clocks:
+        ms = _time_graph(graph, args.steps, stream)
+        # keep sampling a little longer when the timed region is shorter than a sample period
+        if ms < 300:
+            _time_graph(graph, max(1, int(args.steps * 300 / max(ms, 1e-3))), stream)
+    torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = wl.weight_bytes / (ms_per_step * 1e-3) / 1e9
+
+    # ---- end to end: host x -> device, the step through the public API, outputs -> host
+    def e2e_step():
+        wl.x_dev.copy_(wl.x_host, non_blocking=True)
+        graph.replay()
+        if dist:
+            wl.full_out.copy_(wl.gathered)
+            wl.out_host.copy_(wl.out_dev, non_blocking=True)
+        else:
+            wl.out_host.copy_(wl.out_dev, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            e2e_step()
+    stream.synchronize()
+    if dist:
+        torch.distributed.barrier()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        s0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        s1.record(stream)
+    s1.synchronize()
+    e2e_ms = s0.elapsed_time(s1)
+    if dist:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = wl.weight_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
+
+    # ---- roofline of the dominant kernel: 4096x14336 decode GEMV alone, 64 matrices in rotation
+    peaks, peak_src = _peaks()
+    roof = None
+    if rank == 0:
+        big = [cl for cl in wl.calls if cl[7] in ("gate", "up")]
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=stream):
+            for (x, qs, sc, n, k, out, ws, _) in big:
+                c.iq2_xxs_matmul(x, qs, sc, n, k, out=out, workspace=ws)
+        for _ in range(3):
+            g2.replay()
+        reps = max(3, args.steps // 4)
+        ms_big = _time_graph(g2, reps, stream)
+        per_launch_ms = ms_big / (reps * len(big))
+        n_loc, k = big[0][3], big[0][4]
+        bytes_per_launch = synth.packed_bytes(n_loc, k)
+        achieved = bytes_per_launch / (per_launch_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "gemv_kernel<1> (+ its x-limb prep), 4096x14336 m=1",
+                "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peak_src,
+                "us_per_launch": round(per_launch_ms * 1e3, 3), "algorithmic_bytes": bytes_per_launch,
+                "traffic": _ncu_traffic(bytes_per_launch)}
+        del g2
+
+    del graph
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 activations x IQ2_XXS weights (s32/f32 accumulate)",
+            "data": "synthetic (seeded IQ2_XXS blocks with the benchmark distribution, N(0,1) f32 x)",
+            "config": {"workload": "config1: Llama-3-8B projections q,k,v,o,gate,up,down x 32 layers, M=1",
+                       "m": args.m, "layers": args.layers,
+                       "weight_bytes_per_step": wl.weight_bytes,
+                       "parallelism": f"column-shard over {world} GPUs + NCCL all-gather" if world > 1 else "1 GPU",
+                       "l2": "no flush needed: 1.80 GB of distinct weights per step vs 126 MB L2",
+                       "timing": "CUDA events around K replays of a CUDA graph of one step"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": wl.x_host.numel() * 4,
+                    "d2h_bytes_per_step": wl.out_host.numel() * 4,
+                    "path": "pinned host x -> device, 224 public-API calls, outputs -> pinned host"},
+            "gpu_launches": wl.launches_per_step() * args.steps,
+            "clocks": clocks.summary(),
+            "roofline": roof,
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args)
+    return line
+
+
+def _ncu_traffic(bytes_per_launch: int):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "gemv_kernel_4096x14336_m1.json"
+    try:
+        d = json.loads(p.read_text())
+        return d.get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------------------- CPU
+def cpu_baseline(args, seconds: float = 10.0, steps: int | None = None):
+    """The reference's own kernels (compiled from source for the host) on a bounded sample of
+    the workload: the 7 projections of layer 0 at M=1, repeated for ~`seconds`."""
+    from oracle.oracle import Oracle, RefKernels
+    from candelora_metal_kernels_b200 import synth
+    kind = "reference" if RefKernels.available() else "port"
+    impl = RefKernels() if kind == "reference" else Oracle()
+    threads = os.cpu_count() or 1
+    layer = []
+    total = 0
+    for pi, (name, k, n) in enumerate(synth.LLAMA3_8B_PROJECTIONS):
+        qs, sc = synth.iq2xxs_weights(n, k, pi)
+        x = synth.activations(args.m, k, seed=10_000 + pi).numpy()
+        layer.append((x, qs.numpy(), sc.numpy(), n, k))
+        total += synth.packed_bytes(n, k)
+
+    def one():
+        for (x, qs, sc, n, k) in layer:
+            if kind == "reference":
+                impl.matmul(x, qs, sc, n, k, "f32", threads=threads)
+            else:
+                impl.matmul(x, qs, sc, n, k, threads=threads)
+
+    one()  # warm
+    t0 = time.perf_counter()
+    reps = 0
+    times = []
+    while (steps is None and time.perf_counter() - t0 < seconds) or (steps is not None and reps < steps):
+        t1 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t1)
+        reps += 1
+    el = sum(times)
+    return {"value": round(total * reps / el / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"layer-0 q,k,v,o,gate,up,down at M=1 ({total} packed bytes) x {reps} passes, {el:.1f} s",
+            "ms_per_sample": round(el / reps * 1e3, 2)}
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return None
+    cb = cpu_baseline(args, steps=args.steps)
+    # warm-up passes are included in cpu_baseline's first untimed call; W extra untimed passes:
+    return {"metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_sample"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 activations x IQ2_XXS weights (f32 accumulate)", "data": "synthetic",
+            "config": {"workload": "config1: Llama-3-8B projections, M=1 (host cores; bounded sample per step)",
+                       "m": args.m},
+            "cpu_baseline": {"value": cb["value"], "unit": "GB/s", "cores": cb["cores"], "kind": cb["kind"],
+                             "sample": cb["sample"]},
+            "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# ---------------------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,285 @@
+// C ABI of the IQ2_XXS matmul (declared in include/candelora_iq2.h).
+//
+// Validation follows the reference's host dispatch iq2_matmul_metal (src/iq2_matmul.rs:197-365)
+// and iq2_dequantize_to_f16_metal (:367-505): the same conditions fail, in the same order, with
+// the same messages where the reference has one ("Metal" reads "CUDA"). Shape parsing of x
+// (rank 1 / rank 2, src/iq2_matmul.rs:170-195) belongs to the tensor-level host bindings; here
+// x is already [m, in_dim].
+#include <atomic>
+#include <cinttypes>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/candelora_iq2.h"
+#include "iq2xxs_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(const char* what, cudaError_t e) {
+    return fail(IQ2_ERR_CUDA, "%s: CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
+}
+
+// Per-device SM count, read once per device.
+std::atomic<int> g_num_sms[64];
+
+int num_sms_for_current_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+    if (dev >= 64) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }
+    int v = g_num_sms[dev].load(std::memory_order_relaxed);
+    if (v <= 0) {
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        g_num_sms[dev].store(v, std::memory_order_relaxed);
+    }
+    return v;
+}
+
+const char* variant_name(int v) {
+    switch (v) {
+        case IQ2_VARIANT_IQ2_XXS: return "Iq2Xxs";
+        case IQ2_VARIANT_IQ2_XS: return "Iq2Xs";
+        case IQ2_VARIANT_IQ2_S: return "Iq2S";
+        case IQ2_VARIANT_IQ3_S: return "Iq3S";
+        default: return "?";
+    }
+}
+
+// Where a pointer lives: -1 = not device memory, otherwise the device ordinal.
+int pointer_device(const void* p) {
+    cudaPointerAttributes a;
+    cudaError_t e = cudaPointerGetAttributes(&a, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();  // clear the sticky-free error state of this query
+        return -1;
+    }
+    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) return a.device;
+    return -1;
+}
+
+std::string where(int dev) {
+    if (dev < 0) return "Cpu";
+    char b[32];
+    snprintf(b, sizeof(b), "Cuda(%d)", dev);
+    return b;
+}
+
+// Common validation of the weight buffers (src/iq2_matmul.rs:210-259 / :380-424).
+int check_weights(const char* op, const uint8_t* weight_bytes, size_t weight_bytes_len,
+                  const uint8_t* weight_scales, size_t weight_scales_len, uint32_t out_dim,
+                  uint32_t in_dim, int variant, int dev_expected, const void* x) {
+    if (weight_bytes == nullptr || weight_scales == nullptr)
+        return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL weight pointer", op);
+    const int db = pointer_device(weight_bytes), ds = pointer_device(weight_scales);
+    const int dx = x ? pointer_device(x) : db;
+    if ((x ? dx : db) < 0) return fail(IQ2_ERR_DEVICE, "%s requires a CUDA device", op);
+    if (dx != db || dx != ds || dx != dev_expected) {
+        if (x)
+            return fail(IQ2_ERR_DEVICE, "%s device mismatch: x=%s, bytes=%s, scales=%s", op,
+                        where(dx).c_str(), where(db).c_str(), where(ds).c_str());
+        return fail(IQ2_ERR_DEVICE, "%s device mismatch: bytes=%s, scales=%s", op,
+                    where(db).c_str(), where(ds).c_str());
+    }
+    const uint64_t blocks_per_row = ((uint64_t)in_dim + 255u) / 256u;
+    const uint64_t per_block_bytes = 64, per_block_scales = 2;  // IQ2_XXS (src/iq2_matmul.rs:14-17)
+    const uint64_t nblocks = (uint64_t)out_dim * blocks_per_row;  // < 2^56, cannot overflow
+    const uint64_t expected_bytes = nblocks * per_block_bytes;
+    const uint64_t expected_scales = nblocks * per_block_scales;
+    if (expected_bytes > (uint64_t)SIZE_MAX) return fail(IQ2_ERR_OVERFLOW, "%s bytes size overflow", op);
+    if (weight_bytes_len < expected_bytes)
+        return fail(IQ2_ERR_TOO_SMALL, "%s weight_bytes too small: got %zu expected at least %" PRIu64, op,
+                    weight_bytes_len, expected_bytes);
+    if (weight_scales_len < expected_scales)
+        return fail(IQ2_ERR_TOO_SMALL, "%s weight_scales too small: got %zu expected at least %" PRIu64, op,
+                    weight_scales_len, expected_scales);
+    if (variant != IQ2_VARIANT_IQ2_XXS)
+        return fail(IQ2_ERR_UNSUPPORTED, "%s: variant %s has no CUDA kernel in this build", op,
+                    variant_name(variant));
+    return IQ2_OK;
+}
+
+// Checks that need no CUDA call, in the reference's order (zero dims first, :210-212).
+int check_args(const char* op, uint32_t out_dim, uint32_t in_dim, int variant) {
+    if (out_dim == 0 || in_dim == 0) return fail(IQ2_ERR_ZERO_DIM, "%s expects non-zero dimensions", op);
+    if (variant < IQ2_VARIANT_IQ2_XXS || variant > IQ2_VARIANT_IQ3_S)
+        return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: unknown variant %d", op, variant);
+    return IQ2_OK;
+}
+
+// The current device, or IQ2_ERR_DEVICE when there is none (the reference's "requires a Metal
+// device", :213-215).
+int current_device(const char* op, int* dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(IQ2_ERR_DEVICE, "%s requires a CUDA device (%s)", op, cudaGetErrorString(e));
+    }
+    return IQ2_OK;
+}
+
+size_t workspace_for(uint32_t m, uint32_t out_dim, uint32_t in_dim, int x_dtype, int num_sms) {
+    if (m == 0 || out_dim == 0 || in_dim == 0) return 0;
+    if (m <= 16) return iq2::gemv_workspace_size(m, out_dim, in_dim, num_sms);
+    return iq2::gemm_workspace_size(m, out_dim, in_dim, x_dtype);
+}
+
+int matmul_impl(const char* op, const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
+                size_t weight_bytes_len, const uint8_t* weight_scales, size_t weight_scales_len,
+                uint32_t out_dim, uint32_t in_dim, int variant, float* out, void* workspace,
+                size_t workspace_bytes, iq2_stream_t stream) {
+    int rc = check_args(op, out_dim, in_dim, variant);
+    if (rc != IQ2_OK) return rc;
+    int dev = 0;
+    if ((rc = current_device(op, &dev)) != IQ2_OK) return rc;
+    cudaError_t e = cudaSuccess;
+    if (m > 0 && x == nullptr) return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL x", op);
+    rc = check_weights(op, weight_bytes, weight_bytes_len, weight_scales, weight_scales_len,
+                           out_dim, in_dim, variant, dev, m > 0 ? x : nullptr);
+    if (rc != IQ2_OK) return rc;
+    if (x_dtype < IQ2_DTYPE_F32 || x_dtype > IQ2_DTYPE_BF16)
+        return fail(IQ2_ERR_DTYPE, "%s unsupported x dtype: %d", op, x_dtype);
+    if (m == 0) return IQ2_OK;  // empty [0, out_dim] output: nothing to launch (:261-268)
+    if (out == nullptr) return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL out", op);
+    if (pointer_device(out) != dev) return fail(IQ2_ERR_DEVICE, "%s: out is not memory of Cuda(%d)", op, dev);
+    const size_t esize = x_dtype == IQ2_DTYPE_F32 ? 4 : 2;
+    if (reinterpret_cast<uintptr_t>(x) % esize != 0 || reinterpret_cast<uintptr_t>(out) % 4 != 0)
+        return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: x/out not aligned to their element size", op);
+    const int sms = num_sms_for_current_device();
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (m <= 16) {
+        if (iq2::gemv_fast_path_ok(m, in_dim, weight_bytes, weight_scales)) {
+            const size_t need = iq2::gemv_workspace_size(m, out_dim, in_dim, sms);
+            if (workspace == nullptr || workspace_bytes < need)
+                return fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
+                            workspace ? workspace_bytes : (size_t)0);
+            e = iq2::launch_gemv(x, x_dtype, m, weight_bytes, weight_scales, out_dim, in_dim, out,
+                                 workspace, sms, s);
+        } else {
+            e = iq2::launch_gemv_generic(x, x_dtype, m, weight_bytes, weight_scales, out_dim, in_dim,
+                                         out, sms, s);
+        }
+    } else if (iq2::gemm_path_ok(m, out_dim, in_dim, x, x_dtype, weight_bytes, weight_scales, out)) {
+        const size_t need = iq2::gemm_workspace_size(m, out_dim, in_dim, x_dtype);
+        if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+            return fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
+                        workspace ? workspace_bytes : (size_t)0);
+        e = iq2::launch_gemm(x, x_dtype, m, weight_bytes, weight_scales, out_dim, in_dim, out,
+                             workspace, sms, s);
+    } else {
+        e = iq2::launch_gemv_generic(x, x_dtype, m, weight_bytes, weight_scales, out_dim, in_dim,
+                                     out, sms, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(op, e);
+    return IQ2_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* iq2_last_error(void) { return g_last_error.c_str(); }
+
+int iq2_abi_version(void) { return IQ2_ABI_VERSION; }
+
+size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, int x_dtype,
+                                 int variant) {
+    if (variant != IQ2_VARIANT_IQ2_XXS) return 0;
+    return workspace_for(m, out_dim, in_dim, x_dtype, num_sms_for_current_device());
+}
+
+int iq2_matmul(const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
+               size_t weight_bytes_len, const uint8_t* weight_scales, size_t weight_scales_len,
+               uint32_t out_dim, uint32_t in_dim, int variant, float* out, void* workspace,
+               size_t workspace_bytes, iq2_stream_t stream) {
+    g_last_error.clear();
+    return matmul_impl("iq2_matmul", x, x_dtype, m, weight_bytes, weight_bytes_len, weight_scales,
+                       weight_scales_len, out_dim, in_dim, variant, out, workspace, workspace_bytes,
+                       stream);
+}
+
+int iq2_matmul_with_activation_quant(const void* x, int x_dtype, uint32_t m,
+                                     const uint8_t* weight_bytes, size_t weight_bytes_len,
+                                     const uint8_t* weight_scales, size_t weight_scales_len,
+                                     uint32_t out_dim, uint32_t in_dim, int variant, int act_mode,
+                                     int strict, float* out, void* workspace,
+                                     size_t workspace_bytes, iq2_stream_t stream) {
+    g_last_error.clear();
+    switch (act_mode) {
+        case IQ2_ACT_QUANT_OFF:
+            break;
+        case IQ2_ACT_QUANT_W8A8:
+            return fail(IQ2_ERR_UNSUPPORTED, "W8A8 kernel path is not implemented in this build");
+        case IQ2_ACT_QUANT_W4A8:
+            if (strict)
+                return fail(IQ2_ERR_UNSUPPORTED,
+                            "activation quant mode W4A8 requested in strict mode, but W4A8 kernel "
+                            "path is not implemented yet");
+            break;  // non-strict W4A8 falls back to the float path (src/iq2_matmul.rs:581-589)
+        default:
+            return fail(IQ2_ERR_INVALID_ARGUMENT, "unknown activation quant mode %d", act_mode);
+    }
+    return matmul_impl("iq2_matmul", x, x_dtype, m, weight_bytes, weight_bytes_len, weight_scales,
+                       weight_scales_len, out_dim, in_dim, variant, out, workspace, workspace_bytes,
+                       stream);
+}
+
+int iq2_dequantize(const uint8_t* weight_bytes, size_t weight_bytes_len,
+                   const uint8_t* weight_scales, size_t weight_scales_len, uint32_t out_dim,
+                   uint32_t in_dim, int variant, void* out, int out_dtype, iq2_stream_t stream) {
+    g_last_error.clear();
+    const char* op = "iq2_dequantize_to_f16";
+    int rc = check_args(op, out_dim, in_dim, variant);
+    if (rc != IQ2_OK) return rc;
+    int dev = 0;
+    if ((rc = current_device(op, &dev)) != IQ2_OK) return rc;
+    cudaError_t e = cudaSuccess;
+    rc = check_weights(op, weight_bytes, weight_bytes_len, weight_scales, weight_scales_len,
+                           out_dim, in_dim, variant, dev, nullptr);
+    if (rc != IQ2_OK) return rc;
+    if (out_dtype < IQ2_DTYPE_F32 || out_dtype > IQ2_DTYPE_BF16)
+        return fail(IQ2_ERR_DTYPE, "%s unsupported out dtype: %d", op, out_dtype);
+    if (out == nullptr) return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL out", op);
+    if (pointer_device(out) != dev) return fail(IQ2_ERR_DEVICE, "%s: out is not memory of Cuda(%d)", op, dev);
+    const size_t esize = out_dtype == IQ2_DTYPE_F32 ? 4 : 2;
+    if (reinterpret_cast<uintptr_t>(out) % esize != 0)
+        return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: out not aligned to its element size", op);
+    e = iq2::launch_dequant(weight_bytes, weight_scales, out_dim, in_dim, out, out_dtype,
+                            num_sms_for_current_device(), reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(op, e);
+    return IQ2_OK;
+}
+
+int iq2_gather_columns(const float* gathered, uint32_t shards, uint32_t m, uint32_t shard_cols,
+                       float* out, iq2_stream_t stream) {
+    g_last_error.clear();
+    if (shards == 0 || m == 0 || shard_cols == 0) return IQ2_OK;
+    if (gathered == nullptr || out == nullptr)
+        return fail(IQ2_ERR_INVALID_ARGUMENT, "iq2_gather_columns: NULL pointer");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (pointer_device(gathered) != dev || pointer_device(out) != dev)
+        return fail(IQ2_ERR_DEVICE, "iq2_gather_columns: buffers are not memory of Cuda(%d)", dev);
+    cudaError_t e = iq2::launch_gather_columns(gathered, shards, m, shard_cols, out,
+                                               num_sms_for_current_device(),
+                                               reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail("iq2_gather_columns", e);
+    return IQ2_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,34 @@
+// Internal launch interface between the C ABI (iq2xxs_capi.cu) and the kernel files.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace iq2 {
+
+// Decode GEMV (iq2xxs_gemv.cu), m <= 16.
+bool gemv_fast_path_ok(uint32_t m, uint32_t k, const uint8_t* qs, const uint8_t* sc);
+size_t gemv_workspace_size(uint32_t m, uint32_t n, uint32_t k, int num_sms);
+cudaError_t launch_gemv(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
+                        uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,
+                        cudaStream_t stream);
+cudaError_t launch_gemv_generic(const void* x, int x_dtype, uint32_t m, const uint8_t* qs,
+                                const uint8_t* sc, uint32_t n, uint32_t k, float* out,
+                                int num_sms, cudaStream_t stream);
+
+// Tensor-core GEMM (iq2xxs_gemm.cu), m > 16.
+bool gemm_path_ok(uint32_t m, uint32_t n, uint32_t k, const void* x, int x_dtype, const uint8_t* qs,
+                  const uint8_t* sc, const float* out);
+size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype);
+cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
+                        uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,
+                        cudaStream_t stream);
+
+// Dequantisation and the sharding gather (iq2xxs_dequant.cu).
+cudaError_t launch_dequant(const uint8_t* qs, const uint8_t* sc, uint32_t n, uint32_t k, void* out,
+                           int out_dtype, int num_sms, cudaStream_t stream);
+cudaError_t launch_gather_columns(const float* gathered, uint32_t shards, uint32_t m,
+                                  uint32_t shard_cols, float* out, int num_sms, cudaStream_t stream);
+
+}  // namespace iq2

@@ -1,0 +1,128 @@
+/*
+ * candelora_iq2.h -- C ABI of the B200 (sm_100a) IQ2_XXS quantised matmul.
+ *
+ * This is the boundary a host binding (the Rust candle op, a ctypes/cgo stub, the C++ mirror
+ * in this repository) calls. It replaces the Metal dispatch of the reference crate
+ * candelora-metal-kernels: every entry point below names the reference function it stands in
+ * for (file:line in that crate).
+ *
+ * Conventions
+ *  - All tensors are DEVICE pointers on the caller's current CUDA device, contiguous, with the
+ *    reference's layouts:
+ *      x              [m, in_dim]   row-major, f32 / f16 / bf16 (x_dtype)
+ *      weight_bytes   u8 [out_dim * ceil(in_dim/256) * 64]   the 64-byte `qs` of every 256-weight
+ *                     block, row n's blocks contiguous (block index n*blocks_per_row + blk)
+ *      weight_scales  u8 [out_dim * ceil(in_dim/256) * 2]    little-endian fp16 `d` per block
+ *      out            f32 [m, out_dim] row-major (always f32, whatever x_dtype is)
+ *  - Every call is stream-ordered on `stream` and never synchronises the host. No entry point
+ *    allocates device memory: scratch space is the caller's `workspace` (size from the
+ *    matching *_workspace_size query). The workspace may be reused by later calls on the same
+ *    stream; concurrent calls need separate workspaces.
+ *  - Return value 0 = success; otherwise an IQ2_ERR_* code, and iq2_last_error() returns a
+ *    message for the calling thread (the reference's bail! strings where one exists).
+ *  - Thread-safe and re-entrant: there is no global mutable state apart from the per-thread
+ *    error message and a per-device cache of device attributes.
+ */
+#ifndef CANDELORA_IQ2_H
+#define CANDELORA_IQ2_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without the CUDA headers (same type: struct CUstream_st*). NULL = legacy stream. */
+typedef struct CUstream_st* iq2_stream_t;
+
+#define IQ2_ABI_VERSION 1
+
+/* Status codes. The reference bails with a message in each of these situations. */
+enum iq2_status {
+    IQ2_OK = 0,
+    IQ2_ERR_INVALID_ARGUMENT = 1, /* NULL pointer, unknown enum value                               */
+    IQ2_ERR_ZERO_DIM = 2,         /* "expects non-zero dimensions"      src/iq2_matmul.rs:210-212   */
+    IQ2_ERR_DEVICE = 3,           /* pointer not device memory of the current device  :213-225      */
+    IQ2_ERR_DTYPE = 4,            /* "unsupported x dtype"               :73-74                      */
+    IQ2_ERR_OVERFLOW = 5,         /* "size overflow" / "too large"       :238-245, :305-311          */
+    IQ2_ERR_TOO_SMALL = 6,        /* "weight_bytes too small" / "weight_scales too small" :246-259  */
+    IQ2_ERR_UNSUPPORTED = 7,      /* W4A8 in strict mode :300-302, :581-589; variant not built      */
+    IQ2_ERR_WORKSPACE = 8,        /* workspace NULL or smaller than the *_workspace_size query      */
+    IQ2_ERR_CUDA = 9              /* a CUDA runtime call failed                                     */
+};
+
+/* Activation dtypes (the reference dispatches on x.dtype(), src/iq2_matmul.rs:59-75). */
+enum iq2_dtype { IQ2_DTYPE_F32 = 0, IQ2_DTYPE_F16 = 1, IQ2_DTYPE_BF16 = 2 };
+
+/* Iq2MatmulVariant (src/iq2_matmul.rs:31-37). Only IQ2_XXS has kernels in this library; the
+ * others return IQ2_ERR_UNSUPPORTED. */
+enum iq2_variant {
+    IQ2_VARIANT_IQ2_XXS = 0,
+    IQ2_VARIANT_IQ2_XS = 1,
+    IQ2_VARIANT_IQ2_S = 2,
+    IQ2_VARIANT_IQ3_S = 3
+};
+
+/* ActivationQuantMode (src/activation_quant.rs:7-15). */
+enum iq2_act_quant_mode { IQ2_ACT_QUANT_OFF = 0, IQ2_ACT_QUANT_W8A8 = 1, IQ2_ACT_QUANT_W4A8 = 2 };
+
+/* Message for the last failed call on this thread ("" if none). Valid until the next call. */
+const char* iq2_last_error(void);
+
+/* IQ2_ABI_VERSION of the loaded library. */
+int iq2_abi_version(void);
+
+/* Bytes of device scratch iq2_matmul needs for this problem (0 is possible). */
+size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, int x_dtype,
+                                 int variant);
+
+/*
+ * out = x @ dequant(W)^T, f32 accumulate, f32 output [m, out_dim].
+ * Replaces iq2_matmul (src/iq2_matmul.rs:535-553) -> iq2_matmul_metal (:197-365) with
+ * ActivationQuantMode::Off, and through it iq2_xxs_matmul (:604-619).
+ * m == 0 is valid and launches nothing (the reference returns an empty [0, out_dim] tensor).
+ * weight_*_len are the element counts of the caller's buffers (checked like :246-259).
+ * Routing (not part of the contract): m <= 16 runs the decode GEMV (int8 tensor-core decode,
+ * f32-accurate); larger m runs the tcgen05 GEMM (bf16 operands, f32 accumulate).
+ */
+int iq2_matmul(const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
+               size_t weight_bytes_len, const uint8_t* weight_scales, size_t weight_scales_len,
+               uint32_t out_dim, uint32_t in_dim, int variant, float* out, void* workspace,
+               size_t workspace_bytes, iq2_stream_t stream);
+
+/*
+ * iq2_matmul with an activation-quant contract. Replaces iq2_matmul_with_activation_quant
+ * (src/iq2_matmul.rs:555-591): OFF -> iq2_matmul; W4A8 -> IQ2_ERR_UNSUPPORTED when strict,
+ * else iq2_matmul; W8A8 -> IQ2_ERR_UNSUPPORTED in this version (no W8A8 kernel yet).
+ */
+int iq2_matmul_with_activation_quant(const void* x, int x_dtype, uint32_t m,
+                                     const uint8_t* weight_bytes, size_t weight_bytes_len,
+                                     const uint8_t* weight_scales, size_t weight_scales_len,
+                                     uint32_t out_dim, uint32_t in_dim, int variant, int act_mode,
+                                     int strict, float* out, void* workspace,
+                                     size_t workspace_bytes, iq2_stream_t stream);
+
+/*
+ * Dense dequantisation to out [out_dim, in_dim] in out_dtype (f16 / bf16 / f32).
+ * Replaces iq2_dequantize_to_f16 (src/iq2_matmul.rs:593-602, :367-505) when out_dtype is
+ * IQ2_DTYPE_F16: bit-identical to the reference kernel iq2_xxs_dequantize_f16
+ * (src/metal_src/iq2_matmul.metal:868-887). f32 gives the exact weight value; bf16 its RNE.
+ */
+int iq2_dequantize(const uint8_t* weight_bytes, size_t weight_bytes_len,
+                   const uint8_t* weight_scales, size_t weight_scales_len, uint32_t out_dim,
+                   uint32_t in_dim, int variant, void* out, int out_dtype, iq2_stream_t stream);
+
+/*
+ * Column-sharding helper for multi-GPU runs: out [m, shards*shard_cols] <- gathered
+ * [shards, m, shard_cols] (the layout an all-gather of per-rank f32 outputs produces).
+ * No reference counterpart (the reference is single-device).
+ */
+int iq2_gather_columns(const float* gathered, uint32_t shards, uint32_t m, uint32_t shard_cols,
+                       float* out, iq2_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CANDELORA_IQ2_H */

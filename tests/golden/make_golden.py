@@ -1,0 +1,66 @@
+#!/usr/bin/env python3
+"""Writes the golden fixtures in tests/golden/ from the REFERENCE'S OWN KERNELS.
+
+The reference's kernels (src/metal_src/iq2_matmul.metal, with its tables) are compiled from
+source as C++ by oracle/Makefile into oracle/_ref/libiq2ref.so and run on host cores; this script
+calls them on:
+  ref_parity.npz   the reference test fixture of parity_case(Iq2Xxs) (src/iq2_matmul.rs:1065-1100:
+                   m=2, out_dim=7, in_dim=320, LCG bytes 0xA11CE5ED / scales 0xC0FFEE12, every d
+                   forced to 1.0, last byte 0x5A, x = deterministic_x) with x in f32, f16 and bf16,
+                   plus the f16 dequantisation;
+  baseline_small.npz  benchmark-distribution inputs (non-unit d ~U[1e-3,1e-2], N(0,1) x) that the
+                   reference tests never cover: matmul m=3 x 4096 -> 33 (f32 x), m=2 x 1000 -> 9
+                   (bf16 x, ragged K), and the f16 dequantisation of the 9 x 1000 matrix.
+Needs oracle/_ref/libiq2ref.so (make -C oracle ref). Run from the repository root.
+"""
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+
+from oracle.oracle import RefKernels, reference_parity_fixture  # noqa: E402
+from candelora_metal_kernels_b200 import synth  # noqa: E402
+
+OUT = Path(__file__).resolve().parent
+
+
+def bits16(x: torch.Tensor) -> np.ndarray:
+    return x.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def main():
+    ref = RefKernels()
+    # --- the reference's own parity fixture
+    x, wb, ws = reference_parity_fixture()
+    xt = torch.from_numpy(x)
+    out = {
+        "x_f32": x, "weight_bytes": wb, "weight_scales": ws,
+        "x_f16_bits": bits16(xt.to(torch.float16)), "x_bf16_bits": bits16(xt.to(torch.bfloat16)),
+    }
+    out["y_f32"] = ref.matmul(x, wb, ws, 7, 320, "f32")
+    out["y_f16"] = ref.matmul(out["x_f16_bits"], wb, ws, 7, 320, "f16")
+    out["y_bf16"] = ref.matmul(out["x_bf16_bits"], wb, ws, 7, 320, "bf16")
+    out["deq_f16_bits"] = ref.dequantize_f16(wb, ws, 7, 320)
+    np.savez_compressed(OUT / "ref_parity.npz", **out)
+
+    # --- benchmark-distribution cases (non-unit d)
+    b = {}
+    qs, sc = synth.iq2xxs_weights(33, 4096, seed=11)
+    xa = synth.activations(3, 4096, seed=12)
+    b["a_weight_bytes"], b["a_weight_scales"], b["a_x_f32"] = qs.numpy(), sc.numpy(), xa.numpy()
+    b["a_y"] = ref.matmul(b["a_x_f32"], b["a_weight_bytes"], b["a_weight_scales"], 33, 4096, "f32")
+    qs, sc = synth.iq2xxs_weights(9, 1000, seed=13)
+    xb = synth.activations(2, 1000, seed=14, dtype=torch.bfloat16)
+    b["b_weight_bytes"], b["b_weight_scales"], b["b_x_bf16_bits"] = qs.numpy(), sc.numpy(), bits16(xb)
+    b["b_y"] = ref.matmul(b["b_x_bf16_bits"], b["b_weight_bytes"], b["b_weight_scales"], 9, 1000, "bf16")
+    b["b_deq_f16_bits"] = ref.dequantize_f16(b["b_weight_bytes"], b["b_weight_scales"], 9, 1000)
+    np.savez_compressed(OUT / "baseline_small.npz", **b)
+    print("wrote", OUT / "ref_parity.npz", OUT / "baseline_small.npz")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,76 @@
+"""The C ABI library: it loads, exports every symbol include/candelora_iq2.h declares, and its
+argument checks that need no GPU behave like the reference's bail conditions."""
+import ctypes
+
+import pytest
+import torch
+
+from conftest import header_functions
+from candelora_metal_kernels_b200 import _lib
+from candelora_metal_kernels_b200.build import LIB, build
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _lib.load()
+
+
+def test_header_declares_the_expected_entry_points():
+    names = header_functions()
+    assert names == sorted(_lib.SIGNATURES), names
+
+
+def test_library_exports_every_header_symbol(lib):
+    raw = ctypes.CDLL(str(LIB))
+    for name in header_functions():
+        assert hasattr(raw, name), f"{name} missing from {LIB.name}"
+
+
+def test_abi_version(lib):
+    assert lib.iq2_abi_version() == 1
+
+
+def _matmul(lib, m=1, out_dim=4, in_dim=256, variant=0, x_dtype=0):
+    return lib.iq2_matmul(None, x_dtype, m, None, 0, None, 0, out_dim, in_dim, variant, None, None, 0, None)
+
+
+def test_zero_dims_rejected_first(lib):
+    assert _matmul(lib, out_dim=0) == _lib.IQ2_ERR_ZERO_DIM
+    assert b"expects non-zero dimensions" in lib.iq2_last_error()
+    assert _matmul(lib, in_dim=0) == _lib.IQ2_ERR_ZERO_DIM
+    rc = lib.iq2_dequantize(None, 0, None, 0, 0, 8, 0, None, 1, None)
+    assert rc == _lib.IQ2_ERR_ZERO_DIM
+    assert b"iq2_dequantize_to_f16 expects non-zero dimensions" in lib.iq2_last_error()
+
+
+def test_unknown_variant_rejected(lib):
+    assert _matmul(lib, variant=9) == _lib.IQ2_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")
+def test_no_device_is_a_device_error(lib):
+    assert _matmul(lib) == _lib.IQ2_ERR_DEVICE
+    assert b"requires a CUDA device" in lib.iq2_last_error()
+
+
+def test_error_message_is_per_call(lib):
+    _matmul(lib, out_dim=0)
+    assert lib.iq2_last_error() != b""
+    assert lib.iq2_gather_columns(None, 0, 0, 0, None, None) == _lib.IQ2_OK
+    assert lib.iq2_last_error() == b""
+
+
+def test_workspace_query_needs_no_device(lib):
+    assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 0) > 0
+    assert lib.iq2_matmul_workspace_size(0, 4096, 4096, 0, 0) == 0
+    assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 1) == 0  # no kernels for other variants
+
+
+def test_activation_quant_modes_without_device(lib):
+    args = (None, 0, 1, None, 0, None, 0, 4, 256, 0)
+    tail = (None, None, 0, None)
+    assert lib.iq2_matmul_with_activation_quant(*args, 1, 0, *tail) == _lib.IQ2_ERR_UNSUPPORTED
+    assert lib.iq2_matmul_with_activation_quant(*args, 2, 1, *tail) == _lib.IQ2_ERR_UNSUPPORTED
+    assert b"strict" in lib.iq2_last_error()
+    assert lib.iq2_matmul_with_activation_quant(*args, 7, 0, *tail) == _lib.IQ2_ERR_INVALID_ARGUMENT

@@ -1,0 +1,78 @@
+"""Error behaviour on a GPU box: the reference's bail conditions (src/iq2_matmul.rs:210-259,
+:300-302, :581-589) and the C ABI's workspace contract."""
+import ctypes
+
+import pytest
+import torch
+
+import candelora_metal_kernels_b200 as c
+from candelora_metal_kernels_b200 import _lib, synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(n=16, k=512, m=2):
+    qs, sc = synth.iq2xxs_weights(n, k, seed=1)
+    return synth.activations(m, k, seed=2, device="cuda"), qs.cuda(), sc.cuda()
+
+
+def test_buffers_too_small():
+    x, qs, sc = _setup()
+    with pytest.raises(c.Iq2Error, match="weight_bytes too small: got 2047 expected at least 2048") as e:
+        c.iq2_xxs_matmul(x, qs[:-1], sc, 16, 512)
+    assert e.value.code == _lib.IQ2_ERR_TOO_SMALL
+    with pytest.raises(c.Iq2Error, match="weight_scales too small: got 63 expected at least 64"):
+        c.iq2_xxs_matmul(x, qs, sc[:-1], 16, 512)
+    with pytest.raises(c.Iq2Error, match="weight_bytes too small"):
+        c.iq2_dequantize_to_f16(qs[:100], sc, 16, 512)
+
+
+def test_device_mismatch_and_host_tensors():
+    x, qs, sc = _setup()
+    with pytest.raises(c.Iq2Error, match="requires a CUDA device"):
+        c.iq2_xxs_matmul(x.cpu(), qs, sc, 16, 512)
+    with pytest.raises(c.Iq2Error, match="device mismatch"):
+        c.iq2_xxs_matmul(x, qs.cpu(), sc, 16, 512)
+
+
+def test_dtype_and_shape_errors():
+    x, qs, sc = _setup()
+    with pytest.raises(c.Iq2Error, match="expects U8 weight bytes/scales"):
+        c.iq2_xxs_matmul(x, qs.to(torch.int32), sc, 16, 512)
+    with pytest.raises(c.Iq2Error, match="unsupported x dtype"):
+        c.iq2_xxs_matmul(x.double(), qs, sc, 16, 512)
+    with pytest.raises(c.Iq2Error, match="x last dim=512 expected in_dim=256"):
+        c.iq2_xxs_matmul(x, qs, sc, 16, 256)
+    with pytest.raises(c.Iq2Error, match="rank 1 or 2"):
+        c.iq2_xxs_matmul(x[None], qs, sc, 16, 512)
+
+
+def test_other_variants_and_activation_modes():
+    x, qs, sc = _setup()
+    with pytest.raises(c.Iq2Error, match="no CUDA kernel") as e:
+        c.iq2_xs_matmul(x, torch.zeros(16 * 2 * 64, dtype=torch.uint8, device="cuda"),
+                        torch.zeros(16 * 2 * 10, dtype=torch.uint8, device="cuda"), 16, 512)
+    assert e.value.code == _lib.IQ2_ERR_UNSUPPORTED
+    strict = c.ActivationQuantConfig(c.ActivationQuantMode.W4A8, strict=True)
+    with pytest.raises(c.Iq2Error, match="strict mode"):
+        c.iq2_matmul_with_activation_quant(x, qs, sc, 16, 512, c.Iq2MatmulVariant.Iq2Xxs, strict)
+    lax = c.ActivationQuantConfig(c.ActivationQuantMode.W4A8, strict=False)
+    y = c.iq2_matmul_with_activation_quant(x, qs, sc, 16, 512, c.Iq2MatmulVariant.Iq2Xxs, lax)
+    assert torch.equal(y, c.iq2_xxs_matmul(x, qs, sc, 16, 512))
+
+
+def test_c_abi_workspace_contract():
+    x, qs, sc = _setup(n=1024, k=4096, m=1)
+    lib = _lib.load()
+    out = torch.empty((1, 1024), device="cuda")
+    need = lib.iq2_matmul_workspace_size(1, 1024, 4096, 0, 0)
+    assert need > 0
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    args = [ctypes.c_void_p(x.data_ptr()), 0, 1, ctypes.c_void_p(qs.data_ptr()), qs.numel(),
+            ctypes.c_void_p(sc.data_ptr()), sc.numel(), 1024, 4096, 0, ctypes.c_void_p(out.data_ptr())]
+    assert lib.iq2_matmul(*args, None, 0, stream) == _lib.IQ2_ERR_WORKSPACE
+    assert lib.iq2_matmul(*args, ctypes.c_void_p(ws.data_ptr()), need - 1, stream) == _lib.IQ2_ERR_WORKSPACE
+    assert lib.iq2_matmul(*args, ctypes.c_void_p(ws.data_ptr()), need, stream) == _lib.IQ2_OK
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
