@@ -138,23 +138,36 @@ class Workload:
             self.gathered = torch.empty(world * out_elems, dtype=torch.float32, device=device)
             self.full_out = torch.empty(world * out_elems, dtype=torch.float32, device=device)
 
-    def step(self):
-        from candelora_metal_kernels_b200 import iq2_xxs_matmul
-        for (x, qs, sc, n, k, out, ws, _) in self.calls:
-            iq2_xxs_matmul(x, qs, sc, n, k, out=out, workspace=ws)
+        from candelora_metal_kernels_b200 import grouped_workspace_bytes
+        self.problems = [(x, qs, sc, n, k, out) for (x, qs, sc, n, k, out, _, _) in self.calls]
+        self.grouped_ws = torch.empty(max(grouped_workspace_bytes(self.problems), 1), dtype=torch.uint8,
+                                      device=device)
+
+    def step(self, grouped: bool = False):
+        """One step: every projection through iq2_xxs_matmul (the reference-shaped call), or all of
+        them through one iq2_matmul_grouped call."""
+        from candelora_metal_kernels_b200 import iq2_matmul_grouped, iq2_xxs_matmul
+        if grouped:
+            iq2_matmul_grouped(self.problems, workspace=self.grouped_ws)
+        else:
+            for (x, qs, sc, n, k, out, ws, _) in self.calls:
+                iq2_xxs_matmul(x, qs, sc, n, k, out=out, workspace=ws)
         if self.world > 1:
             torch.distributed.all_gather_into_tensor(self.gathered, self.out_dev)
 
-    def launches_per_step(self) -> int:
-        return 2 * len(self.calls)  # x-limb prep + decode GEMV per projection
+    def launches_per_step(self, grouped: bool = False) -> int:
+        # x-limb prep + decode GEMV per call (per 256 projections when grouped)
+        return 2 * ((len(self.calls) + 255) // 256) if grouped else 2 * len(self.calls)
 
 
 def _time_graph(graph, steps: int, stream) -> float:
+    """Device time of `steps` replays, events recorded on the stream the replays run on."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(steps):
-        graph.replay()
-    end.record(stream)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
     end.synchronize()
     return start.elapsed_time(end)
 
@@ -178,8 +191,17 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         wl.step()
-    for _ in range(max(args.warmup, 3)):
-        graph.replay()
+    # the same step through one grouped call
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            wl.step(grouped=True)
+    stream.synchronize()
+    ggraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ggraph, stream=stream):
+        wl.step(grouped=True)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
     torch.cuda.synchronize()
 
     # ---- timed region: K steps, barrier + sync on both sides, max over ranks
@@ -199,6 +221,21 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         ms = float(t.item())
     ms_per_step = ms / args.steps
     value = wl.weight_bytes / (ms_per_step * 1e-3) / 1e9
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            ggraph.replay()
+    if dist:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    gms = _time_graph(ggraph, args.steps, stream)
+    if dist:
+        t = torch.tensor([gms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        gms = float(t.item())
+    grouped = {"value": round(wl.weight_bytes / (gms / args.steps * 1e-3) / 1e9, 2), "unit": "GB/s",
+               "ms_per_step": round(gms / args.steps, 4),
+               "path": "the same 224 projections in one iq2_matmul_grouped call per step",
+               "gpu_launches": wl.launches_per_step(True) * args.steps}
 
     # ---- end to end: host x -> device, the step through the public API, outputs -> host
     def e2e_step():
@@ -239,8 +276,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         with torch.cuda.graph(g2, stream=stream):
             for (x, qs, sc, n, k, out, ws, _) in big:
                 c.iq2_xxs_matmul(x, qs, sc, n, k, out=out, workspace=ws)
-        for _ in range(3):
-            g2.replay()
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g2.replay()
         reps = max(3, args.steps // 4)
         ms_big = _time_graph(g2, reps, stream)
         per_launch_ms = ms_big / (reps * len(big))
@@ -254,7 +292,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 "traffic": _ncu_traffic(bytes_per_launch)}
         del g2
 
-    del graph
+    del graph, ggraph
     line = None
     if rank == 0:
         line = {
@@ -273,6 +311,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                     "d2h_bytes_per_step": wl.out_host.numel() * 4,
                     "path": "pinned host x -> device, 224 public-API calls, outputs -> pinned host"},
             "gpu_launches": wl.launches_per_step() * args.steps,
+            "grouped": grouped,
             "clocks": clocks.summary(),
             "roofline": roof,
         }

@@ -11,7 +11,9 @@ from .iq2_matmul import (
     Iq2MatmulVariant,
     iq2_dequantize,
     iq2_dequantize_to_f16,
+    grouped_workspace_bytes,
     iq2_matmul,
+    iq2_matmul_grouped,
     iq2_matmul_with_activation_quant,
     iq2_s_matmul,
     iq2_xs_matmul,
@@ -29,7 +31,9 @@ __all__ = [
     "LIB_PATH",
     "iq2_dequantize",
     "iq2_dequantize_to_f16",
+    "grouped_workspace_bytes",
     "iq2_matmul",
+    "iq2_matmul_grouped",
     "iq2_matmul_with_activation_quant",
     "iq2_s_matmul",
     "iq2_xs_matmul",

@@ -34,9 +34,19 @@ SIGNATURES = {
     "iq2_matmul": ([_vp, _int, _u32, _vp, _sz, _vp, _sz, _u32, _u32, _int, _vp, _vp, _sz, _vp], _int),
     "iq2_matmul_with_activation_quant": (
         [_vp, _int, _u32, _vp, _sz, _vp, _sz, _u32, _u32, _int, _int, _int, _vp, _vp, _sz, _vp], _int),
+    "iq2_matmul_grouped_workspace_size": ([_vp, _u32, _u32, _int], _sz),
+    "iq2_matmul_grouped": ([_vp, _u32, _u32, _int, _vp, _sz, _vp], _int),
     "iq2_dequantize": ([_vp, _sz, _vp, _sz, _u32, _u32, _int, _vp, _int, _vp], _int),
     "iq2_gather_columns": ([_vp, _u32, _u32, _u32, _vp, _vp], _int),
 }
+
+
+class Iq2MatmulProblem(ctypes.Structure):
+    """struct iq2_matmul_problem."""
+
+    _fields_ = [("x", ctypes.c_void_p), ("weight_bytes", ctypes.c_void_p), ("weight_bytes_len", ctypes.c_size_t),
+                ("weight_scales", ctypes.c_void_p), ("weight_scales_len", ctypes.c_size_t),
+                ("out_dim", ctypes.c_uint32), ("in_dim", ctypes.c_uint32), ("out", ctypes.c_void_p)]
 
 
 class Iq2Error(RuntimeError):

@@ -9,7 +9,9 @@
 #include <cinttypes>
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <string>
+#include <vector>
 
 #include "../../include/candelora_iq2.h"
 #include "iq2xxs_internal.h"
@@ -189,6 +191,50 @@ int matmul_impl(const char* op, const void* x, int x_dtype, uint32_t m, const ui
     return IQ2_OK;
 }
 
+// Splits a grouped call into launches: fast-path problems in chunks of gemv_max_group() when
+// m <= 16; everything else one by one. With `ws` NULL only sizes the workspace.
+int grouped_impl(const iq2_matmul_problem* probs, uint32_t count, uint32_t m, int x_dtype, void* ws,
+                 size_t ws_bytes, iq2_stream_t stream, size_t* need_out) {
+    const char* op = "iq2_matmul_grouped";
+    const int sms = num_sms_for_current_device();
+    size_t need = 0;
+    std::vector<iq2::GemvProblemHost> fast;
+    std::vector<uint32_t> slow;
+    for (uint32_t i = 0; i < count; ++i) {
+        const iq2_matmul_problem& p = probs[i];
+        if (m <= 16 && iq2::gemv_fast_path_ok(m, p.in_dim, p.weight_bytes, p.weight_scales)) {
+            fast.push_back({p.x, p.weight_bytes, p.weight_scales, p.out_dim, p.in_dim, p.out});
+        } else {
+            slow.push_back(i);
+            need = std::max(need, workspace_for(m, p.out_dim, p.in_dim, x_dtype, sms));
+        }
+    }
+    const uint32_t chunk = iq2::gemv_max_group();
+    for (size_t c0 = 0; c0 < fast.size(); c0 += chunk) {
+        const uint32_t n = (uint32_t)std::min<size_t>(chunk, fast.size() - c0);
+        need = std::max(need, iq2::gemv_group_workspace_size(fast.data() + c0, n, m, sms));
+    }
+    if (need_out) *need_out = need;
+    if (ws == nullptr && need_out) return IQ2_OK;
+    if (need > 0 && (ws == nullptr || ws_bytes < need))
+        return fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
+                    ws ? ws_bytes : (size_t)0);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    for (size_t c0 = 0; c0 < fast.size(); c0 += chunk) {
+        const uint32_t n = (uint32_t)std::min<size_t>(chunk, fast.size() - c0);
+        cudaError_t e = iq2::launch_gemv_group(fast.data() + c0, n, m, x_dtype, ws, sms, s);
+        if (e != cudaSuccess) return cuda_fail(op, e);
+    }
+    for (uint32_t i : slow) {
+        const iq2_matmul_problem& p = probs[i];
+        int rc = matmul_impl(op, p.x, x_dtype, m, p.weight_bytes, p.weight_bytes_len, p.weight_scales,
+                             p.weight_scales_len, p.out_dim, p.in_dim, IQ2_VARIANT_IQ2_XXS, p.out, ws,
+                             ws_bytes, stream);
+        if (rc != IQ2_OK) return rc;
+    }
+    return IQ2_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -237,6 +283,44 @@ int iq2_matmul_with_activation_quant(const void* x, int x_dtype, uint32_t m,
     return matmul_impl("iq2_matmul", x, x_dtype, m, weight_bytes, weight_bytes_len, weight_scales,
                        weight_scales_len, out_dim, in_dim, variant, out, workspace, workspace_bytes,
                        stream);
+}
+
+size_t iq2_matmul_grouped_workspace_size(const iq2_matmul_problem* problems, uint32_t count,
+                                         uint32_t m, int x_dtype) {
+    if (problems == nullptr || count == 0 || m == 0) return 0;
+    size_t need = 0;
+    grouped_impl(problems, count, m, x_dtype, nullptr, 0, nullptr, &need);
+    return need;
+}
+
+int iq2_matmul_grouped(const iq2_matmul_problem* problems, uint32_t count, uint32_t m, int x_dtype,
+                       void* workspace, size_t workspace_bytes, iq2_stream_t stream) {
+    g_last_error.clear();
+    const char* op = "iq2_matmul_grouped";
+    if (count == 0) return IQ2_OK;
+    if (problems == nullptr) return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL problems", op);
+    if (x_dtype < IQ2_DTYPE_F32 || x_dtype > IQ2_DTYPE_BF16)
+        return fail(IQ2_ERR_DTYPE, "%s unsupported x dtype: %d", op, x_dtype);
+    int dev = 0;
+    int rc = current_device(op, &dev);
+    if (rc != IQ2_OK) return rc;
+    // every problem is validated like a single iq2_matmul call before anything is launched
+    for (uint32_t i = 0; i < count; ++i) {
+        const iq2_matmul_problem& p = problems[i];
+        if ((rc = check_args(op, p.out_dim, p.in_dim, IQ2_VARIANT_IQ2_XXS)) != IQ2_OK) return rc;
+        if (m > 0 && p.x == nullptr) return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: problem %u: NULL x", op, i);
+        rc = check_weights(op, p.weight_bytes, p.weight_bytes_len, p.weight_scales, p.weight_scales_len,
+                           p.out_dim, p.in_dim, IQ2_VARIANT_IQ2_XXS, dev, m > 0 ? p.x : nullptr);
+        if (rc != IQ2_OK) return rc;
+        if (m == 0) continue;
+        if (p.out == nullptr || pointer_device(p.out) != dev)
+            return fail(IQ2_ERR_DEVICE, "%s: problem %u: out is not memory of Cuda(%d)", op, i, dev);
+        const size_t esize = x_dtype == IQ2_DTYPE_F32 ? 4 : 2;
+        if (reinterpret_cast<uintptr_t>(p.x) % esize != 0 || reinterpret_cast<uintptr_t>(p.out) % 4 != 0)
+            return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: problem %u: x/out not aligned to their element size", op, i);
+    }
+    if (m == 0) return IQ2_OK;
+    return grouped_impl(problems, count, m, x_dtype, workspace, workspace_bytes, stream, nullptr);
 }
 
 int iq2_dequantize(const uint8_t* weight_bytes, size_t weight_bytes_len,

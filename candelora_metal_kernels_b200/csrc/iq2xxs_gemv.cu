@@ -1,4 +1,4 @@
-// IQ2_XXS decode GEMV for small m (m <= 16) on sm_100a.
+// IQ2_XXS decode GEMV for small m (m <= 16) on sm_100a, single or grouped projections.
 //
 // Computes out[m, n] = sum_k x[m, k] * W[n, k] with W the IQ2_XXS weights in the reference's
 // split layout (reference: iq2_xxs_matmul_kernel, src/metal_src/iq2_matmul.metal:188-240;
@@ -8,26 +8,32 @@
 //   aux_g = bytes 0..3 (four 8-bit grid indices), aux_s = bytes 4..7 (four 7-bit sign indices
 //   at bits 7g..7g+6, 4-bit scale s at bits 28..31), d = fp16 block scale.
 //
-// B200 design. Every weight is used once at m = 1, so the cost that matters is the work per
-// weight on the way from HBM to an accumulator. The weights never become floats:
-//   * d*(0.5+s)*0.25 = d * (2s+1) / 8, and every signed grid value is an int8 in
-//     {+-8, +-25, +-43}. One `prmt` turns a 16-bit selector (grid code | sign, from two
-//     lane-replicated shared-memory tables) into four signed int8 weights.
+// B200 design. At m = 1 every weight is used once, so what matters is the work per weight
+// between HBM and an accumulator; the weights never become floats:
+//   * d*(0.5+s)*0.25 = d*(2s+1)/8 and every signed grid value is an int8 in {+-8,+-25,+-43}. One
+//     `prmt` turns a 16-bit selector (grid code | sign, from two lane-replicated shared-memory
+//     tables, so a warp's random lookups never share a bank) into four signed int8 weights.
 //   * x is split per (token, 256-block) into four 7-bit signed limbs of a 28-bit fixed-point
-//     value (gemv_prep_kernel), so x @ W^T becomes integer tensor-core work:
-//     mma.m16n8k32 s8 x s8 -> s32 per 32-weight sub-block, scaled by the odd integer (2s+1)
-//     in s32 (exact: |sum| < 2^31), and turned into f32 once per 256-block with d and the
-//     limb/token scale. The only rounding is the 2^-28-relative quantisation of x and f32
-//     rounding of the per-block partial sums, far inside the 1e-4 relative L2 bound.
-//   * The weight stream is staged with cp.async into a per-warp shared-memory ring (no
-//     register staging, several KB in flight per warp); 16-byte chunks are XOR-swizzled so the
-//     8 rows a warp reads per step hit 8 different banks.
-//   * Work units are (32 or 16 rows) x (a few 256-blocks of K): split-K keeps every SM busy
-//     for k/v-sized projections. Split-K partials are summed in a fixed order by the last
-//     warp to finish a row group (an atomic ticket per group), so results are deterministic.
+//     value (gemv_prep_kernel): x @ W^T becomes mma.m16n8k32 s8 x s8 -> s32 per 32-weight
+//     sub-block, scaled by the odd integer 2s+1 in s32 (exact, |sum| < 2^31) and turned into f32
+//     once per 256-block with d and the limb scale. The only rounding is the 2^-28-relative
+//     quantisation of x and f32 rounding of per-block partial sums (rel. error ~1e-6).
+//   * Weights stream through a per-warp cp.async ring in shared memory (one 256-weight block of
+//     ROWS rows per stage, ~140 KB in flight per SM), 16-byte chunks XOR-swizzled so the rows a
+//     warp reads together sit in different banks; one 16-byte read feeds two sub-blocks.
+//   * Stream-K: the (projection, row group, sub-block) steps of a launch are split into equal
+//     contiguous ranges, one per warp, so every warp finishes at the same time whatever the
+//     shapes. A row group cut by a range boundary is finished by the last of its (at most a few)
+//     warps, which sums the others' partials in warp order: results are deterministic.
+//   * Grouped launches: one prep launch and one GEMV launch serve up to 256 projections (e.g.
+//     q/k/v or gate/up sharing x), amortising launch and table-fill costs; projections that share
+//     an x share its limbs. Both kernels use programmatic dependent launch: the GEMV fills its
+//     tables and starts streaming weights while the prep runs.
 #include "iq2xxs_common.cuh"
 #include "iq2xxs_codebook.h"
 #include "iq2xxs_internal.h"
+
+#include <vector>
 
 namespace iq2 {
 
@@ -35,49 +41,64 @@ namespace {
 
 constexpr int GEMV_WARPS = 16;
 constexpr int LUT_BYTES = 256 * 256;  // 256 rows x (32 lanes grid selectors | 32 lanes sign)
+constexpr int MAX_PROBLEMS = 256;     // per launch
 
 template <int NT>
 struct GemvShape {
-    static constexpr int T = NT <= 2 ? 2 : 1;           // 16-row mma tiles per warp
-    static constexpr int ROWS = 16 * T;                 // rows per work unit
-    static constexpr int STAGE_QS = ROWS * 128;         // 2 blocks of qs per row
-    static constexpr int STAGE_BYTES = STAGE_QS + ROWS * 4;  // + 2 fp16 scales per row
-    static constexpr int NSTAGES = T == 2 ? 2 : 4;
+    static constexpr int T = NT <= 2 ? 2 : 1;          // 16-row mma tiles per warp
+    static constexpr int ROWS = 16 * T;                // rows of a row group
+    static constexpr int STAGE_QS = ROWS * 64;         // one block of qs per row
+    static constexpr int STAGE_BYTES = STAGE_QS + ROWS * 4;  // + the aligned scale word per row
+    static constexpr int NSTAGES = T == 2 ? 4 : 8;
     static constexpr int SMEM = LUT_BYTES + GEMV_WARPS * NSTAGES * STAGE_BYTES;
 };
 
+int nt_for(uint32_t m) { return m <= 2 ? 1 : (m <= 4 ? 2 : (m <= 8 ? 4 : 8)); }
+int rows_for(uint32_t m) { return nt_for(m) <= 2 ? 32 : 16; }
+
 // ---------------------------------------------------------------------------------------------
-// x -> int8 limb fragments. One warp per (token m, block b); lane = (sub-block sbi, group t)
-// owns the 8 activations k = b*256 + sbi*32 + t*8 + [0, 8).
+// x -> int8 limb fragments. One warp per (x item, token m, block b); lane = (sub-block sbi,
+// group t) owns the 8 activations k = b*256 + sbi*32 + t*8 + [0, 8).
 // With amax = max |x| over the block and amax = f * 2^E (f in [0.5, 1)):
 //   q = rint(x * 2^(27-E)) (|q| <= 2^27), |q| = L3*2^21 + L2*2^14 + L1*2^7 + L0 (7-bit limbs),
 //   each limb carrying the sign of q; column scale of limb l = 2^(E - 27 + 7l) / 8 (the /8 is
 //   the weight scale's (2s+1)/8). Non-finite blocks get NaN scales, so the output is NaN.
-// Output fragment layout (mma B operand, m16n8k32 "col"): for sub-block sb and n8 tile nt,
-//   xb[((sb*NT + nt)*32 + col*4 + t)*8 + i] = limb of activation group t, element i, where
-//   col = (m % 2)*4 + l and nt = m / 2.
+// Fragment layout (mma B operand, m16n8k32 "col"), sub-block sb, n8 tile nt:
+//   xb[((sb*NT + nt)*32 + col*4 + t)*8 + i] = limb of group t, element i; col = (m%2)*4 + l.
+struct PrepItem {
+    const void* x;
+    uint8_t* xb;
+    float* colscale;
+    uint32_t K, nb, warp_begin, pad;
+};
+
+struct PrepLaunch {
+    PrepItem item[MAX_PROBLEMS];
+    uint32_t count, M;
+    uint32_t* counters;
+    uint32_t ncounters;
+};
+
 template <typename XT, int NT>
-__global__ void __launch_bounds__(256) gemv_prep_kernel(const XT* __restrict__ x, uint32_t M,
-                                                        uint32_t K, uint32_t nb,
-                                                        uint8_t* __restrict__ xb,
-                                                        float* __restrict__ colscale,
-                                                        uint32_t* __restrict__ counters,
-                                                        uint32_t ncounters) {
+__global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ PrepLaunch L) {
     // x may be written by the previous kernel and the workspace may still be read by the
     // previous GEMV: wait for both before touching memory. Only then let the GEMV launch, so
     // its early weight prefetch also runs after every earlier kernel has finished.
     pdl_wait();
     pdl_launch_dependents();
-    if (blockIdx.x == 0) {
-        for (uint32_t i = threadIdx.x; i < ncounters; i += blockDim.x) counters[i] = 0u;
-    }
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < L.ncounters; i += gridDim.x * blockDim.x)
+        L.counters[i] = 0u;
     const uint32_t wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    if (wid >= M * nb) return;
-    const uint32_t m = wid / nb, b = wid % nb;
+    uint32_t it = 0;
+    while (it + 1 < L.count && L.item[it + 1].warp_begin <= wid) ++it;
+    const PrepItem& P = L.item[it];
+    const uint32_t local = wid - P.warp_begin;
+    if (local >= L.M * P.nb) return;
+    const uint32_t m = local / P.nb, b = local % P.nb;
     const int sbi = lane >> 2, t = lane & 3;
     const size_t k0 = (size_t)b * QK + sbi * 32 + t * 8;
-    const XT* xr = x + (size_t)m * K;
+    const XT* xr = static_cast<const XT*>(P.x) + (size_t)m * P.K;
 
     float v[8];
     float amax = 0.0f;
@@ -85,14 +106,12 @@ __global__ void __launch_bounds__(256) gemv_prep_kernel(const XT* __restrict__ x
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const size_t k = k0 + i;
-        v[i] = k < K ? to_f32(xr[k]) : 0.0f;
+        v[i] = k < P.K ? to_f32(xr[k]) : 0.0f;
         bad |= !isfinite(v[i]);
         amax = fmaxf(amax, fabsf(v[i]));
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-    }
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
     bad = __any_sync(0xFFFFFFFFu, bad);
 
     int E = 0;
@@ -101,8 +120,7 @@ __global__ void __launch_bounds__(256) gemv_prep_kernel(const XT* __restrict__ x
     if (!bad && amax > 0.0f) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const float qf = rintf(ldexpf(v[i], 27 - E));
-            const int q = (int)qf;
+            const int q = (int)rintf(ldexpf(v[i], 27 - E));
             const uint32_t mag = (uint32_t)(q < 0 ? -q : q);
 #pragma unroll
             for (int l = 0; l < 4; ++l) {
@@ -117,7 +135,7 @@ __global__ void __launch_bounds__(256) gemv_prep_kernel(const XT* __restrict__ x
     const size_t sb = (size_t)b * 8 + sbi;
 #pragma unroll
     for (int l = 0; l < 4; ++l) {
-        uint2* dst = reinterpret_cast<uint2*>(xb + ((sb * NT + nt) * 32 + (colbase + l) * 4 + t) * 8);
+        uint2* dst = reinterpret_cast<uint2*>(P.xb + ((sb * NT + nt) * 32 + (colbase + l) * 4 + t) * 8);
         *dst = make_uint2(lo[l], hi[l]);
     }
     if (lane < 4) {
@@ -125,39 +143,80 @@ __global__ void __launch_bounds__(256) gemv_prep_kernel(const XT* __restrict__ x
         if (bad) s = __int_as_float(0x7FC00000);
         else if (amax == 0.0f) s = 0.0f;
         else s = ldexpf(1.0f, E - 30 + 7 * lane);
-        colscale[(size_t)b * (NT * 8) + nt * 8 + colbase + lane] = s;
+        P.colscale[(size_t)b * (NT * 8) + nt * 8 + colbase + lane] = s;
     }
 }
 
 // ---------------------------------------------------------------------------------------------
-struct GemvParams {
+struct GemvProblem {  // 64 bytes
     const uint8_t* qs;
     const uint8_t* sc;
     const uint8_t* xb;
     const float* colscale;
     float* out;
-    float* partial;
-    uint32_t* counters;
-    size_t row_bytes;  // nb * 64
-    uint32_t M, N, nb;
-    uint32_t S, kb;    // K splits per row group, blocks per split
-    uint32_t total_units;
+    uint32_t N, nb, row_groups, tb_begin;  // tb_begin: first tile-block (ROWS rows x 1 block)
+    uint32_t counter_base, pad;
 };
 
-// Four signed int8 weights of one 8-weight group (row's sub-block word q), for this lane's
-// group t: lo = weights 0..3, hi = weights 4..7.
-__device__ __forceinline__ void decode_group(const uint8_t* lut, uint2 q, uint32_t selg,
-                                             uint32_t laneoff, uint32_t rot, uint32_t soff,
-                                             uint32_t& lo, uint32_t& hi) {
-    const uint32_t ga = prmt(q.x, laneoff, selg);               // grid_idx*256 + lane*4
-    const uint32_t sa = (__funnelshift_r(q.y, q.y, rot) & 0x7F00u) | soff;  // sign_idx*256+128+lane*4
+struct GemvLaunch {
+    GemvProblem prob[MAX_PROBLEMS];
+    uint32_t count, M;
+    uint32_t total_steps;  // 8 sub-block steps per tile-block
+    uint32_t pad;
+    float* partial;        // [warps][2][ROWS * M]
+    uint32_t* counters;
+};
+
+// Stream-K partition of [0, total) over W warps: the first r warps get q+1 steps, the rest q.
+struct Partition {
+    uint32_t q, r;
+    __device__ __forceinline__ uint32_t begin(uint32_t w) const { return w * q + min(w, r); }
+    __device__ __forceinline__ uint32_t owner(uint32_t s) const {
+        const uint32_t big = r * (q + 1);
+        return s < big ? s / (q + 1) : r + (s - big) / q;
+    }
+};
+
+// Four signed int8 weights of one 8-weight group (sub-block word {aux_g, aux_s}) for this
+// lane's group t: lo = weights 0..3, hi = weights 4..7.
+__device__ __forceinline__ void decode_group(const uint8_t* lut, uint32_t aux_g, uint32_t aux_s,
+                                             uint32_t selg, uint32_t laneoff, uint32_t rot,
+                                             uint32_t soff, uint32_t& lo, uint32_t& hi) {
+    const uint32_t ga = prmt(aux_g, laneoff, selg);                             // idx*256 + lane*4
+    const uint32_t sa = (__funnelshift_r(aux_s, aux_s, rot) & 0x7F00u) | soff;  // sidx*256+128+lane*4
     const uint32_t sel = lds32(lut, ga) | lds32(lut, sa);
     lo = prmt(KPOS, KNEG, sel);
     hi = prmt(KPOS, KNEG, sel >> 16);
 }
 
+// Cursor over the tile-blocks (problem p, row group rg, block blk) of a launch, in order.
+struct TbCursor {
+    uint32_t tb, p, rg, blk;
+};
+
+__device__ __forceinline__ void cursor_seek(const GemvLaunch& L, uint32_t tb, TbCursor& c) {
+    uint32_t p = 0;
+    while (p + 1 < L.count && L.prob[p + 1].tb_begin <= tb) ++p;
+    const uint32_t local = tb - L.prob[p].tb_begin;
+    c.tb = tb;
+    c.p = p;
+    c.rg = local / L.prob[p].nb;
+    c.blk = local % L.prob[p].nb;
+}
+
+__device__ __forceinline__ void cursor_next(const GemvLaunch& L, TbCursor& c) {
+    ++c.tb;
+    if (++c.blk == L.prob[c.p].nb) {
+        c.blk = 0;
+        if (++c.rg == L.prob[c.p].row_groups) {
+            c.rg = 0;
+            ++c.p;
+        }
+    }
+}
+
 template <int NT>
-__global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvLaunch L) {
     using S_ = GemvShape<NT>;
     constexpr int T = S_::T, ROWS = S_::ROWS, STAGE_QS = S_::STAGE_QS;
     constexpr int STAGE_BYTES = S_::STAGE_BYTES, NSTAGES = S_::NSTAGES;
@@ -167,121 +226,147 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const GemvPara
     const int g = lane >> 2, t = lane & 3;
     uint8_t* ring = smem + LUT_BYTES + warp * (NSTAGES * STAGE_BYTES);
 
-    // Lane-replicated selector tables: row e holds IQ2XXS_GRID_SEL[e] in bytes [0,128) (one
-    // copy per lane) and IQ2XXS_SIGN_SEL[e] in [128,256) for e < 128. A lane only ever reads
-    // its own copy, so the random table lookups of a warp never conflict on a bank.
-    {
-        uint32_t* lw = reinterpret_cast<uint32_t*>(smem);
-        for (int i = threadIdx.x; i < 256 * 64; i += blockDim.x) {
-            const int e = i >> 6, w = i & 63;
-            lw[i] = (w < 32) ? IQ2XXS_GRID_SEL[e] : (e < 128 ? IQ2XXS_SIGN_SEL[e] : 0u);
-        }
-    }
-    __syncthreads();
-
+    // This warp's step range [a, b) and the tile-blocks it touches [tb0, tb1).
     const uint32_t W = gridDim.x * GEMV_WARPS;
-    const uint32_t gw = blockIdx.x * GEMV_WARPS + warp;
-    const uint32_t laneoff = (uint32_t)lane * 4u;
-    const uint32_t selg = 0x5504u | ((uint32_t)t << 4);
-    const uint32_t rot = (7u * t + 24u) & 31u;
-    const uint32_t soff = 128u + laneoff;
+    const uint32_t w = blockIdx.x * GEMV_WARPS + warp;
+    const Partition part{L.total_steps / W, L.total_steps % W};
+    const uint32_t a = part.begin(w), b = part.begin(w + 1);
+    const uint32_t tb0 = a >> 3, tb1 = (b + 7) >> 3;
 
-    // ---- producer side: issue cursor over (unit, stage) ----
-    uint32_t iu = gw, ist = 0;
+    // ---- issue side: cp.async stages of one tile-block each, NSTAGES ahead ----
+    TbCursor ic;
+    if (a < b) cursor_seek(L, tb0, ic);
     int islot = 0;
     auto issue = [&]() {
-        if (iu < p.total_units) {
-            const uint32_t rg = iu / p.S, s = iu % p.S;
-            const uint32_t blk = s * p.kb + 2u * ist;
-            const uint32_t row0 = rg * ROWS;
+        if (a < b && ic.tb < tb1) {
+            const GemvProblem& P = L.prob[ic.p];
             uint8_t* st = ring + islot * STAGE_BYTES;
+            const uint32_t s_lo = ic.tb * 8 < a ? a - ic.tb * 8 : 0u;        // first sub-block needed
+            const uint32_t s_hi = min(8u, b - ic.tb * 8);                     // one past the last
+            const uint32_t ch_lo = s_lo >> 1, ch_hi = (s_hi + 1) >> 1;        // 16-byte chunks needed
+            const uint32_t row0 = ic.rg * ROWS;
+            const size_t row_bytes = (size_t)P.nb * QS_BYTES;
 #pragma unroll
-            for (int c = 0; c < ROWS * 8 / 32; ++c) {
+            for (int c = 0; c < ROWS * 4 / 32; ++c) {
                 const int idx = c * 32 + lane;
-                const int r = idx >> 3, ch = idx & 7;
+                const int r = idx >> 2, ch = idx & 3;
                 const uint32_t row = row0 + r;
-                const bool ok = row < p.N;
-                const uint8_t* src = p.qs + (ok ? (size_t)row * p.row_bytes + (size_t)blk * QS_BYTES + ch * 16 : 0);
-                cp_async_16(smem_u32(st + r * 128 + ((ch ^ (r & 7)) << 4)), src, ok ? 16u : 0u);
+                const bool ok = row < P.N && (uint32_t)ch >= ch_lo && (uint32_t)ch < ch_hi;
+                const uint8_t* src = P.qs + (ok ? (size_t)row * row_bytes + (size_t)ic.blk * QS_BYTES + ch * 16 : 0);
+                // swizzle: chunk ch of row r goes to chunk ch ^ ((r >> 1) & 3); bank group r & 1
+                cp_async_16(smem_u32(st + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4)), src, ok ? 16u : 0u);
             }
             if (lane < ROWS) {
                 const uint32_t row = row0 + lane;
-                const bool ok = row < p.N;
-                const uint8_t* src = p.sc + (ok ? ((size_t)row * p.nb + blk) * SC_BYTES : 0);
-                cp_async_4(smem_u32(st + STAGE_QS + lane * 4), src, ok ? 4u : 0u);
+                const bool ok = row < P.N;
+                // the 4-byte aligned word holding this row's d; near the end of the buffer only
+                // the bytes that exist are read (the rest of the word is zero-filled)
+                const size_t e = ((size_t)row * P.nb + ic.blk) * SC_BYTES;
+                const size_t ea = e & ~(size_t)3, total = (size_t)P.N * P.nb * SC_BYTES;
+                const uint32_t nbytes = ok ? (uint32_t)min((size_t)4, total - ea) : 0u;
+                cp_async_4(smem_u32(st + STAGE_QS + lane * 4), P.sc + (ok ? ea : 0), nbytes);
             }
-            const uint32_t nblk = min(p.kb, p.nb - s * p.kb);
-            if ((++ist) * 2u >= nblk) {
-                ist = 0;
-                iu += W;
-            }
+            cursor_next(L, ic);
         }
         cp_async_commit();
         islot = (islot + 1 == NSTAGES) ? 0 : islot + 1;
     };
 
+    // Issue the first stages before anything else: they only read weights.
 #pragma unroll
     for (int i = 0; i < NSTAGES; ++i) issue();
 
-    // Everything above (table fill, first weight stages) reads only constants and weights; the
-    // x fragments, scales table, counters and outputs come from / are shared with the prep
-    // kernel, so wait for it here.
+    // Lane-replicated selector tables: row e holds IQ2XXS_GRID_SEL[e] in bytes [0,128) (one
+    // copy per lane) and IQ2XXS_SIGN_SEL[e] in [128,256) for e < 128. A lane only ever reads
+    // its own copy, so the random table lookups of a warp never conflict on a bank.
+    {
+        uint4* lw = reinterpret_cast<uint4*>(smem);
+        for (int i = threadIdx.x; i < 256 * 16; i += blockDim.x) {
+            const int e = i >> 4, q4 = i & 15;
+            const uint32_t v = (q4 < 8) ? IQ2XXS_GRID_SEL[e] : (e < 128 ? IQ2XXS_SIGN_SEL[e] : 0u);
+            lw[i] = make_uint4(v, v, v, v);
+        }
+    }
+    __syncthreads();
+    // x fragments, column scales, counters and outputs are produced by / shared with the prep
+    // kernel: wait for it here.
     pdl_wait();
+    if (a >= b) {
+        cp_async_wait<0>();
+        pdl_launch_dependents();
+        return;
+    }
+
+    const uint32_t laneoff = (uint32_t)lane * 4u;
+    const uint32_t selg = 0x5504u | ((uint32_t)t << 4);
+    const uint32_t rot = (7u * t + 24u) & 31u;
+    const uint32_t soff = 128u + laneoff;
+    const uint32_t swz = (uint32_t)((g >> 1) & 3);   // rows g, g+8, g+16, g+24 share it
+    const uint32_t rowbase = (uint32_t)(g & 1) * 64u + (uint32_t)(g >> 1) * 128u;  // byte offset of row g
+    // rows tt*16+g and tt*16+g+8 are rowbase + tt*1024 and rowbase + tt*1024 + 512
 
     bool bact[NT];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) bact[nt] = (uint32_t)(nt * 2 + (g >> 2)) < p.M;
+    for (int nt = 0; nt < NT; ++nt) bact[nt] = (uint32_t)(nt * 2 + (g >> 2)) < L.M;
 
     float F[T][NT][4];
 #pragma unroll
-    for (int a = 0; a < T; ++a)
+    for (int i = 0; i < T; ++i)
 #pragma unroll
-        for (int b = 0; b < NT; ++b)
+        for (int j = 0; j < NT; ++j)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) F[a][b][c] = 0.0f;
+            for (int k = 0; k < 4; ++k) F[i][j][k] = 0.0f;
 
-    uint32_t cu = gw, cst = 0;
+    TbCursor cc;
+    cursor_seek(L, tb0, cc);
     int slot = 0;
-    while (cu < p.total_units) {
+    for (; cc.tb < tb1;) {
+        const GemvProblem& P = L.prob[cc.p];
         cp_async_wait<NSTAGES - 1>();
         __syncwarp();
         const uint8_t* st = ring + slot * STAGE_BYTES;
-        const uint32_t rg = cu / p.S, s = cu % p.S;
-        const uint32_t nblk_u = min(p.kb, p.nb - s * p.kb);
-        const uint32_t blk0 = s * p.kb + 2u * cst;
+        const uint32_t s_lo = cc.tb * 8 < a ? a - cc.tb * 8 : 0u;
+        const uint32_t s_hi = min(8u, b - cc.tb * 8);
 
-#pragma unroll 1
-        for (int bi = 0; bi < 2; ++bi) {
-            const uint32_t gblk = blk0 + bi;
-            int I[T][NT][4];
+        int I[T][NT][4];
 #pragma unroll
-            for (int a = 0; a < T; ++a)
+        for (int i = 0; i < T; ++i)
 #pragma unroll
-                for (int b = 0; b < NT; ++b)
+            for (int j = 0; j < NT; ++j)
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) I[a][b][c] = 0;
+                for (int k = 0; k < 4; ++k) I[i][j][k] = 0;
 
+        const uint8_t* xbp = P.xb + (size_t)cc.blk * 8 * NT * 256 + lane * 8;
 #pragma unroll
-            for (int sbi = 0; sbi < 8; ++sbi) {
-                const int sb = bi * 8 + sbi;
+        for (int pair = 0; pair < 4; ++pair) {
+            // one 16-byte chunk = sub-blocks 2*pair and 2*pair+1 of every row
+            const uint32_t coff = ((uint32_t)pair ^ swz) << 4;
+            uint4 qw[T][2];
+#pragma unroll
+            for (int tt = 0; tt < T; ++tt) {
+                qw[tt][0] = *reinterpret_cast<const uint4*>(st + rowbase + tt * 1024 + coff);
+                qw[tt][1] = *reinterpret_cast<const uint4*>(st + rowbase + tt * 1024 + 512 + coff);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t sb = pair * 2 + h;
+                const bool in = sb >= s_lo && sb < s_hi;  // sub-blocks outside the range add 0
                 uint32_t bf[NT][2];
-                const uint8_t* bsrc = p.xb + ((size_t)(gblk * 8 + sbi) * NT) * 256 + lane * 8;
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     uint2 v = make_uint2(0u, 0u);
-                    if (bact[nt]) v = __ldg(reinterpret_cast<const uint2*>(bsrc + nt * 256));
+                    if (bact[nt] && in) v = __ldg(reinterpret_cast<const uint2*>(xbp + (sb * NT + nt) * 256));
                     bf[nt][0] = v.x;
                     bf[nt][1] = v.y;
                 }
-                const uint32_t off = ((((uint32_t)sb >> 1) ^ (uint32_t)g) << 4) | (((uint32_t)sb & 1u) << 3);
 #pragma unroll
                 for (int tt = 0; tt < T; ++tt) {
-                    const uint2 q0 = lds64(st, (tt * 16 + g) * 128 + off);
-                    const uint2 q1 = lds64(st, (tt * 16 + g + 8) * 128 + off);
+                    const uint32_t g0 = h ? qw[tt][0].z : qw[tt][0].x, s0 = h ? qw[tt][0].w : qw[tt][0].y;
+                    const uint32_t g1 = h ? qw[tt][1].z : qw[tt][1].x, s1 = h ? qw[tt][1].w : qw[tt][1].y;
                     uint32_t a0, a1, a2, a3;
-                    decode_group(lut, q0, selg, laneoff, rot, soff, a0, a2);
-                    decode_group(lut, q1, selg, laneoff, rot, soff, a1, a3);
-                    const int c0 = (int)((q0.y >> 27) | 1u), c1 = (int)((q1.y >> 27) | 1u);
+                    decode_group(lut, g0, s0, selg, laneoff, rot, soff, a0, a2);
+                    decode_group(lut, g1, s1, selg, laneoff, rot, soff, a1, a3);
+                    const int c0 = (int)((s0 >> 27) | 1u), c1 = (int)((s1 >> 27) | 1u);
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
                         int d[4];
@@ -293,15 +378,22 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const GemvPara
                     }
                 }
             }
-            // Block epilogue: s32 -> f32 with d (per row) and the limb/token scale (per column).
+        }
+        // Block epilogue: s32 -> f32 with d (per row) and the limb scale (per column).
+        {
             float2 cs[NT];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
-                cs[nt] = __ldg(reinterpret_cast<const float2*>(p.colscale + (size_t)gblk * (NT * 8) + nt * 8 + 2 * t));
+                cs[nt] = __ldg(reinterpret_cast<const float2*>(P.colscale + (size_t)cc.blk * (NT * 8) + nt * 8 + 2 * t));
+            const uint32_t row0 = cc.rg * ROWS;
 #pragma unroll
             for (int tt = 0; tt < T; ++tt) {
-                const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(st + STAGE_QS + (tt * 16 + g) * 4 + bi * 2));
-                const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(st + STAGE_QS + (tt * 16 + g + 8) * 4 + bi * 2));
+                const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
+                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(st + STAGE_QS + r0 * 4);
+                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(st + STAGE_QS + r1 * 4);
+                const uint32_t o0 = ((row0 + r0) * P.nb + cc.blk) & 1u, o1 = ((row0 + r1) * P.nb + cc.blk) & 1u;
+                const float d0 = half_bits_to_float(o0 ? (w0 >> 16) : w0);
+                const float d1 = half_bits_to_float(o1 ? (w1 >> 16) : w1);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     F[tt][nt][0] = fmaf((float)I[tt][nt][0], d0 * cs[nt].x, F[tt][nt][0]);
@@ -312,18 +404,20 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const GemvPara
             }
         }
 
-        const bool last = (cst + 1u) * 2u >= nblk_u;
+        const uint32_t p = cc.p, rg = cc.rg;
+        const bool rg_done = (cc.blk + 1 == P.nb) || (cc.tb + 1 == tb1);
+        cursor_next(L, cc);
         __syncwarp();
         issue();  // refill the slot just consumed
         slot = (slot + 1 == NSTAGES) ? 0 : slot + 1;
-        if (!last) {
-            ++cst;
-            continue;
-        }
+        if (!rg_done) continue;
 
-        // ---- unit epilogue: reduce limb columns to tokens, write out or a split-K partial ----
+        // ---- row group epilogue: reduce limb columns to tokens; write out or a partial ----
+        const uint32_t rg_first = (P.tb_begin + rg * P.nb) * 8, rg_end = rg_first + P.nb * 8;
+        const bool complete = a <= rg_first && b >= rg_end;
         const uint32_t row0 = rg * ROWS;
-        float* dst_base = p.S == 1 ? p.out : p.partial + (size_t)s * p.M * p.N;
+        const uint32_t j = a >= rg_first ? 0u : 1u;  // this row group is my first (0) or last (1)
+        float* pslot = L.partial + ((size_t)w * 2 + j) * ROWS * L.M;
 #pragma unroll
         for (int tt = 0; tt < T; ++tt) {
 #pragma unroll
@@ -333,36 +427,44 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const GemvPara
                 v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 1);
                 v1 += __shfl_xor_sync(0xFFFFFFFFu, v1, 1);
                 const uint32_t m = nt * 2 + (t >> 1);
-                const uint32_t r0 = row0 + tt * 16 + g, r1 = r0 + 8;
-                if ((t & 1) == 0 && m < p.M) {
-                    float* dst = dst_base + (size_t)m * p.N;
-                    if (r0 < p.N) dst[r0] = v0;
-                    if (r1 < p.N) dst[r1] = v1;
+                const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
+                if ((t & 1) == 0 && m < L.M) {
+                    if (complete) {
+                        float* o = P.out + (size_t)m * P.N;
+                        if (row0 + r0 < P.N) o[row0 + r0] = v0;
+                        if (row0 + r1 < P.N) o[row0 + r1] = v1;
+                    } else {
+                        pslot[m * ROWS + r0] = v0;
+                        pslot[m * ROWS + r1] = v1;
+                    }
                 }
                 F[tt][nt][0] = F[tt][nt][1] = F[tt][nt][2] = F[tt][nt][3] = 0.0f;
             }
         }
-        if (p.S > 1) {
+        if (!complete) {
+            const uint32_t w_first = part.owner(rg_first), w_last = part.owner(rg_end - 1);
+            const uint32_t count = w_last - w_first + 1;
             __threadfence();
             __syncwarp();
             uint32_t prev = 0;
-            if (lane == 0) prev = atomicAdd(p.counters + rg, 1u);
+            if (lane == 0) prev = atomicAdd(L.counters + P.counter_base + rg, 1u);
             prev = __shfl_sync(0xFFFFFFFFu, prev, 0);
-            if (prev == p.S - 1) {
+            if (prev == count - 1) {
                 __threadfence();
-                for (uint32_t idx = lane; idx < (uint32_t)ROWS * p.M; idx += 32) {
-                    const uint32_t m = idx / ROWS, row = row0 + idx % ROWS;
-                    if (row >= p.N) continue;
+                for (uint32_t idx = lane; idx < (uint32_t)ROWS * L.M; idx += 32) {
+                    const uint32_t m = idx / ROWS, r = idx % ROWS;
+                    if (row0 + r >= P.N) continue;
                     float acc = 0.0f;
-                    for (uint32_t ss = 0; ss < p.S; ++ss)
-                        acc += __ldcg(p.partial + ((size_t)ss * p.M + m) * p.N + row);
-                    p.out[(size_t)m * p.N + row] = acc;
+                    for (uint32_t ww = w_first; ww <= w_last; ++ww) {
+                        const uint32_t jj = part.begin(ww) >= rg_first ? 0u : 1u;
+                        acc += __ldcg(L.partial + ((size_t)ww * 2 + jj) * ROWS * L.M + m * ROWS + r);
+                    }
+                    P.out[(size_t)m * P.N + row0 + r] = acc;
                 }
-                if (lane == 0) p.counters[rg] = 0u;
+                if (lane == 0) L.counters[P.counter_base + rg] = 0u;
             }
         }
-        cst = 0;
-        cu += W;
+        (void)p;
     }
     cp_async_wait<0>();
     pdl_launch_dependents();
@@ -386,9 +488,9 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const XT* __restrict_
     const int lane = threadIdx.x & 31;
     const uint32_t mchunks = (M + 7) / 8;
     const size_t total = (size_t)N * mchunks;
-    for (size_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total;
-         w += (size_t)gridDim.x * blockDim.x / 32) {
-        const uint32_t n = (uint32_t)(w / mchunks), mc = (uint32_t)(w % mchunks) * 8;
+    for (size_t wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < total;
+         wi += (size_t)gridDim.x * blockDim.x / 32) {
+        const uint32_t n = (uint32_t)(wi / mchunks), mc = (uint32_t)(wi % mchunks) * 8;
         float acc[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
@@ -403,10 +505,10 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const XT* __restrict_
             const uint32_t signs = ksigns_s[(aux_s >> (7 * gi)) & 0x7F];
             const size_t k0 = (size_t)sbk * 32 + gi * 8;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const size_t k = k0 + j;
+            for (int jj = 0; jj < 8; ++jj) {
+                const size_t k = k0 + jj;
                 if (k >= K) break;
-                const float wv = dl * (float)((gw >> (8 * j)) & 0xFF) * (((signs >> j) & 1u) ? -1.0f : 1.0f);
+                const float wv = dl * (float)((gw >> (8 * jj)) & 0xFF) * (((signs >> jj) & 1u) ? -1.0f : 1.0f);
 #pragma unroll
                 for (int mm = 0; mm < 8; ++mm) {
                     if (mc + mm < M) acc[mm] = fmaf(to_f32(x[(size_t)(mc + mm) * K + k]), wv, acc[mm]);
@@ -424,60 +526,95 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const XT* __restrict_
 }
 
 // ---------------------------------------------------------------------------------------------
-template <int NT>
-int nt_of() { return NT; }
-
-struct Plan {
-    int nt;
-    uint32_t rows, row_groups, S, kb, units, grid;
-    size_t off_xb, off_cs, off_partial, off_counters, total;
-};
-
+// Host-side planning of a grouped launch: workspace layout and launch parameters.
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-Plan make_plan(uint32_t m, uint32_t n, uint32_t k, int num_sms) {
-    Plan pl{};
-    pl.nt = m <= 2 ? 1 : (m <= 4 ? 2 : (m <= 8 ? 4 : 8));
-    pl.rows = pl.nt <= 2 ? 32u : 16u;
-    const uint32_t nb = (k + QK - 1) / QK;
-    pl.row_groups = (n + pl.rows - 1) / pl.rows;
-    const uint64_t warps = (uint64_t)num_sms * GEMV_WARPS;
-    uint32_t kb = 2;
-    while (kb * 2 <= nb && (uint64_t)pl.row_groups * ((nb + kb * 2 - 1) / (kb * 2)) >= 6 * warps) kb *= 2;
-    pl.kb = kb;
-    pl.S = (nb + kb - 1) / kb;
-    pl.units = pl.row_groups * pl.S;
-    const uint64_t ctas = (pl.units + GEMV_WARPS - 1) / GEMV_WARPS;
-    pl.grid = (uint32_t)(ctas < (uint64_t)num_sms ? ctas : (uint64_t)num_sms);
+struct GroupPlan {
+    int nt, rows;
+    uint32_t warps;          // W = grid * GEMV_WARPS
+    uint32_t grid;
+    uint32_t total_steps;
+    size_t off_counters, off_partial, off_x, total;
+    std::vector<uint32_t> x_of;       // problem -> unique x index
+    std::vector<const void*> xs;      // unique x pointers
+    std::vector<uint32_t> xk;         // their K
+    std::vector<size_t> off_xb, off_cs;
+    std::vector<uint32_t> counter_base;
+};
+
+GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int num_sms) {
+    GroupPlan pl;
+    pl.nt = nt_for(m);
+    pl.rows = rows_for(m);
+    uint64_t steps = 0;
+    uint32_t counters = 0;
+    pl.counter_base.resize(count);
+    for (uint32_t i = 0; i < count; ++i) {
+        const uint32_t nb = (probs[i].k + QK - 1) / QK;
+        const uint32_t rgs = (probs[i].n + pl.rows - 1) / pl.rows;
+        pl.counter_base[i] = counters;
+        counters += rgs;
+        steps += (uint64_t)rgs * nb * 8;
+        uint32_t xi = 0;
+        while (xi < pl.xs.size() && !(pl.xs[xi] == probs[i].x && pl.xk[xi] == probs[i].k)) ++xi;
+        if (xi == pl.xs.size()) {
+            pl.xs.push_back(probs[i].x);
+            pl.xk.push_back(probs[i].k);
+        }
+        pl.x_of.push_back(xi);
+    }
+    pl.total_steps = (uint32_t)steps;
+    // at least ~16 steps per warp, at most one CTA per SM
+    uint64_t ctas = (steps + (uint64_t)GEMV_WARPS * 16 - 1) / ((uint64_t)GEMV_WARPS * 16);
+    if (ctas < 1) ctas = 1;
+    if (ctas > (uint64_t)num_sms) ctas = num_sms;
+    pl.grid = (uint32_t)ctas;
+    pl.warps = pl.grid * GEMV_WARPS;
     size_t off = 0;
-    pl.off_xb = off;
-    off = align_up(off + (size_t)nb * 8 * pl.nt * 256, 256);
-    pl.off_cs = off;
-    off = align_up(off + (size_t)nb * pl.nt * 8 * sizeof(float), 256);
-    pl.off_partial = off;
-    if (pl.S > 1) off = align_up(off + (size_t)pl.S * m * n * sizeof(float), 256);
     pl.off_counters = off;
-    if (pl.S > 1) off = align_up(off + (size_t)pl.row_groups * sizeof(uint32_t), 256);
+    off = align_up(off + (size_t)counters * sizeof(uint32_t), 256);
+    pl.off_partial = off;
+    off = align_up(off + (size_t)pl.warps * 2 * pl.rows * m * sizeof(float), 256);
+    pl.off_x = off;
+    for (size_t xi = 0; xi < pl.xs.size(); ++xi) {
+        const uint32_t nb = (pl.xk[xi] + QK - 1) / QK;
+        pl.off_xb.push_back(off);
+        off = align_up(off + (size_t)nb * 8 * pl.nt * 256, 256);
+        pl.off_cs.push_back(off);
+        off = align_up(off + (size_t)nb * pl.nt * 8 * sizeof(float), 256);
+    }
     pl.total = off;
     return pl;
 }
 
 template <int NT>
-cudaError_t launch_gemv_nt(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
-                           uint32_t n, uint32_t k, float* out, uint8_t* ws, const Plan& pl,
-                           cudaStream_t stream) {
-    const uint32_t nb = (k + QK - 1) / QK;
-    uint8_t* xb = ws + pl.off_xb;
-    float* cs = reinterpret_cast<float*>(ws + pl.off_cs);
-    float* partial = reinterpret_cast<float*>(ws + pl.off_partial);
-    uint32_t* counters = reinterpret_cast<uint32_t*>(ws + pl.off_counters);
-    const uint32_t ncounters = pl.S > 1 ? pl.row_groups : 0u;
-    const uint32_t prep_blocks = (m * nb * 32 + 255) / 256;
+cudaError_t launch_group_nt(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
+                            uint8_t* ws, const GroupPlan& pl, cudaStream_t stream) {
+    using S_ = GemvShape<NT>;
+    // ---- prep launch (unique x's) ----
+    PrepLaunch pre;
+    pre.count = (uint32_t)pl.xs.size();
+    pre.M = m;
+    pre.counters = reinterpret_cast<uint32_t*>(ws + pl.off_counters);
+    pre.ncounters = pl.counter_base.empty() ? 0u
+                                            : pl.counter_base.back() + (probs[count - 1].n + pl.rows - 1) / pl.rows;
+    uint32_t warps = 0;
+    for (uint32_t xi = 0; xi < pre.count; ++xi) {
+        PrepItem& it = pre.item[xi];
+        it.x = pl.xs[xi];
+        it.xb = ws + pl.off_xb[xi];
+        it.colscale = reinterpret_cast<float*>(ws + pl.off_cs[xi]);
+        it.K = pl.xk[xi];
+        it.nb = (pl.xk[xi] + QK - 1) / QK;
+        it.warp_begin = warps;
+        it.pad = 0;
+        warps += m * it.nb;
+    }
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(prep_blocks);
+    cfg.gridDim = dim3((warps * 32 + 255) / 256);
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
@@ -485,43 +622,49 @@ cudaError_t launch_gemv_nt(const void* x, int x_dtype, uint32_t m, const uint8_t
     cfg.numAttrs = 1;
     cudaError_t e;
     switch (x_dtype) {
-        case 0: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<float, NT>, static_cast<const float*>(x), m, k,
-                                       nb, xb, cs, counters, ncounters); break;
-        case 1: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__half, NT>, static_cast<const __half*>(x), m,
-                                       k, nb, xb, cs, counters, ncounters); break;
-        default: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__nv_bfloat16, NT>,
-                                        static_cast<const __nv_bfloat16*>(x), m, k, nb, xb, cs, counters,
-                                        ncounters); break;
+        case 0: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<float, NT>, pre); break;
+        case 1: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__half, NT>, pre); break;
+        default: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__nv_bfloat16, NT>, pre); break;
     }
     if (e != cudaSuccess) return e;
-    using S_ = GemvShape<NT>;
-    static bool attr_set[64] = {};  // per device; benign race (idempotent attribute set)
+
+    // ---- GEMV launch ----
+    static bool attr_set[64] = {};  // per device; an idempotent attribute, so a race is benign
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev]) {
+    if (dev >= 64 || !attr_set[dev]) {
         e = cudaFuncSetAttribute(gemv_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, S_::SMEM);
         if (e != cudaSuccess) return e;
-        attr_set[dev] = true;
+        if (dev < 64) attr_set[dev] = true;
     }
-    GemvParams p;
-    p.qs = qs;
-    p.sc = sc;
-    p.xb = xb;
-    p.colscale = cs;
-    p.out = out;
-    p.partial = partial;
-    p.counters = counters;
-    p.row_bytes = (size_t)nb * QS_BYTES;
-    p.M = m;
-    p.N = n;
-    p.nb = nb;
-    p.S = pl.S;
-    p.kb = pl.kb;
-    p.total_units = pl.units;
+    GemvLaunch L;
+    L.count = count;
+    L.M = m;
+    L.total_steps = pl.total_steps;
+    L.pad = 0;
+    L.partial = reinterpret_cast<float*>(ws + pl.off_partial);
+    L.counters = reinterpret_cast<uint32_t*>(ws + pl.off_counters);
+    uint32_t tb = 0;
+    for (uint32_t i = 0; i < count; ++i) {
+        GemvProblem& P = L.prob[i];
+        const uint32_t nb = (probs[i].k + QK - 1) / QK;
+        P.qs = probs[i].qs;
+        P.sc = probs[i].sc;
+        P.xb = ws + pl.off_xb[pl.x_of[i]];
+        P.colscale = reinterpret_cast<const float*>(ws + pl.off_cs[pl.x_of[i]]);
+        P.out = probs[i].out;
+        P.N = probs[i].n;
+        P.nb = nb;
+        P.row_groups = (probs[i].n + pl.rows - 1) / pl.rows;
+        P.tb_begin = tb;
+        P.counter_base = pl.counter_base[i];
+        P.pad = 0;
+        tb += P.row_groups * nb;
+    }
     cfg.gridDim = dim3(pl.grid);
     cfg.blockDim = dim3(GEMV_WARPS * 32);
     cfg.dynamicSmemBytes = S_::SMEM;
-    e = cudaLaunchKernelEx(&cfg, gemv_kernel<NT>, p);
+    e = cudaLaunchKernelEx(&cfg, gemv_kernel<NT>, L);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -529,26 +672,40 @@ cudaError_t launch_gemv_nt(const void* x, int x_dtype, uint32_t m, const uint8_t
 }  // namespace
 
 bool gemv_fast_path_ok(uint32_t m, uint32_t k, const uint8_t* qs, const uint8_t* sc) {
-    const uint32_t nb = (k + QK - 1) / QK;
-    return m >= 1 && m <= 16 && nb >= 2 && (nb % 2) == 0 &&
-           (reinterpret_cast<uintptr_t>(qs) % 16) == 0 && (reinterpret_cast<uintptr_t>(sc) % 4) == 0;
+    return m >= 1 && m <= 16 && k >= 1 && (reinterpret_cast<uintptr_t>(qs) % 16) == 0 &&
+           (reinterpret_cast<uintptr_t>(sc) % 4) == 0;
+}
+
+uint32_t gemv_max_group() { return MAX_PROBLEMS; }
+
+size_t gemv_group_workspace_size(const GemvProblemHost* probs, uint32_t count, uint32_t m, int num_sms) {
+    if (count == 0) return 0;
+    return plan_group(probs, count, m, num_sms).total;
 }
 
 size_t gemv_workspace_size(uint32_t m, uint32_t n, uint32_t k, int num_sms) {
-    return make_plan(m, n, k, num_sms).total;
+    GemvProblemHost p{nullptr, nullptr, nullptr, n, k, nullptr};
+    return gemv_group_workspace_size(&p, 1, m, num_sms);
+}
+
+cudaError_t launch_gemv_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
+                              void* workspace, int num_sms, cudaStream_t stream) {
+    if (count == 0) return cudaSuccess;
+    const GroupPlan pl = plan_group(probs, count, m, num_sms);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    switch (pl.nt) {
+        case 1: return launch_group_nt<1>(probs, count, m, x_dtype, ws, pl, stream);
+        case 2: return launch_group_nt<2>(probs, count, m, x_dtype, ws, pl, stream);
+        case 4: return launch_group_nt<4>(probs, count, m, x_dtype, ws, pl, stream);
+        default: return launch_group_nt<8>(probs, count, m, x_dtype, ws, pl, stream);
+    }
 }
 
 cudaError_t launch_gemv(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
                         uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,
                         cudaStream_t stream) {
-    const Plan pl = make_plan(m, n, k, num_sms);
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    switch (pl.nt) {
-        case 1: return launch_gemv_nt<1>(x, x_dtype, m, qs, sc, n, k, out, ws, pl, stream);
-        case 2: return launch_gemv_nt<2>(x, x_dtype, m, qs, sc, n, k, out, ws, pl, stream);
-        case 4: return launch_gemv_nt<4>(x, x_dtype, m, qs, sc, n, k, out, ws, pl, stream);
-        default: return launch_gemv_nt<8>(x, x_dtype, m, qs, sc, n, k, out, ws, pl, stream);
-    }
+    GemvProblemHost p{x, qs, sc, n, k, out};
+    return launch_gemv_group(&p, 1, m, x_dtype, workspace, num_sms, stream);
 }
 
 cudaError_t launch_gemv_generic(const void* x, int x_dtype, uint32_t m, const uint8_t* qs,

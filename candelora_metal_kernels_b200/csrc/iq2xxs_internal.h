@@ -7,8 +7,20 @@
 
 namespace iq2 {
 
-// Decode GEMV (iq2xxs_gemv.cu), m <= 16.
+// Decode GEMV (iq2xxs_gemv.cu), m <= 16. A group is up to gemv_max_group() projections with
+// the same m and x dtype, computed by one prep launch and one GEMV launch.
+struct GemvProblemHost {
+    const void* x;
+    const uint8_t* qs;
+    const uint8_t* sc;
+    uint32_t n, k;
+    float* out;
+};
 bool gemv_fast_path_ok(uint32_t m, uint32_t k, const uint8_t* qs, const uint8_t* sc);
+uint32_t gemv_max_group();
+size_t gemv_group_workspace_size(const GemvProblemHost* probs, uint32_t count, uint32_t m, int num_sms);
+cudaError_t launch_gemv_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
+                              void* workspace, int num_sms, cudaStream_t stream);
 size_t gemv_workspace_size(uint32_t m, uint32_t n, uint32_t k, int num_sms);
 cudaError_t launch_gemv(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
                         uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,

@@ -150,6 +150,62 @@ def iq2_matmul_with_activation_quant(x, weight_bytes, weight_scales, out_dim, in
                    strict=activation_quant.strict, out=out, workspace=workspace)
 
 
+def iq2_matmul_grouped(problems, *, workspace=None):
+    """Several IQ2_XXS projections with the same m and x dtype in as few launches as possible
+    (iq2_matmul_grouped in the C ABI; no reference counterpart -- the reference dispatches one
+    projection at a time). `problems` is a sequence of (x, weight_bytes, weight_scales, out_dim,
+    in_dim) or (..., out) tuples, x of shape [m, in_dim]; returns the list of f32 outputs."""
+    lib = _lib.load()
+    op = "iq2_matmul_grouped"
+    if not problems:
+        return []
+    outs, keep = [], []
+    arr = (_lib.Iq2MatmulProblem * len(problems))()
+    m = dtype = device = None
+    for i, pr in enumerate(problems):
+        x, wb, ws, out_dim, in_dim = pr[:5]
+        out = pr[5] if len(pr) > 5 else None
+        _check_common(op, wb, ws, out_dim, in_dim, x)
+        x2, mi, _ = _parse_x_shape(x, in_dim)
+        x2 = x2.contiguous()
+        _check_weight_layout(op, wb, ws)
+        if x2.dtype not in _X_DTYPES:
+            _bail(_lib.IQ2_ERR_DTYPE, f"iq2_matmul unsupported x dtype: {x2.dtype}")
+        if m is None:
+            m, dtype, device = mi, x2.dtype, x.device
+        elif mi != m or x2.dtype != dtype or x.device != device:
+            _bail(_lib.IQ2_ERR_INVALID_ARGUMENT, f"{op}: every problem needs the same m, x dtype and device")
+        if out is None:
+            out = torch.empty((mi, out_dim), dtype=torch.float32, device=x.device)
+        keep.append(x2)
+        outs.append(out)
+        arr[i] = _lib.Iq2MatmulProblem(x2.data_ptr(), wb.data_ptr(), wb.numel(), ws.data_ptr(), ws.numel(),
+                                       out_dim, in_dim, out.data_ptr())
+    with torch.cuda.device(device):
+        need = int(lib.iq2_matmul_grouped_workspace_size(arr, len(problems), m, _X_DTYPES[dtype]))
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
+        rc = lib.iq2_matmul_grouped(arr, len(problems), m, _X_DTYPES[dtype], ctypes.c_void_p(workspace.data_ptr()),
+                                    workspace.numel(), _stream_handle(device))
+    _lib.check(rc)
+    return outs
+
+
+def grouped_workspace_bytes(problems) -> int:
+    """Workspace iq2_matmul_grouped needs for these (x, weight_bytes, weight_scales, out_dim,
+    in_dim[, out]) problems (the output pointers do not affect the size)."""
+    lib = _lib.load()
+    arr = (_lib.Iq2MatmulProblem * len(problems))()
+    m = dtype = None
+    for i, pr in enumerate(problems):
+        x, wb, ws, out_dim, in_dim = pr[:5]
+        x2, mi, _ = _parse_x_shape(x, in_dim)
+        m, dtype = mi, x2.dtype
+        arr[i] = _lib.Iq2MatmulProblem(x2.data_ptr(), wb.data_ptr(), wb.numel(), ws.data_ptr(), ws.numel(),
+                                       out_dim, in_dim, None)
+    return int(lib.iq2_matmul_grouped_workspace_size(arr, len(problems), m, _X_DTYPES[dtype]))
+
+
 def iq2_dequantize(weight_bytes, weight_scales, out_dim, in_dim, variant=Iq2MatmulVariant.Iq2Xxs,
                    dtype: torch.dtype = torch.float16, out=None) -> torch.Tensor:
     """Dense [out_dim, in_dim] weights in f16 (reference-identical), bf16 (RNE) or f32 (exact)."""

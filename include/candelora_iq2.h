@@ -103,6 +103,32 @@ int iq2_matmul_with_activation_quant(const void* x, int x_dtype, uint32_t m,
                                      int strict, float* out, void* workspace,
                                      size_t workspace_bytes, iq2_stream_t stream);
 
+/* One projection of a grouped call (see iq2_matmul_grouped). */
+typedef struct iq2_matmul_problem {
+    const void* x;                 /* [m, in_dim] in the call's x_dtype                      */
+    const uint8_t* weight_bytes;   /* IQ2_XXS qs, layout as for iq2_matmul                   */
+    size_t weight_bytes_len;
+    const uint8_t* weight_scales;  /* fp16 d per block                                       */
+    size_t weight_scales_len;
+    uint32_t out_dim, in_dim;
+    float* out;                    /* [m, out_dim] f32                                       */
+} iq2_matmul_problem;
+
+/* Bytes of device scratch iq2_matmul_grouped needs for these problems. */
+size_t iq2_matmul_grouped_workspace_size(const iq2_matmul_problem* problems, uint32_t count,
+                                         uint32_t m, int x_dtype);
+
+/*
+ * `count` independent IQ2_XXS projections with the same m and x dtype, e.g. the q/k/v or
+ * gate/up projections of a layer, in as few launches as possible (one x-prep and one GEMV
+ * launch per 256 projections when m <= 16; projections that share an x pointer share its
+ * preparation). Each problem's result equals iq2_matmul on it. No reference counterpart: the
+ * reference issues one dispatch per projection (src/iq2_matmul.rs:316-357); this is the batched
+ * form of that call.
+ */
+int iq2_matmul_grouped(const iq2_matmul_problem* problems, uint32_t count, uint32_t m, int x_dtype,
+                       void* workspace, size_t workspace_bytes, iq2_stream_t stream);
+
 /*
  * Dense dequantisation to out [out_dim, in_dim] in out_dtype (f16 / bf16 / f32).
  * Replaces iq2_dequantize_to_f16 (src/iq2_matmul.rs:593-602, :367-505) when out_dtype is

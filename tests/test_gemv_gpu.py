@@ -141,3 +141,45 @@ def test_nonfinite_activation_block_gives_nan_row():
     x[1, 300] = float("inf")
     y = c.iq2_xxs_matmul(x, qs.cuda(), sc.cuda(), n, k)
     assert torch.isfinite(y[0]).all() and not torch.isfinite(y[1]).any()
+
+
+def test_grouped_matches_oracle_and_single_calls(oracle):
+    """iq2_matmul_grouped over projections of different shapes, two of them sharing x."""
+    m = 2
+    shapes = [(4096, 4096), (1024, 4096), (1024, 4096), (14336, 1024), (300, 320), (4096, 14336)]
+    xs = {k: synth.activations(m, k, seed=k, device="cuda") for k in {k for _, k in shapes}}
+    probs, refs = [], []
+    for i, (n, k) in enumerate(shapes):
+        qs, sc = synth.iq2xxs_weights(n, k, seed=500 + i)
+        probs.append((xs[k], qs.cuda(), sc.cuda(), n, k))
+        cols = np.unique(np.concatenate([np.arange(min(n, 16)), np.random.default_rng(i).integers(0, n, 24), [n - 1]]))
+        refs.append((cols, oracle.matmul(xs[k].cpu().numpy(), qs.numpy(), sc.numpy(), n, k, cols=cols)))
+    outs = c.iq2_matmul_grouped(probs)
+    for (cols, ref), y, pr in zip(refs, outs, probs):
+        assert rel_l2(y.cpu().numpy()[:, cols], ref) <= GEMV_TOL
+        single = c.iq2_xxs_matmul(*pr[:5])
+        assert rel_l2(y.cpu().numpy(), single.cpu().numpy()) <= 1e-6
+
+
+def test_grouped_many_problems_beyond_one_launch(oracle):
+    """More projections than one launch holds (256): split into several launches."""
+    m, n, k = 1, 64, 512
+    x = synth.activations(m, k, seed=3, device="cuda")
+    probs = []
+    for i in range(300):
+        qs, sc = synth.iq2xxs_weights(n, k, seed=i)
+        probs.append((x, qs.cuda(), sc.cuda(), n, k))
+    outs = c.iq2_matmul_grouped(probs)
+    for i in (0, 255, 256, 299):
+        qs, sc = probs[i][1].cpu().numpy(), probs[i][2].cpu().numpy()
+        assert rel_l2(outs[i].cpu().numpy(), oracle.matmul(x.cpu().numpy(), qs, sc, n, k)) <= GEMV_TOL
+
+
+def test_stream_k_boundaries_all_m(oracle):
+    """Shapes whose step counts split unevenly over the warps, for every n8-tile width."""
+    for m in (1, 2, 3, 4, 6, 8, 11, 16):
+        n, k = 97, 2816  # 11 blocks per row
+        qs, sc = synth.iq2xxs_weights(n, k, seed=m)
+        x = synth.activations(m, k, seed=m + 100, device="cuda")
+        y = c.iq2_xxs_matmul(x, qs.cuda(), sc.cuda(), n, k)
+        assert rel_l2(y.cpu().numpy(), oracle.matmul(x.cpu().numpy(), qs.numpy(), sc.numpy(), n, k)) <= GEMV_TOL, m
