@@ -40,6 +40,32 @@ __device__ __forceinline__ uint2 lds64(const uint8_t* base, uint32_t off) {
     return *reinterpret_cast<const uint2*>(base + off);
 }
 
+// Shared-memory loads from 32-bit shared-window addresses (PTX .shared state space).
+// ld_shared_const: for tables that are read-only once filled (after a barrier that the load
+// depends on through its address), so the compiler may schedule it freely.
+__device__ __forceinline__ uint32_t ld_shared_const(uint32_t addr) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+// ld_shared_v4: 16 bytes at addr + OFF, kept in program order with the other volatile asm
+// (the cp.async waits that make the data valid).
+template <int OFF>
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4+%5];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr), "n"(OFF));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ld_shared_u32_volatile(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
 // 16-byte (or `bytes`-wide) asynchronous global->shared copy; src_bytes = 0 writes zeros and
 // reads nothing.
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {

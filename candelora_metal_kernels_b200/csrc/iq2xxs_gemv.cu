@@ -41,7 +41,7 @@ namespace {
 
 constexpr int GEMV_WARPS = 16;
 constexpr int LUT_BYTES = 256 * 256;  // 256 rows x (32 lanes grid selectors | 32 lanes sign)
-constexpr int MAX_PROBLEMS = 256;     // per launch
+constexpr int MAX_PROBLEMS = 256;     // per grouped launch
 
 template <int NT>
 struct GemvShape {
@@ -50,7 +50,10 @@ struct GemvShape {
     static constexpr int STAGE_QS = ROWS * 64;         // one block of qs per row
     static constexpr int STAGE_BYTES = STAGE_QS + ROWS * 4;  // + the aligned scale word per row
     static constexpr int NSTAGES = T == 2 ? 4 : 8;
-    static constexpr int SMEM = LUT_BYTES + GEMV_WARPS * NSTAGES * STAGE_BYTES;
+    static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;  // per warp
+    // The table sits at the first 64 KB-aligned shared address of the block's window and the
+    // warps' rings fill the space around it; whatever the window's base, this suffices:
+    static constexpr int SMEM = LUT_BYTES + (GEMV_WARPS + 1) * RING_BYTES;
 };
 
 int nt_for(uint32_t m) { return m <= 2 ? 1 : (m <= 4 ? 2 : (m <= 8 ? 4 : 8)); }
@@ -72,15 +75,16 @@ struct PrepItem {
     uint32_t K, nb, warp_begin, pad;
 };
 
+template <int CAP>
 struct PrepLaunch {
-    PrepItem item[MAX_PROBLEMS];
+    PrepItem item[CAP];
     uint32_t count, M;
     uint32_t* counters;
     uint32_t ncounters;
 };
 
-template <typename XT, int NT>
-__global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ PrepLaunch L) {
+template <typename XT, int NT, int CAP>
+__global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ PrepLaunch<CAP> L) {
     // x may be written by the previous kernel and the workspace may still be read by the
     // previous GEMV: wait for both before touching memory. Only then let the GEMV launch, so
     // its early weight prefetch also runs after every earlier kernel has finished.
@@ -158,8 +162,9 @@ struct GemvProblem {  // 64 bytes
     uint32_t counter_base, pad;
 };
 
+template <int CAP>
 struct GemvLaunch {
-    GemvProblem prob[MAX_PROBLEMS];
+    GemvProblem prob[CAP];
     uint32_t count, M;
     uint32_t total_steps;  // 8 sub-block steps per tile-block
     uint32_t pad;
@@ -177,24 +182,13 @@ struct Partition {
     }
 };
 
-// Four signed int8 weights of one 8-weight group (sub-block word {aux_g, aux_s}) for this
-// lane's group t: lo = weights 0..3, hi = weights 4..7.
-__device__ __forceinline__ void decode_group(const uint8_t* lut, uint32_t aux_g, uint32_t aux_s,
-                                             uint32_t selg, uint32_t laneoff, uint32_t rot,
-                                             uint32_t soff, uint32_t& lo, uint32_t& hi) {
-    const uint32_t ga = prmt(aux_g, laneoff, selg);                             // idx*256 + lane*4
-    const uint32_t sa = (__funnelshift_r(aux_s, aux_s, rot) & 0x7F00u) | soff;  // sidx*256+128+lane*4
-    const uint32_t sel = lds32(lut, ga) | lds32(lut, sa);
-    lo = prmt(KPOS, KNEG, sel);
-    hi = prmt(KPOS, KNEG, sel >> 16);
-}
-
 // Cursor over the tile-blocks (problem p, row group rg, block blk) of a launch, in order.
 struct TbCursor {
     uint32_t tb, p, rg, blk;
 };
 
-__device__ __forceinline__ void cursor_seek(const GemvLaunch& L, uint32_t tb, TbCursor& c) {
+template <int CAP>
+__device__ __forceinline__ void cursor_seek(const GemvLaunch<CAP>& L, uint32_t tb, TbCursor& c) {
     uint32_t p = 0;
     while (p + 1 < L.count && L.prob[p + 1].tb_begin <= tb) ++p;
     const uint32_t local = tb - L.prob[p].tb_begin;
@@ -204,7 +198,8 @@ __device__ __forceinline__ void cursor_seek(const GemvLaunch& L, uint32_t tb, Tb
     c.blk = local % L.prob[p].nb;
 }
 
-__device__ __forceinline__ void cursor_next(const GemvLaunch& L, TbCursor& c) {
+template <int CAP>
+__device__ __forceinline__ void cursor_next(const GemvLaunch<CAP>& L, TbCursor& c) {
     ++c.tb;
     if (++c.blk == L.prob[c.p].nb) {
         c.blk = 0;
@@ -215,16 +210,100 @@ __device__ __forceinline__ void cursor_next(const GemvLaunch& L, TbCursor& c) {
     }
 }
 
-template <int NT>
-__global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvLaunch L) {
+// Per-lane decode constants. The table base is 64 KB-aligned, so every table address is
+// assembled by one byte permute (grid: base | idx<<8 | lane*4) or one LOP3 (sign: base | 128 |
+// sidx<<8 | lane*4), with no add.
+struct DecodeK {
+    uint32_t gsrc;  // bytes {lane*4, 0, base.b2, base.b3}
+    uint32_t gsel;  // prmt selector {gsrc.b0, aux_g.byte t, gsrc.b2, gsrc.b3}
+    uint32_t rot;   // rotate that brings sign index t (bits 7t..7t+6) to bits 8..14
+    uint32_t soff;  // base | 128 | lane*4
+};
+
+// Four signed int8 weights of one 8-weight group (sub-block word {aux_g, aux_s}) for this
+// lane's group t: lo = weights 0..3, hi = weights 4..7.
+__device__ __forceinline__ void decode_group(const DecodeK& k, uint32_t aux_g, uint32_t aux_s,
+                                             uint32_t& lo, uint32_t& hi) {
+    const uint32_t ga = prmt(aux_g, k.gsrc, k.gsel);
+    const uint32_t sa = (__funnelshift_r(aux_s, aux_s, k.rot) & 0x7F00u) | k.soff;
+    const uint32_t sel = ld_shared_const(ga) | ld_shared_const(sa);
+    lo = prmt(KPOS, KNEG, sel);
+    hi = prmt(KPOS, KNEG, sel >> 16);
+}
+
+// One stage (a block of ROWS rows) of the decode: accumulate s32 sums per 256-block in I.
+// PARTIAL: only sub-blocks [s_lo, s_hi) count (the first/last stage of a warp's range).
+template <int NT, bool PARTIAL>
+__device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, const uint8_t* xbp,
+                                              const bool (&bact)[NT], uint32_t s_lo, uint32_t s_hi,
+                                              uint32_t rowbase, uint32_t swz,
+                                              int (&I)[GemvShape<NT>::T][NT][4]) {
+    constexpr int T = GemvShape<NT>::T;
+#pragma unroll
+    for (int pair = 0; pair < 4; ++pair) {
+        // one 16-byte chunk = sub-blocks 2*pair and 2*pair+1 of a row
+        const uint32_t a0 = st_s + rowbase + (((uint32_t)pair ^ swz) << 4);
+        uint4 qw[T][2];
+        qw[0][0] = ld_shared_v4<0>(a0);
+        qw[0][1] = ld_shared_v4<512>(a0);
+        if (T == 2) {
+            qw[T - 1][0] = ld_shared_v4<1024>(a0);
+            qw[T - 1][1] = ld_shared_v4<1536>(a0);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t sb = pair * 2 + h;
+            uint32_t bf[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                bool on = bact[nt];
+                if (PARTIAL) on = on && sb >= s_lo && sb < s_hi;  // other sub-blocks add 0
+                uint2 v = make_uint2(0u, 0u);
+                if (on) v = __ldg(reinterpret_cast<const uint2*>(xbp + (sb * NT + nt) * 256));
+                bf[nt][0] = v.x;
+                bf[nt][1] = v.y;
+            }
+#pragma unroll
+            for (int tt = 0; tt < T; ++tt) {
+                const uint32_t g0 = h ? qw[tt][0].z : qw[tt][0].x, s0 = h ? qw[tt][0].w : qw[tt][0].y;
+                const uint32_t g1 = h ? qw[tt][1].z : qw[tt][1].x, s1 = h ? qw[tt][1].w : qw[tt][1].y;
+                uint32_t w0, w1, w2, w3;
+                decode_group(dk, g0, s0, w0, w2);
+                decode_group(dk, g1, s1, w1, w3);
+                const int c0 = (int)((s0 >> 27) | 1u), c1 = (int)((s1 >> 27) | 1u);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    int d[4];
+                    mma_s8_16832(d, w0, w1, w2, w3, bf[nt][0], bf[nt][1]);
+                    I[tt][nt][0] += c0 * d[0];
+                    I[tt][nt][1] += c0 * d[1];
+                    I[tt][nt][2] += c1 * d[2];
+                    I[tt][nt][3] += c1 * d[3];
+                }
+            }
+        }
+    }
+}
+
+template <int NT, int CAP>
+__global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvLaunch<CAP> L) {
     using S_ = GemvShape<NT>;
     constexpr int T = S_::T, ROWS = S_::ROWS, STAGE_QS = S_::STAGE_QS;
-    constexpr int STAGE_BYTES = S_::STAGE_BYTES, NSTAGES = S_::NSTAGES;
+    constexpr int STAGE_BYTES = S_::STAGE_BYTES, NSTAGES = S_::NSTAGES, RING_BYTES = S_::RING_BYTES;
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint8_t* lut = smem;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    uint8_t* ring = smem + LUT_BYTES + warp * (NSTAGES * STAGE_BYTES);
+
+    // ---- shared layout: table at the first 64 KB-aligned address, rings around it ----
+    const uint32_t base_s = smem_u32(smem);
+    const uint32_t lut_s = (base_s + 0xFFFFu) & ~0xFFFFu;
+    const uint32_t gap = lut_s - base_s;
+    const uint32_t gap_warps = gap / RING_BYTES;
+    const uint32_t ring_off = (uint32_t)warp < gap_warps
+                                  ? (uint32_t)warp * RING_BYTES
+                                  : gap + LUT_BYTES + ((uint32_t)warp - gap_warps) * RING_BYTES;
+    uint8_t* ring = smem + ring_off;
+    const uint32_t ring_s = base_s + ring_off;
 
     // This warp's step range [a, b) and the tile-blocks it touches [tb0, tb1).
     const uint32_t W = gridDim.x * GEMV_WARPS;
@@ -233,6 +312,14 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     const uint32_t a = part.begin(w), b = part.begin(w + 1);
     const uint32_t tb0 = a >> 3, tb1 = (b + 7) >> 3;
 
+    // ---- the decode table: 64 KB image from global memory (one cp.async group) ----
+    {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(&IQ2XXS_LUT_IMAGE);
+        for (int i = threadIdx.x; i < LUT_BYTES / 16; i += blockDim.x)
+            cp_async_16(lut_s + i * 16, src + i * 16, 16u);
+        cp_async_commit();
+    }
+
     // ---- issue side: cp.async stages of one tile-block each, NSTAGES ahead ----
     TbCursor ic;
     if (a < b) cursor_seek(L, tb0, ic);
@@ -240,31 +327,31 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     auto issue = [&]() {
         if (a < b && ic.tb < tb1) {
             const GemvProblem& P = L.prob[ic.p];
-            uint8_t* st = ring + islot * STAGE_BYTES;
+            const uint32_t st_s = ring_s + islot * STAGE_BYTES;
             const uint32_t s_lo = ic.tb * 8 < a ? a - ic.tb * 8 : 0u;        // first sub-block needed
             const uint32_t s_hi = min(8u, b - ic.tb * 8);                     // one past the last
             const uint32_t ch_lo = s_lo >> 1, ch_hi = (s_hi + 1) >> 1;        // 16-byte chunks needed
             const uint32_t row0 = ic.rg * ROWS;
+            const uint8_t* qrow = P.qs + ((size_t)row0 * P.nb + ic.blk) * QS_BYTES;
             const size_t row_bytes = (size_t)P.nb * QS_BYTES;
 #pragma unroll
             for (int c = 0; c < ROWS * 4 / 32; ++c) {
                 const int idx = c * 32 + lane;
                 const int r = idx >> 2, ch = idx & 3;
-                const uint32_t row = row0 + r;
-                const bool ok = row < P.N && (uint32_t)ch >= ch_lo && (uint32_t)ch < ch_hi;
-                const uint8_t* src = P.qs + (ok ? (size_t)row * row_bytes + (size_t)ic.blk * QS_BYTES + ch * 16 : 0);
-                // swizzle: chunk ch of row r goes to chunk ch ^ ((r >> 1) & 3); bank group r & 1
-                cp_async_16(smem_u32(st + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4)), src, ok ? 16u : 0u);
+                const bool ok = row0 + r < P.N && (uint32_t)ch >= ch_lo && (uint32_t)ch < ch_hi;
+                const uint8_t* src = ok ? qrow + (size_t)r * row_bytes + ch * 16 : P.qs;
+                // swizzle: chunk ch of row r goes to chunk ch ^ ((r >> 1) & 3)
+                cp_async_16(st_s + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4), src, ok ? 16u : 0u);
             }
             if (lane < ROWS) {
-                const uint32_t row = row0 + lane;
-                const bool ok = row < P.N;
                 // the 4-byte aligned word holding this row's d; near the end of the buffer only
                 // the bytes that exist are read (the rest of the word is zero-filled)
+                const uint32_t row = row0 + lane;
+                const bool ok = row < P.N;
                 const size_t e = ((size_t)row * P.nb + ic.blk) * SC_BYTES;
                 const size_t ea = e & ~(size_t)3, total = (size_t)P.N * P.nb * SC_BYTES;
                 const uint32_t nbytes = ok ? (uint32_t)min((size_t)4, total - ea) : 0u;
-                cp_async_4(smem_u32(st + STAGE_QS + lane * 4), P.sc + (ok ? ea : 0), nbytes);
+                cp_async_4(st_s + STAGE_QS + lane * 4, P.sc + (ok ? ea : 0), nbytes);
             }
             cursor_next(L, ic);
         }
@@ -272,21 +359,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         islot = (islot + 1 == NSTAGES) ? 0 : islot + 1;
     };
 
-    // Issue the first stages before anything else: they only read weights.
+    // The first stages only read weights: start them before waiting for anything.
 #pragma unroll
     for (int i = 0; i < NSTAGES; ++i) issue();
-
-    // Lane-replicated selector tables: row e holds IQ2XXS_GRID_SEL[e] in bytes [0,128) (one
-    // copy per lane) and IQ2XXS_SIGN_SEL[e] in [128,256) for e < 128. A lane only ever reads
-    // its own copy, so the random table lookups of a warp never conflict on a bank.
-    {
-        uint4* lw = reinterpret_cast<uint4*>(smem);
-        for (int i = threadIdx.x; i < 256 * 16; i += blockDim.x) {
-            const int e = i >> 4, q4 = i & 15;
-            const uint32_t v = (q4 < 8) ? IQ2XXS_GRID_SEL[e] : (e < 128 ? IQ2XXS_SIGN_SEL[e] : 0u);
-            lw[i] = make_uint4(v, v, v, v);
-        }
-    }
+    cp_async_wait<NSTAGES>();  // the table group (issued first) has landed
     __syncthreads();
     // x fragments, column scales, counters and outputs are produced by / shared with the prep
     // kernel: wait for it here.
@@ -297,13 +373,13 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         return;
     }
 
-    const uint32_t laneoff = (uint32_t)lane * 4u;
-    const uint32_t selg = 0x5504u | ((uint32_t)t << 4);
-    const uint32_t rot = (7u * t + 24u) & 31u;
-    const uint32_t soff = 128u + laneoff;
-    const uint32_t swz = (uint32_t)((g >> 1) & 3);   // rows g, g+8, g+16, g+24 share it
-    const uint32_t rowbase = (uint32_t)(g & 1) * 64u + (uint32_t)(g >> 1) * 128u;  // byte offset of row g
-    // rows tt*16+g and tt*16+g+8 are rowbase + tt*1024 and rowbase + tt*1024 + 512
+    DecodeK dk;
+    dk.gsrc = (lut_s & 0xFFFF0000u) | ((uint32_t)lane * 4u);
+    dk.gsel = 0x7604u | ((uint32_t)t << 4);
+    dk.rot = (7u * t + 24u) & 31u;
+    dk.soff = lut_s | 128u | ((uint32_t)lane * 4u);
+    const uint32_t swz = (uint32_t)((g >> 1) & 3);  // rows g, g+8, g+16, g+24 share it
+    const uint32_t rowbase = (uint32_t)g * 64u;     // rows tt*16+g (+8): rowbase + tt*1024 (+512)
 
     bool bact[NT];
 #pragma unroll
@@ -324,6 +400,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         const GemvProblem& P = L.prob[cc.p];
         cp_async_wait<NSTAGES - 1>();
         __syncwarp();
+        const uint32_t st_s = ring_s + slot * STAGE_BYTES;
         const uint8_t* st = ring + slot * STAGE_BYTES;
         const uint32_t s_lo = cc.tb * 8 < a ? a - cc.tb * 8 : 0u;
         const uint32_t s_hi = min(8u, b - cc.tb * 8);
@@ -337,48 +414,11 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 for (int k = 0; k < 4; ++k) I[i][j][k] = 0;
 
         const uint8_t* xbp = P.xb + (size_t)cc.blk * 8 * NT * 256 + lane * 8;
-#pragma unroll
-        for (int pair = 0; pair < 4; ++pair) {
-            // one 16-byte chunk = sub-blocks 2*pair and 2*pair+1 of every row
-            const uint32_t coff = ((uint32_t)pair ^ swz) << 4;
-            uint4 qw[T][2];
-#pragma unroll
-            for (int tt = 0; tt < T; ++tt) {
-                qw[tt][0] = *reinterpret_cast<const uint4*>(st + rowbase + tt * 1024 + coff);
-                qw[tt][1] = *reinterpret_cast<const uint4*>(st + rowbase + tt * 1024 + 512 + coff);
-            }
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const uint32_t sb = pair * 2 + h;
-                const bool in = sb >= s_lo && sb < s_hi;  // sub-blocks outside the range add 0
-                uint32_t bf[NT][2];
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    uint2 v = make_uint2(0u, 0u);
-                    if (bact[nt] && in) v = __ldg(reinterpret_cast<const uint2*>(xbp + (sb * NT + nt) * 256));
-                    bf[nt][0] = v.x;
-                    bf[nt][1] = v.y;
-                }
-#pragma unroll
-                for (int tt = 0; tt < T; ++tt) {
-                    const uint32_t g0 = h ? qw[tt][0].z : qw[tt][0].x, s0 = h ? qw[tt][0].w : qw[tt][0].y;
-                    const uint32_t g1 = h ? qw[tt][1].z : qw[tt][1].x, s1 = h ? qw[tt][1].w : qw[tt][1].y;
-                    uint32_t a0, a1, a2, a3;
-                    decode_group(lut, g0, s0, selg, laneoff, rot, soff, a0, a2);
-                    decode_group(lut, g1, s1, selg, laneoff, rot, soff, a1, a3);
-                    const int c0 = (int)((s0 >> 27) | 1u), c1 = (int)((s1 >> 27) | 1u);
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        int d[4];
-                        mma_s8_16832(d, a0, a1, a2, a3, bf[nt][0], bf[nt][1]);
-                        I[tt][nt][0] += c0 * d[0];
-                        I[tt][nt][1] += c0 * d[1];
-                        I[tt][nt][2] += c1 * d[2];
-                        I[tt][nt][3] += c1 * d[3];
-                    }
-                }
-            }
-        }
+        if (s_lo == 0 && s_hi == 8)
+            stage_compute<NT, false>(dk, st_s, xbp, bact, s_lo, s_hi, rowbase, swz, I);
+        else
+            stage_compute<NT, true>(dk, st_s, xbp, bact, s_lo, s_hi, rowbase, swz, I);
+
         // Block epilogue: s32 -> f32 with d (per row) and the limb scale (per column).
         {
             float2 cs[NT];
@@ -389,8 +429,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
 #pragma unroll
             for (int tt = 0; tt < T; ++tt) {
                 const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
-                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(st + STAGE_QS + r0 * 4);
-                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(st + STAGE_QS + r1 * 4);
+                const uint32_t w0 = ld_shared_u32_volatile(st_s + STAGE_QS + r0 * 4);
+                const uint32_t w1 = ld_shared_u32_volatile(st_s + STAGE_QS + r1 * 4);
                 const uint32_t o0 = ((row0 + r0) * P.nb + cc.blk) & 1u, o1 = ((row0 + r1) * P.nb + cc.blk) & 1u;
                 const float d0 = half_bits_to_float(o0 ? (w0 >> 16) : w0);
                 const float d1 = half_bits_to_float(o1 ? (w1 >> 16) : w1);
@@ -403,8 +443,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 }
             }
         }
+        (void)st;
 
-        const uint32_t p = cc.p, rg = cc.rg;
+        const uint32_t rg = cc.rg;
         const bool rg_done = (cc.blk + 1 == P.nb) || (cc.tb + 1 == tb1);
         cursor_next(L, cc);
         __syncwarp();
@@ -464,7 +505,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 if (lane == 0) L.counters[P.counter_base + rg] = 0u;
             }
         }
-        (void)p;
     }
     cp_async_wait<0>();
     pdl_launch_dependents();
@@ -587,12 +627,12 @@ GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, i
     return pl;
 }
 
-template <int NT>
-cudaError_t launch_group_nt(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
-                            uint8_t* ws, const GroupPlan& pl, cudaStream_t stream) {
+template <int NT, int CAP>
+cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
+                             uint8_t* ws, const GroupPlan& pl, cudaStream_t stream) {
     using S_ = GemvShape<NT>;
     // ---- prep launch (unique x's) ----
-    PrepLaunch pre;
+    PrepLaunch<CAP> pre;
     pre.count = (uint32_t)pl.xs.size();
     pre.M = m;
     pre.counters = reinterpret_cast<uint32_t*>(ws + pl.off_counters);
@@ -622,9 +662,9 @@ cudaError_t launch_group_nt(const GemvProblemHost* probs, uint32_t count, uint32
     cfg.numAttrs = 1;
     cudaError_t e;
     switch (x_dtype) {
-        case 0: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<float, NT>, pre); break;
-        case 1: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__half, NT>, pre); break;
-        default: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__nv_bfloat16, NT>, pre); break;
+        case 0: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<float, NT, CAP>, pre); break;
+        case 1: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__half, NT, CAP>, pre); break;
+        default: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__nv_bfloat16, NT, CAP>, pre); break;
     }
     if (e != cudaSuccess) return e;
 
@@ -633,11 +673,11 @@ cudaError_t launch_group_nt(const GemvProblemHost* probs, uint32_t count, uint32
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemv_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, S_::SMEM);
+        e = cudaFuncSetAttribute(gemv_kernel<NT, CAP>, cudaFuncAttributeMaxDynamicSharedMemorySize, S_::SMEM);
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set[dev] = true;
     }
-    GemvLaunch L;
+    GemvLaunch<CAP> L;
     L.count = count;
     L.M = m;
     L.total_steps = pl.total_steps;
@@ -664,9 +704,18 @@ cudaError_t launch_group_nt(const GemvProblemHost* probs, uint32_t count, uint32
     cfg.gridDim = dim3(pl.grid);
     cfg.blockDim = dim3(GEMV_WARPS * 32);
     cfg.dynamicSmemBytes = S_::SMEM;
-    e = cudaLaunchKernelEx(&cfg, gemv_kernel<NT>, L);
+    e = cudaLaunchKernelEx(&cfg, gemv_kernel<NT, CAP>, L);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
+}
+
+template <int NT>
+cudaError_t launch_group_nt(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
+                            uint8_t* ws, const GroupPlan& pl, cudaStream_t stream) {
+    // parameter capacity: a single projection ships ~100 bytes of launch parameters, not 16 KB
+    if (count <= 1) return launch_group_cap<NT, 1>(probs, count, m, x_dtype, ws, pl, stream);
+    if (count <= 16) return launch_group_cap<NT, 16>(probs, count, m, x_dtype, ws, pl, stream);
+    return launch_group_cap<NT, MAX_PROBLEMS>(probs, count, m, x_dtype, ws, pl, stream);
 }
 
 }  // namespace
