@@ -1,20 +1,451 @@
-// IQ2_XXS prefill GEMM (m > 16) on the sm_100a tensor cores. Until the tcgen05 kernel is in
-// place, m > 16 is served by the generic GEMV kernel (gemm_path_ok returns false).
+// IQ2_XXS prefill GEMM (m > 16) on the sm_100a tensor cores: tcgen05.mma with TMEM accumulators.
+//
+// out[m, n] = sum_k x[m, k] * W[n, k] (reference: iq2_xxs_matmul_kernel,
+// src/metal_src/iq2_matmul.metal:188-240, which recomputes the weights per output element) as a
+// dense bf16 x bf16 -> f32 contraction:
+//   * A = x, bf16 [M, K] (f32/f16 x is first narrowed to bf16 into the workspace), loaded by TMA
+//     as 128-row x 64-k boxes with the 128-byte swizzle;
+//   * B = W, dequantised to bf16 in shared memory by 8 decode warps, directly in the canonical
+//     SW128 K-major layout the MMA reads. Each weight is bf16(d*(2s+1)/8 * g) for g in {8,25,43}:
+//     the three products of a 32-weight sub-block are rounded once and a `prmt` picks the bf16
+//     pairs by grid code (IQ2XXS_BF16_SEL), an XOR applies the signs (IQ2_SIGN_PAIR_MASK). This
+//     is bit-identical to rounding every weight's exact f32 value (the dequant kernel's bf16).
+//   * D: two 128 x 256 f32 accumulators in TMEM (all 512 columns): one CTA computes a tile of 256
+//     tokens x 256 weight rows, issuing per 64-k stage 2 x 4 tcgen05.mma (M=128, N=256, K=16)
+//     from one thread; tcgen05.commit frees each stage when the tensor core has read it.
+//   * Pipeline: 3 stages of 64 KB, mbarriers for "x landed" (TMA transaction bytes), "weights
+//     written" (decode warps) and "stage free" (MMA commit). Every wait is bounded: on timeout
+//     the kernel records an error code, stops issuing work and still frees its TMEM.
+// No TMA multicast is used anywhere (this library also runs on multi-GPU jobs).
 #include "iq2xxs_common.cuh"
+#include "iq2xxs_codebook.h"
 #include "iq2xxs_internal.h"
+
+#include <cuda.h>
+
+#include <algorithm>
 
 namespace iq2 {
 
-bool gemm_path_ok(uint32_t, uint32_t, uint32_t, const void*, int, const uint8_t*, const uint8_t*,
-                  const float*) {
-    return false;
+namespace {
+
+constexpr int G_BM = 256;                       // tokens per CTA (two M=128 MMAs)
+constexpr int G_BN = 256;                       // weight rows per CTA (MMA N)
+constexpr int G_BK = 64;                        // k per stage (one 128-byte swizzle row of bf16)
+constexpr int G_STAGES = 3;
+constexpr int G_DEC_WARPS = 8;                  // decode warps = epilogue warps
+constexpr int G_TMA_WARP = G_DEC_WARPS;         // warp 8
+constexpr int G_MMA_WARP = G_DEC_WARPS + 1;     // warp 9
+constexpr int G_THREADS = (G_DEC_WARPS + 2) * 32;
+constexpr int G_A_HALF = 128 * G_BK * 2;        // 16 KB: one 128-token box
+constexpr int G_A_BYTES = 2 * G_A_HALF;         // 32 KB
+constexpr int G_B_BYTES = G_BN * G_BK * 2;      // 32 KB
+constexpr int G_STAGE_BYTES = G_A_BYTES + G_B_BYTES;
+constexpr int G_SEL_BYTES = 256 * 16 + 128 * 16;  // decode tables
+constexpr int G_SMEM = 1024 /*align*/ + G_STAGES * G_STAGE_BYTES + G_SEL_BYTES + 256 /*barriers*/;
+constexpr uint32_t G_TMEM_COLS = 512;
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: only a broken pipeline waits that long
+
+// Instruction descriptor, kind::f16: F32 accumulate, BF16 A and B, both K-major, M=128, N=256.
+constexpr uint32_t G_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(G_BN >> 3) << 17) |
+                             ((uint32_t)(128 >> 4) << 24);
+
+struct GemmParams {
+    const uint8_t* qs;
+    const uint8_t* sc;
+    float* out;
+    uint32_t* err;  // error word (0 = ok); set on a pipeline timeout
+    uint32_t M, N, K, nb;
+};
+
+// ---- mbarrier / tcgen05 / TMA wrappers (inline PTX) ----
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+                 "r"(bytes)
+                 : "memory");
+}
+// One test of the phase; a thread may be suspended for at most ~10 us (the hint) inside it.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(10000u)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: false (and the error code recorded) if the phase does not complete within
+// WAIT_LIMIT_NS of wall time.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* err, uint32_t code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > WAIT_LIMIT_NS) {
+            atomicOr(err, code);
+            return false;
+        }
+    }
 }
 
-size_t gemm_workspace_size(uint32_t, uint32_t, uint32_t, int) { return 0; }
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
-cudaError_t launch_gemm(const void*, int, uint32_t, const uint8_t*, const uint8_t*, uint32_t, uint32_t,
-                        float*, void*, int, cudaStream_t) {
-    return cudaErrorNotSupported;
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            dst),
+        "l"(map), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// SW128 K-major shared-memory matrix descriptor: start address, LBO = 16 B (unused for swizzled
+// K-major), SBO = 1024 B between 8-row groups, version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---- the kernel ----
+__global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                            const GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_s = smem_u32(smem_raw);
+    const uint32_t base_s = (raw_s + 1023u) & ~1023u;  // SW128 tiles need 1024-byte alignment
+    uint8_t* base = smem_raw + (base_s - raw_s);
+    const uint32_t sel_s = base_s + G_STAGES * G_STAGE_BYTES;
+    const uint32_t sgn_s = sel_s + 256 * 16;
+    const uint32_t bar_s = sgn_s + 128 * 16;
+    // barriers: full_a[S], full_b[S], empty[S], acc_full; then the TMEM address word; abort flag
+    auto full_a = [&](int s) { return bar_s + 8u * s; };
+    auto full_b = [&](int s) { return bar_s + 8u * (G_STAGES + s); };
+    auto empty = [&](int s) { return bar_s + 8u * (2 * G_STAGES + s); };
+    const uint32_t acc_full = bar_s + 8u * (3 * G_STAGES);
+    uint32_t* tmem_addr_word = reinterpret_cast<uint32_t*>(base + (bar_s - base_s) + 8 * (3 * G_STAGES + 1));
+    volatile uint32_t* abort_flag = tmem_addr_word + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t n0 = blockIdx.x * G_BN, m0 = blockIdx.y * G_BM;
+    const uint32_t KT = (p.K + G_BK - 1) / G_BK;
+
+    // decode tables -> shared memory
+    for (int i = threadIdx.x; i < 256 * 4; i += blockDim.x)
+        reinterpret_cast<uint32_t*>(base + (sel_s - base_s))[i] = (&IQ2XXS_BF16_SEL[0][0])[i];
+    for (int i = threadIdx.x; i < 128 * 4; i += blockDim.x)
+        reinterpret_cast<uint32_t*>(base + (sgn_s - base_s))[i] = (&IQ2_SIGN_PAIR_MASK[0][0])[i];
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < G_STAGES; ++s) {
+            mbar_init(full_a(s), 1);
+            mbar_init(full_b(s), G_DEC_WARPS);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(acc_full, 1);
+        *abort_flag = 0u;
+        fence_barrier_init();
+    }
+    if (warp == G_MMA_WARP) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_addr_word)),
+                     "r"(G_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_addr_word;
+
+    if (warp == G_TMA_WARP) {
+        // ---------------- x producer ----------------
+        if (lane == 0) {
+            for (uint32_t kt = 0; kt < KT; ++kt) {
+                const int s = kt % G_STAGES;
+                if (kt >= G_STAGES && !mbar_wait(empty(s), ((kt / G_STAGES) - 1) & 1, p.err, 1u)) {
+                    *abort_flag = 1u;
+                    break;
+                }
+                if (*abort_flag) break;
+                const uint32_t a_s = base_s + s * G_STAGE_BYTES;
+                mbar_expect_tx(full_a(s), G_A_BYTES);
+                tma_load_2d(a_s, &tmap_x, full_a(s), (int)(kt * G_BK), (int)m0);
+                tma_load_2d(a_s + G_A_HALF, &tmap_x, full_a(s), (int)(kt * G_BK), (int)(m0 + 128));
+            }
+        }
+    } else if (warp == G_MMA_WARP) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            bool ok = true;
+            for (uint32_t kt = 0; kt < KT && ok; ++kt) {
+                const int s = kt % G_STAGES;
+                const uint32_t ph = (kt / G_STAGES) & 1;
+                ok = mbar_wait(full_a(s), ph, p.err, 2u) && mbar_wait(full_b(s), ph, p.err, 4u);
+                if (!ok || *abort_flag) {
+                    *abort_flag = 1u;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_s = base_s + s * G_STAGE_BYTES, b_s = a_s + G_A_BYTES;
+#pragma unroll
+                for (int ks = 0; ks < G_BK / 16; ++ks) {
+                    const uint64_t bd = sw128_desc(b_s + ks * 32);
+                    const uint32_t acc = (kt | ks) ? 1u : 0u;
+                    tc_mma(tmem, sw128_desc(a_s + ks * 32), bd, G_IDESC, acc);
+                    tc_mma(tmem + 256, sw128_desc(a_s + G_A_HALF + ks * 32), bd, G_IDESC, acc);
+                }
+                tc_commit(empty(s));  // the stage is free once these MMAs have read it
+            }
+            tc_commit(acc_full);      // fires when every MMA issued above has completed
+        }
+    } else {
+        // ---------------- weight decode (warps 0..7), then epilogue ----------------
+        const uint32_t r = threadIdx.x;  // tile row 0..255
+        const uint32_t row = n0 + r;
+        const bool rok = row < p.N;
+        const uint8_t* qrow = p.qs + (size_t)(rok ? row : 0) * p.nb * QS_BYTES;
+        const uint8_t* srow = p.sc + (size_t)(rok ? row : 0) * p.nb * SC_BYTES;
+        const uint32_t row_swz = r & 7u;
+        const uint32_t row_off = (r >> 3) * 1024u + (r & 7u) * 128u;
+        uint4 qn = rok ? __ldg(reinterpret_cast<const uint4*>(qrow)) : make_uint4(0, 0, 0, 0);
+        uint32_t dbits = rok ? (uint32_t)srow[0] | ((uint32_t)srow[1] << 8) : 0u;
+        for (uint32_t kt = 0; kt < KT; ++kt) {
+            const int s = kt % G_STAGES;
+            const uint4 q = qn;
+            const uint32_t blk = kt >> 2;
+            if ((kt & 3) == 0 && kt > 0)
+                dbits = rok ? (uint32_t)srow[blk * 2] | ((uint32_t)srow[blk * 2 + 1] << 8) : 0u;
+            if (kt + 1 < KT && rok) qn = __ldg(reinterpret_cast<const uint4*>(qrow + (kt + 1) * 16));
+            if (kt >= G_STAGES) {
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(empty(s), ((kt / G_STAGES) - 1) & 1, p.err, 8u);
+                ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
+                if (!ok) *abort_flag = 1u;
+            }
+            if (*abort_flag) break;
+            const float d = half_bits_to_float(dbits);
+            uint8_t* bt = base + s * G_STAGE_BYTES + G_A_BYTES + row_off;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {  // the stage's two 32-weight sub-blocks
+                const uint32_t aux_g = h ? q.z : q.x, aux_s = h ? q.w : q.y;
+                const float dl = d * (float)((aux_s >> 27) | 1u) * 0.125f;  // d*(2s+1)/8, exact
+                const uint32_t qlo = cvt_bf16x2(dl * 8.0f, dl * 25.0f);     // {bf16(8dl), bf16(25dl)}
+                const uint32_t qhi = cvt_bf16x2(dl * 43.0f, 0.0f);          // {bf16(43dl), 0}
+                const uint32_t k_lo = kt * G_BK + h * 32;                  // first k of the sub-block
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const uint32_t gi = (aux_g >> (8 * t)) & 0xFFu, si = (aux_s >> (7 * t)) & 0x7Fu;
+                    const uint4 sel = *reinterpret_cast<const uint4*>(base + (sel_s - base_s) + gi * 16);
+                    const uint4 sm = *reinterpret_cast<const uint4*>(base + (sgn_s - base_s) + si * 16);
+                    uint4 w;
+                    w.x = prmt(qlo, qhi, sel.x) ^ sm.x;
+                    w.y = prmt(qlo, qhi, sel.y) ^ sm.y;
+                    w.z = prmt(qlo, qhi, sel.z) ^ sm.z;
+                    w.w = prmt(qlo, qhi, sel.w) ^ sm.w;
+                    if (k_lo + t * 8 + 8 > p.K) {  // the K tail: weights past in_dim contribute 0
+                        const uint32_t k0 = k_lo + t * 8;
+                        const uint32_t keep = k0 >= p.K ? 0u : p.K - k0;  // 0..7 weights kept
+                        w.x = keep >= 2 ? w.x : (keep == 1 ? (w.x & 0xFFFFu) : 0u);
+                        w.y = keep >= 4 ? w.y : (keep == 3 ? (w.y & 0xFFFFu) : 0u);
+                        w.z = keep >= 6 ? w.z : (keep == 5 ? (w.z & 0xFFFFu) : 0u);
+                        w.w = keep >= 8 ? w.w : (keep == 7 ? (w.w & 0xFFFFu) : 0u);
+                    }
+                    const uint32_t chunk = (uint32_t)(h * 4 + t);  // 16-byte chunk along k
+                    *reinterpret_cast<uint4*>(bt + ((chunk ^ row_swz) << 4)) = w;
+                }
+            }
+            fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full_b(s));
+        }
+
+        // ---------------- epilogue: TMEM -> registers -> global ----------------
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(acc_full, 0, p.err, 16u);
+        ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
+        if (ok && !*abort_flag) {
+            tc_fence_after();
+            const uint32_t acc = warp >> 2, quad = warp & 3;  // accumulator, TMEM lane quadrant
+            const uint32_t token = m0 + acc * 128 + quad * 32 + lane;
+            float* orow = p.out + (size_t)token * p.N;
+            const bool vec = (p.N % 4) == 0;
+#pragma unroll 1
+            for (int c = 0; c < G_BN / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((quad * 32u) << 16) + acc * 256u + c * 32u, v);
+                if (token < p.M) {
+                    const uint32_t nc = n0 + c * 32;
+                    if (vec && nc + 32 <= p.N) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(orow + nc + j) =
+                                make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                            __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (nc + j < p.N) orow[nc + j] = __uint_as_float(v[j]);
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == G_MMA_WARP) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G_TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// x (f32 / f16) -> bf16, row-major [M, K] (round to nearest even).
+template <typename XT>
+__global__ void __launch_bounds__(256) to_bf16_kernel(const XT* __restrict__ x, __nv_bfloat16* __restrict__ y,
+                                                      size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = __float2bfloat16_rn(to_f32(x[i]));
+}
+
+// Driver entry point for cuTensorMapEncodeTiled (no link-time dependency on libcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+}  // namespace
+
+bool gemm_path_ok(uint32_t m, uint32_t n, uint32_t k, const void* x, int x_dtype, const uint8_t* qs,
+                  const uint8_t* sc, const float* out) {
+    (void)sc;
+    (void)out;
+    (void)n;
+    (void)x_dtype;
+    // TMA rows must be 16-byte aligned: bf16 x (or its bf16 copy) needs k % 8 == 0
+    return m > 16 && k % 8 == 0 && (x_dtype != kDtypeBf16 || reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+           reinterpret_cast<uintptr_t>(qs) % 16 == 0 && encode_fn() != nullptr;
+}
+
+size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype) {
+    (void)n;
+    size_t ws = 256;  // error word
+    if (x_dtype != kDtypeBf16) ws += align256((size_t)m * k * 2);
+    return ws;
+}
+
+cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc, uint32_t n,
+                        uint32_t k, float* out, void* workspace, int num_sms, cudaStream_t stream) {
+    (void)num_sms;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    uint32_t* err = reinterpret_cast<uint32_t*>(ws);
+    cudaError_t e = cudaMemsetAsync(err, 0, 4, stream);
+    if (e != cudaSuccess) return e;
+    const void* xb = x;
+    if (x_dtype != kDtypeBf16) {
+        __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(ws + 256);
+        const size_t total = (size_t)m * k;
+        const unsigned blocks = (unsigned)std::min<size_t>((total + 255) / 256, 148 * 16);
+        if (x_dtype == 0) to_bf16_kernel<float><<<blocks, 256, 0, stream>>>(static_cast<const float*>(x), y, total);
+        else to_bf16_kernel<__half><<<blocks, 256, 0, stream>>>(static_cast<const __half*>(x), y, total);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        xb = y;
+    }
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {k, m};
+    const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+    const cuuint32_t box[2] = {G_BK, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(xb), dims, strides, box,
+                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !attr_set[dev]) {
+        e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) attr_set[dev] = true;
+    }
+    GemmParams p;
+    p.qs = qs;
+    p.sc = sc;
+    p.out = out;
+    p.err = err;
+    p.M = m;
+    p.N = n;
+    p.K = k;
+    p.nb = (k + QK - 1) / QK;
+    dim3 grid((n + G_BN - 1) / G_BN, (m + G_BM - 1) / G_BM);
+    gemm_kernel<<<grid, G_THREADS, G_SMEM, stream>>>(map, p);
+    return cudaGetLastError();
 }
 
 }  // namespace iq2

@@ -7,6 +7,8 @@
 
 namespace iq2 {
 
+constexpr int kDtypeBf16 = 2;  // IQ2_DTYPE_BF16 of the C ABI
+
 // Decode GEMV (iq2xxs_gemv.cu), m <= 16. A group is up to gemv_max_group() projections with
 // the same m and x dtype, computed by one prep launch and one GEMV launch.
 struct GemvProblemHost {

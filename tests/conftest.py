@@ -44,9 +44,9 @@ def parse_codebook():
     """The product's generated codebook header, parsed back into Python lists."""
     text = CODEBOOK.read_text()
     tables = {}
-    for m in re.finditer(r"(\w+)\s+(\w+)\[(\d+)\]\s*=\s*\{(.*?)\};", text, re.S):
+    for m in re.finditer(r"(\w+)\s+(\w+)((?:\[\d+\])+)\s*=\s*\{(.*?)\};", text, re.S):
         vals = [int(v, 0) for v in re.findall(r"0x[0-9a-fA-F]+|\d+", m.group(4).replace("ull", "").replace("u", ""))]
-        tables[m.group(2)] = vals
+        tables[m.group(2)] = vals  # multi-dimensional tables come back flattened
     return tables
 
 

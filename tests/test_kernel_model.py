@@ -125,3 +125,38 @@ def test_gemv_model_worst_case_magnitudes_fit_s32(oracle):
     y_model = model_gemv(x, qs, sc, n, k, cb)
     y_ref = oracle.matmul(x, qs, sc, n, k)
     assert rel_l2(y_model, y_ref) < 1e-6
+
+
+def _bf16_bits(v: np.ndarray) -> np.ndarray:
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32)).to(torch.bfloat16).view(torch.int16).numpy() \
+        .view(np.uint16)
+
+
+def test_gemm_bf16_decode_tables_match_rounded_dequant(oracle):
+    """The GEMM's weight decode (csrc/iq2xxs_gemm.cu): per sub-block the bf16 roundings of
+    dl*{8,25,43}, a prmt by IQ2XXS_BF16_SEL and an XOR by IQ2_SIGN_PAIR_MASK, must equal the bf16
+    rounding of every exact weight (the oracle's f32 dequant)."""
+    cb = parse_codebook()
+    sel, smask = cb["IQ2XXS_BF16_SEL"], cb["IQ2_SIGN_PAIR_MASK"]
+    n, k = 12, 768
+    qs, sc = synth.iq2xxs_weights(n, k, seed=21)
+    qs, sc = qs.numpy(), sc.numpy()
+    want = oracle.dequantize(qs, sc, n, k, "bf16")
+    d = sc.view(np.float16).astype(np.float32).reshape(n, k // 256)
+    words = qs.reshape(n, k // 32, 8)
+    got = np.zeros((n, k), dtype=np.uint16)
+    for r in range(n):
+        for sb in range(k // 32):
+            aux_g = int.from_bytes(bytes(words[r, sb, :4]), "little")
+            aux_s = int.from_bytes(bytes(words[r, sb, 4:]), "little")
+            dl = np.float32(d[r, sb // 8]) * np.float32((aux_s >> 27) | 1) * np.float32(0.125)
+            b8, b25, b43 = _bf16_bits(np.array([dl * 8, dl * 25, dl * 43], dtype=np.float32))
+            qlo, qhi = int(b8) | (int(b25) << 16), int(b43)
+            for t in range(4):
+                gi, si = (aux_g >> (8 * t)) & 0xFF, (aux_s >> (7 * t)) & 0x7F
+                for i in range(4):
+                    w = prmt(qlo, qhi, sel[gi * 4 + i]) ^ smask[si * 4 + i]
+                    col = sb * 32 + t * 8 + 2 * i
+                    got[r, col], got[r, col + 1] = w & 0xFFFF, w >> 16
+    assert np.array_equal(got, want)
