@@ -8,8 +8,10 @@
 //   * B = W, dequantised to bf16 in shared memory by 8 decode warps, directly in the canonical
 //     SW128 K-major layout the MMA reads. Each weight is bf16(d*(2s+1)/8 * g) for g in {8,25,43}:
 //     the three products of a 32-weight sub-block are rounded once and a `prmt` picks the bf16
-//     pairs by grid code (IQ2XXS_BF16_SEL), an XOR applies the signs (IQ2_SIGN_PAIR_MASK). This
-//     is bit-identical to rounding every weight's exact f32 value (the dequant kernel's bf16).
+//     pairs by grid code (IQ2XXS_BF16_SEL), an XOR applies the signs (the sign byte spread to the
+//     bf16 sign bits by one multiply). This is bit-identical to rounding every weight's exact f32
+//     value (the dequant kernel's bf16). Tables are kept small (2 KB + 128 B) because the tensor
+//     core reads its operands through the same shared memory.
 //   * D: two 128 x 256 f32 accumulators in TMEM (all 512 columns): one CTA computes a tile of 256
 //     tokens x 256 weight rows, issuing per 64-k stage 2 x 4 tcgen05.mma (M=128, N=256, K=16)
 //     from one thread; tcgen05.commit frees each stage when the tensor core has read it.
@@ -33,15 +35,15 @@ constexpr int G_BM = 256;                       // tokens per CTA (two M=128 MMA
 constexpr int G_BN = 256;                       // weight rows per CTA (MMA N)
 constexpr int G_BK = 64;                        // k per stage (one 128-byte swizzle row of bf16)
 constexpr int G_STAGES = 3;
-constexpr int G_DEC_WARPS = 8;                  // decode warps = epilogue warps
-constexpr int G_TMA_WARP = G_DEC_WARPS;         // warp 8
-constexpr int G_MMA_WARP = G_DEC_WARPS + 1;     // warp 9
+constexpr int G_DEC_WARPS = 16;                 // decode warps = epilogue warps
+constexpr int G_TMA_WARP = G_DEC_WARPS;         // warp 16
+constexpr int G_MMA_WARP = G_DEC_WARPS + 1;     // warp 17
 constexpr int G_THREADS = (G_DEC_WARPS + 2) * 32;
 constexpr int G_A_HALF = 128 * G_BK * 2;        // 16 KB: one 128-token box
 constexpr int G_A_BYTES = 2 * G_A_HALF;         // 32 KB
 constexpr int G_B_BYTES = G_BN * G_BK * 2;      // 32 KB
 constexpr int G_STAGE_BYTES = G_A_BYTES + G_B_BYTES;
-constexpr int G_SEL_BYTES = 256 * 16 + 128 * 16;  // decode tables
+constexpr int G_SEL_BYTES = 256 * 8 + 128;      // decode tables: selector pairs, sign bytes
 constexpr int G_SMEM = 1024 /*align*/ + G_STAGES * G_STAGE_BYTES + G_SEL_BYTES + 256 /*barriers*/;
 constexpr uint32_t G_TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: only a broken pipeline waits that long
@@ -169,8 +171,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
     const uint32_t base_s = (raw_s + 1023u) & ~1023u;  // SW128 tiles need 1024-byte alignment
     uint8_t* base = smem_raw + (base_s - raw_s);
     const uint32_t sel_s = base_s + G_STAGES * G_STAGE_BYTES;
-    const uint32_t sgn_s = sel_s + 256 * 16;
-    const uint32_t bar_s = sgn_s + 128 * 16;
+    const uint32_t sgn_s = sel_s + 256 * 8;
+    const uint32_t bar_s = sgn_s + 128;
     // barriers: full_a[S], full_b[S], empty[S], acc_full; then the TMEM address word; abort flag
     auto full_a = [&](int s) { return bar_s + 8u * s; };
     auto full_b = [&](int s) { return bar_s + 8u * (G_STAGES + s); };
@@ -183,11 +185,13 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
     const uint32_t n0 = blockIdx.x * G_BN, m0 = blockIdx.y * G_BM;
     const uint32_t KT = (p.K + G_BK - 1) / G_BK;
 
-    // decode tables -> shared memory
-    for (int i = threadIdx.x; i < 256 * 4; i += blockDim.x)
-        reinterpret_cast<uint32_t*>(base + (sel_s - base_s))[i] = (&IQ2XXS_BF16_SEL[0][0])[i];
-    for (int i = threadIdx.x; i < 128 * 4; i += blockDim.x)
-        reinterpret_cast<uint32_t*>(base + (sgn_s - base_s))[i] = (&IQ2_SIGN_PAIR_MASK[0][0])[i];
+    // decode tables -> shared memory: per grid entry the four 16-bit prmt selectors packed in two
+    // words, and the 8-bit sign masks (ksigns)
+    for (int i = threadIdx.x; i < 256 * 2; i += blockDim.x) {
+        const uint32_t* e = IQ2XXS_BF16_SEL[i >> 1];
+        reinterpret_cast<uint32_t*>(base + (sel_s - base_s))[i] = (i & 1) ? (e[2] | (e[3] << 16)) : (e[0] | (e[1] << 16));
+    }
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) base[(sgn_s - base_s) + i] = IQ2_KSIGNS[i];
     if (threadIdx.x == 0) {
         for (int s = 0; s < G_STAGES; ++s) {
             mbar_init(full_a(s), 1);
@@ -252,23 +256,24 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
             tc_commit(acc_full);      // fires when every MMA issued above has completed
         }
     } else {
-        // ---------------- weight decode (warps 0..7), then epilogue ----------------
-        const uint32_t r = threadIdx.x;  // tile row 0..255
+        // ---------------- weight decode (warps 0..15), then epilogue ----------------
+        // thread = (tile row r, sub-block h of the stage's two)
+        const uint32_t r = threadIdx.x & 255u, hh = threadIdx.x >> 8;
         const uint32_t row = n0 + r;
         const bool rok = row < p.N;
         const uint8_t* qrow = p.qs + (size_t)(rok ? row : 0) * p.nb * QS_BYTES;
         const uint8_t* srow = p.sc + (size_t)(rok ? row : 0) * p.nb * SC_BYTES;
         const uint32_t row_swz = r & 7u;
         const uint32_t row_off = (r >> 3) * 1024u + (r & 7u) * 128u;
-        uint4 qn = rok ? __ldg(reinterpret_cast<const uint4*>(qrow)) : make_uint4(0, 0, 0, 0);
+        uint2 qn = rok ? __ldg(reinterpret_cast<const uint2*>(qrow + hh * 8)) : make_uint2(0, 0);
         uint32_t dbits = rok ? (uint32_t)srow[0] | ((uint32_t)srow[1] << 8) : 0u;
         for (uint32_t kt = 0; kt < KT; ++kt) {
             const int s = kt % G_STAGES;
-            const uint4 q = qn;
+            const uint2 q = qn;
             const uint32_t blk = kt >> 2;
             if ((kt & 3) == 0 && kt > 0)
                 dbits = rok ? (uint32_t)srow[blk * 2] | ((uint32_t)srow[blk * 2 + 1] << 8) : 0u;
-            if (kt + 1 < KT && rok) qn = __ldg(reinterpret_cast<const uint4*>(qrow + (kt + 1) * 16));
+            if (kt + 1 < KT && rok) qn = __ldg(reinterpret_cast<const uint2*>(qrow + (kt + 1) * 16 + hh * 8));
             if (kt >= G_STAGES) {
                 bool ok = true;
                 if (lane == 0) ok = mbar_wait(empty(s), ((kt / G_STAGES) - 1) & 1, p.err, 8u);
@@ -278,9 +283,9 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
             if (*abort_flag) break;
             const float d = half_bits_to_float(dbits);
             uint8_t* bt = base + s * G_STAGE_BYTES + G_A_BYTES + row_off;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {  // the stage's two 32-weight sub-blocks
-                const uint32_t aux_g = h ? q.z : q.x, aux_s = h ? q.w : q.y;
+            {  // this thread's 32-weight sub-block of the stage
+                const uint32_t h = hh;
+                const uint32_t aux_g = q.x, aux_s = q.y;
                 const float dl = d * (float)((aux_s >> 27) | 1u) * 0.125f;  // d*(2s+1)/8, exact
                 const uint32_t qlo = cvt_bf16x2(dl * 8.0f, dl * 25.0f);     // {bf16(8dl), bf16(25dl)}
                 const uint32_t qhi = cvt_bf16x2(dl * 43.0f, 0.0f);          // {bf16(43dl), 0}
@@ -288,13 +293,15 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
                     const uint32_t gi = (aux_g >> (8 * t)) & 0xFFu, si = (aux_s >> (7 * t)) & 0x7Fu;
-                    const uint4 sel = *reinterpret_cast<const uint4*>(base + (sel_s - base_s) + gi * 16);
-                    const uint4 sm = *reinterpret_cast<const uint4*>(base + (sgn_s - base_s) + si * 16);
+                    const uint2 sel = *reinterpret_cast<const uint2*>(base + (sel_s - base_s) + gi * 8);
+                    const uint32_t S = base[(sgn_s - base_s) + si];  // bit j: weight j negative
+                    // (S * K_i) & 0x80008000 puts sign bits 2i and 2i+1 at bits 15 and 31 (the two
+                    // bf16 sign bits of pair i): the shifted copies of S never overlap, no carries.
                     uint4 w;
-                    w.x = prmt(qlo, qhi, sel.x) ^ sm.x;
-                    w.y = prmt(qlo, qhi, sel.y) ^ sm.y;
-                    w.z = prmt(qlo, qhi, sel.z) ^ sm.z;
-                    w.w = prmt(qlo, qhi, sel.w) ^ sm.w;
+                    w.x = prmt(qlo, qhi, sel.x) ^ ((S * 0x40008000u) & 0x80008000u);
+                    w.y = prmt(qlo, qhi, sel.x >> 16) ^ ((S * 0x10002000u) & 0x80008000u);
+                    w.z = prmt(qlo, qhi, sel.y) ^ ((S * 0x04000800u) & 0x80008000u);
+                    w.w = prmt(qlo, qhi, sel.y >> 16) ^ ((S * 0x01000200u) & 0x80008000u);
                     if (k_lo + t * 8 + 8 > p.K) {  // the K tail: weights past in_dim contribute 0
                         const uint32_t k0 = k_lo + t * 8;
                         const uint32_t keep = k0 >= p.K ? 0u : p.K - k0;  // 0..7 weights kept
@@ -318,12 +325,13 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
         ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
         if (ok && !*abort_flag) {
             tc_fence_after();
-            const uint32_t acc = warp >> 2, quad = warp & 3;  // accumulator, TMEM lane quadrant
+            // accumulator, TMEM lane quadrant (fixed by the warp's rank in its group of 4), column half
+            const uint32_t acc = (warp >> 2) & 1, quad = warp & 3, chalf = warp >> 3;
             const uint32_t token = m0 + acc * 128 + quad * 32 + lane;
             float* orow = p.out + (size_t)token * p.N;
             const bool vec = (p.N % 4) == 0;
 #pragma unroll 1
-            for (int c = 0; c < G_BN / 32; ++c) {
+            for (int c = chalf * (G_BN / 64); c < (chalf + 1) * (G_BN / 64); ++c) {
                 uint32_t v[32];
                 tmem_ld32(tmem + ((quad * 32u) << 16) + acc * 256u + c * 32u, v);
                 if (token < p.M) {

@@ -135,10 +135,15 @@ def _bf16_bits(v: np.ndarray) -> np.ndarray:
 
 def test_gemm_bf16_decode_tables_match_rounded_dequant(oracle):
     """The GEMM's weight decode (csrc/iq2xxs_gemm.cu): per sub-block the bf16 roundings of
-    dl*{8,25,43}, a prmt by IQ2XXS_BF16_SEL and an XOR by IQ2_SIGN_PAIR_MASK, must equal the bf16
-    rounding of every exact weight (the oracle's f32 dequant)."""
+    dl*{8,25,43}, a prmt by IQ2XXS_BF16_SEL and an XOR by the sign byte spread with one multiply,
+    (S * K_i) & 0x80008000, must equal the bf16 rounding of every exact weight (the oracle's f32
+    dequant). The spread is also checked against the mask table IQ2_SIGN_PAIR_MASK."""
     cb = parse_codebook()
     sel, smask = cb["IQ2XXS_BF16_SEL"], cb["IQ2_SIGN_PAIR_MASK"]
+    K = [0x40008000, 0x10002000, 0x04000800, 0x01000200]
+    for si in range(128):
+        S = cb["IQ2_KSIGNS"][si]
+        assert [((S * K[i]) & 0xFFFFFFFF) & 0x80008000 for i in range(4)] == smask[si * 4:si * 4 + 4]
     n, k = 12, 768
     qs, sc = synth.iq2xxs_weights(n, k, seed=21)
     qs, sc = qs.numpy(), sc.numpy()
