@@ -18,7 +18,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libcandelora_iq2.so"
-SOURCES = ["iq2xxs_capi.cu", "iq2xxs_gemv.cu", "iq2xxs_gemm.cu", "iq2xxs_dequant.cu"]
+SOURCES = ["iq2xxs_capi.cu", "iq2xxs_gemv.cu", "iq2xxs_gemm.cu", "iq2xxs_dequant.cu", "iq2xxs_noalloc.cu"]
 HEADERS = ["iq2xxs_common.cuh", "iq2xxs_codebook.h", "iq2xxs_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -237,6 +237,49 @@ int grouped_impl(const iq2_matmul_problem* probs, uint32_t count, uint32_t m, in
 
 }  // namespace
 
+// Helpers shared with iq2xxs_noalloc.cu (declared in iq2xxs_internal.h).
+namespace iq2 {
+
+int capi_fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int capi_cuda_fail(const char* what, cudaError_t e) { return cuda_fail(what, e); }
+
+int capi_num_sms() { return num_sms_for_current_device(); }
+
+// The checks iq2_matmul makes before choosing a kernel (clears the thread's error message first).
+int capi_validate_matmul(const char* op, const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
+                         size_t weight_bytes_len, const uint8_t* weight_scales, size_t weight_scales_len,
+                         uint32_t out_dim, uint32_t in_dim, const float* out) {
+    g_last_error.clear();
+    int rc = check_args(op, out_dim, in_dim, IQ2_VARIANT_IQ2_XXS);
+    if (rc != IQ2_OK) return rc;
+    int dev = 0;
+    if ((rc = current_device(op, &dev)) != IQ2_OK) return rc;
+    if (m > 0 && x == nullptr) return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL x", op);
+    rc = check_weights(op, weight_bytes, weight_bytes_len, weight_scales, weight_scales_len, out_dim, in_dim,
+                       IQ2_VARIANT_IQ2_XXS, dev, m > 0 ? x : nullptr);
+    if (rc != IQ2_OK) return rc;
+    if (x_dtype < IQ2_DTYPE_F32 || x_dtype > IQ2_DTYPE_BF16)
+        return fail(IQ2_ERR_DTYPE, "%s unsupported x dtype: %d", op, x_dtype);
+    if (m == 0) return IQ2_OK;
+    if (out == nullptr) return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL out", op);
+    if (pointer_device(out) != dev) return fail(IQ2_ERR_DEVICE, "%s: out is not memory of Cuda(%d)", op, dev);
+    const size_t esize = x_dtype == IQ2_DTYPE_F32 ? 4 : 2;
+    if (reinterpret_cast<uintptr_t>(x) % esize != 0 || reinterpret_cast<uintptr_t>(out) % 4 != 0)
+        return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: x/out not aligned to their element size", op);
+    return IQ2_OK;
+}
+
+}  // namespace iq2
+
 extern "C" {
 
 const char* iq2_last_error(void) { return g_last_error.c_str(); }

@@ -129,6 +129,25 @@ size_t iq2_matmul_grouped_workspace_size(const iq2_matmul_problem* problems, uin
 int iq2_matmul_grouped(const iq2_matmul_problem* problems, uint32_t count, uint32_t m, int x_dtype,
                        void* workspace, size_t workspace_bytes, iq2_stream_t stream);
 
+/* Size of the fixed scratch array behind iq2_matmul_noalloc (8 MiB per GPU that loads the library). */
+#define IQ2_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+
+/*
+ * iq2_matmul for the decode path (m <= 16) that allocates nothing and takes no workspace.
+ * No counterpart in the reference (which allocates its output and needs no scratch); it exists
+ * for callers that cannot allocate device memory where they call this: an engine whose memory
+ * pool owns the whole GPU, a decode loop that must not pay cudaMalloc's synchronisation, a C
+ * binding handed only tensor pointers. The caller still provides x and out.
+ * Scratch comes from one library-owned device array of IQ2_NOALLOC_SCRATCH_BYTES, shared by all
+ * calls on a device: problems that would need more (large out_dim x m) fail with
+ * IQ2_ERR_WORKSPACE, and calls whose kernels overlap on the GPU race on it. The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress); make it outside any stream
+ * capture. m > 16 returns IQ2_ERR_UNSUPPORTED. Same checks and results as iq2_matmul otherwise.
+ */
+int iq2_matmul_noalloc(const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
+                       size_t weight_bytes_len, const uint8_t* weight_scales, size_t weight_scales_len,
+                       uint32_t out_dim, uint32_t in_dim, float* out, iq2_stream_t stream);
+
 /*
  * Dense dequantisation to out [out_dim, in_dim] in out_dtype (f16 / bf16 / f32).
  * Replaces iq2_dequantize_to_f16 (src/iq2_matmul.rs:593-602, :367-505) when out_dtype is
