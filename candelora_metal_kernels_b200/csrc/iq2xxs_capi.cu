@@ -167,7 +167,7 @@ int matmul_impl(const char* op, const void* x, int x_dtype, uint32_t m, const ui
     if (m <= 16) {
         if (iq2::gemv_fast_path_ok(m, in_dim, weight_bytes, weight_scales)) {
             const size_t need = iq2::gemv_workspace_size(m, out_dim, in_dim, sms);
-            if (workspace == nullptr || workspace_bytes < need)
+            if (need > 0 && (workspace == nullptr || workspace_bytes < need))
                 return fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
                             workspace ? workspace_bytes : (size_t)0);
             e = iq2::launch_gemv(x, x_dtype, m, weight_bytes, weight_scales, out_dim, in_dim, out,

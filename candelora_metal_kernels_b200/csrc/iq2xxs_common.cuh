@@ -49,6 +49,13 @@ __device__ __forceinline__ uint32_t ld_shared_const(uint32_t addr) {
     return v;
 }
 
+// ld_shared_v2_const: 8 bytes of such a read-only table.
+__device__ __forceinline__ uint2 ld_shared_v2_const(uint32_t addr) {
+    uint2 v;
+    asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
 // ld_shared_v4: 16 bytes at addr + OFF, kept in program order with the other volatile asm
 // (the cp.async waits that make the data valid).
 template <int OFF>
@@ -101,6 +108,11 @@ __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// L2 prefetch: no data reaches the SM, so they may run before a griddepcontrol.wait.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 __device__ __forceinline__ float half_bits_to_float(uint32_t h) {

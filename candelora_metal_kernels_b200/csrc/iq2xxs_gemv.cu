@@ -12,105 +12,92 @@
 // between HBM and an accumulator; the weights never become floats:
 //   * d*(0.5+s)*0.25 = d*(2s+1)/8 and every signed grid value is an int8 in {+-8,+-25,+-43}. One
 //     `prmt` turns a 16-bit selector (grid code | sign, from two lane-replicated shared-memory
-//     tables, so a warp's random lookups never share a bank) into four signed int8 weights.
+//     tables that each CTA builds, so a warp's random lookups never share a bank) into four
+//     signed int8 weights.
 //   * x is split per (token, 256-block) into four 7-bit signed limbs of a 28-bit fixed-point
-//     value (gemv_prep_kernel): x @ W^T becomes mma.m16n8k32 s8 x s8 -> s32 per 32-weight
-//     sub-block, scaled by the odd integer 2s+1 in s32 (exact, |sum| < 2^31) and turned into f32
-//     once per 256-block with d and the limb scale. The only rounding is the 2^-28-relative
-//     quantisation of x and f32 rounding of per-block partial sums (rel. error ~1e-6).
+//     value: x @ W^T becomes mma.m16n8k32 s8 x s8 -> s32 per 32-weight sub-block, scaled by the
+//     odd integer 2s+1 in s32 (exact, |sum| < 2^31) and turned into f32 once per 256-block with d
+//     and the limb scale. The only rounding is the 2^-28-relative quantisation of x and f32
+//     rounding of per-block partial sums (rel. error ~1e-6).
 //   * Weights stream through a per-warp cp.async ring in shared memory (one 256-weight block of
-//     ROWS rows per stage, ~140 KB in flight per SM), 16-byte chunks XOR-swizzled so the rows a
-//     warp reads together sit in different banks; one 16-byte read feeds two sub-blocks.
-//   * Stream-K: the (projection, row group, sub-block) steps of a launch are split into equal
-//     contiguous ranges, one per warp, so every warp finishes at the same time whatever the
-//     shapes. A row group cut by a range boundary is finished by the last of its (at most a few)
-//     warps, which sums the others' partials in warp order: results are deterministic.
-//   * Grouped launches: one prep launch and one GEMV launch serve up to 256 projections (e.g.
-//     q/k/v or gate/up sharing x), amortising launch and table-fill costs; projections that share
-//     an x share its limbs. Both kernels use programmatic dependent launch: the GEMV fills its
-//     tables and starts streaming weights while the prep runs.
+//     ROWS rows per stage), 16-byte chunks XOR-swizzled so the rows a warp reads together sit in
+//     different banks; one 16-byte read feeds two sub-blocks.
+//   * Work split: the launch's row tiles (ROWS rows x all of K of one projection) are dealt to
+//     pairs of CTAs (2-CTA clusters) in contiguous ranges of about equal work; inside a pair the
+//     32 warps split the range's (tile, block, sub-block) steps into equal contiguous pieces
+//     (stream-K). A tile cut between warps is finished after a cluster barrier by its first warp,
+//     which sums the partials of its warps in warp order, reading the other CTA's through
+//     distributed shared memory: deterministic, and nothing goes through global memory.
+//   * x limbs: a single projection whose limbs fit in shared memory gets them computed by every
+//     CTA from x directly (one kernel per call); otherwise gemv_prep_kernel writes them to the
+//     workspace once per distinct x and the GEMV reads them from L2.
+//   * Grouped launches serve up to 256 projections (e.g. q/k/v or gate/up sharing x) with one
+//     prep and one GEMV launch. Kernels use programmatic dependent launch: before its wait a
+//     GEMV only builds its constant table and prefetches its first weights into L2.
 #include "iq2xxs_common.cuh"
 #include "iq2xxs_codebook.h"
 #include "iq2xxs_internal.h"
 
+#include <cstring>
+#include <type_traits>
 #include <vector>
 
 namespace iq2 {
 
 namespace {
 
-constexpr int GEMV_WARPS = 16;
-constexpr int LUT_BYTES = 256 * 256;  // 256 rows x (32 lanes grid selectors | 32 lanes sign)
-constexpr int MAX_PROBLEMS = 256;     // per grouped launch
+constexpr int GEMV_WARPS = 16;            // per CTA; a cluster (2 CTAs) has 32
+constexpr int CLUSTER = 2;
+constexpr int LUT_BYTES = 256 * 256;      // 256 rows x (32 lanes grid selectors | 32 lanes sign)
+constexpr int MAX_PROBLEMS = 256;         // per grouped launch
+constexpr int MAX_CLUSTERS = 96;          // >= SMs / 2 of the device (74 on B200)
+constexpr int SMEM_LIMIT = 227 * 1024;
 
 template <int NT>
 struct GemvShape {
     static constexpr int T = NT <= 2 ? 2 : 1;          // 16-row mma tiles per warp
-    static constexpr int ROWS = 16 * T;                // rows of a row group
+    static constexpr int ROWS = 16 * T;                // rows of a tile
+    static constexpr int TOK = 2 * NT;                 // tokens incl. the zero padding of the last n8 tile
     static constexpr int STAGE_QS = ROWS * 64;         // one block of qs per row
     static constexpr int STAGE_BYTES = STAGE_QS + ROWS * 4;  // + the aligned scale word per row
-    static constexpr int NSTAGES = T == 2 ? 4 : 8;
+    static constexpr int NSTAGES = T == 2 ? 3 : 6;
     static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;  // per warp
+    static constexpr int PART_BYTES = GEMV_WARPS * 2 * TOK * ROWS * 4;  // [warp][first|last][token][row]
     // The table sits at the first 64 KB-aligned shared address of the block's window and the
     // warps' rings fill the space around it; whatever the window's base, this suffices:
-    static constexpr int SMEM = LUT_BYTES + (GEMV_WARPS + 1) * RING_BYTES;
+    static constexpr int SMEM = LUT_BYTES + (GEMV_WARPS + 1) * RING_BYTES + PART_BYTES;
 };
 
 int nt_for(uint32_t m) { return m <= 2 ? 1 : (m <= 4 ? 2 : (m <= 8 ? 4 : 8)); }
 int rows_for(uint32_t m) { return nt_for(m) <= 2 ? 32 : 16; }
 
+// x limbs of one block (256 k) of one x, for the kernel-side layout
+__host__ __device__ inline size_t xs_bytes(uint32_t nb, int nt) { return (size_t)nb * 8 * nt * 256; }
+__host__ __device__ inline size_t cs_bytes(uint32_t nb, int nt) { return (size_t)nb * nt * 8 * sizeof(float); }
+
 // ---------------------------------------------------------------------------------------------
-// x -> int8 limb fragments. One warp per (x item, token m, block b); lane = (sub-block sbi,
-// group t) owns the 8 activations k = b*256 + sbi*32 + t*8 + [0, 8).
-// With amax = max |x| over the block and amax = f * 2^E (f in [0.5, 1)):
+// x -> int8 limb fragments of one (token m, block b). Lane = (sub-block sbi, group t) owns the 8
+// activations k = b*256 + sbi*32 + t*8 + [0, 8). With amax = max |x| over the block and
+// amax = f * 2^E (f in [0.5, 1)):
 //   q = rint(x * 2^(27-E)) (|q| <= 2^27), |q| = L3*2^21 + L2*2^14 + L1*2^7 + L0 (7-bit limbs),
 //   each limb carrying the sign of q; column scale of limb l = 2^(E - 27 + 7l) / 8 (the /8 is
 //   the weight scale's (2s+1)/8). Non-finite blocks get NaN scales, so the output is NaN.
+//   Tokens m >= M (the padding of the last n8 tile) get zero limbs and scales.
 // Fragment layout (mma B operand, m16n8k32 "col"), sub-block sb, n8 tile nt:
 //   xb[((sb*NT + nt)*32 + col*4 + t)*8 + i] = limb of group t, element i; col = (m%2)*4 + l.
-struct PrepItem {
-    const void* x;
-    uint8_t* xb;
-    float* colscale;
-    uint32_t K, nb, warp_begin, pad;
-};
-
-template <int CAP>
-struct PrepLaunch {
-    PrepItem item[CAP];
-    uint32_t count, M;
-    uint32_t* counters;
-    uint32_t ncounters;
-};
-
-template <typename XT, int NT, int CAP>
-__global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ PrepLaunch<CAP> L) {
-    // x may be written by the previous kernel and the workspace may still be read by the
-    // previous GEMV: wait for both before touching memory. Only then let the GEMV launch, so
-    // its early weight prefetch also runs after every earlier kernel has finished.
-    pdl_wait();
-    pdl_launch_dependents();
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < L.ncounters; i += gridDim.x * blockDim.x)
-        L.counters[i] = 0u;
-    const uint32_t wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    uint32_t it = 0;
-    while (it + 1 < L.count && L.item[it + 1].warp_begin <= wid) ++it;
-    const PrepItem& P = L.item[it];
-    const uint32_t local = wid - P.warp_begin;
-    if (local >= L.M * P.nb) return;
-    const uint32_t m = local / P.nb, b = local % P.nb;
+template <typename XT, int NT>
+__device__ __forceinline__ void limb_job(const XT* __restrict__ x, uint32_t M, uint32_t K, uint32_t m,
+                                         uint32_t b, uint8_t* xb, float* colscale, int lane) {
     const int sbi = lane >> 2, t = lane & 3;
     const size_t k0 = (size_t)b * QK + sbi * 32 + t * 8;
-    const XT* xr = static_cast<const XT*>(P.x) + (size_t)m * P.K;
-
+    const XT* xr = x + (size_t)min(m, M - 1u) * K;
     float v[8];
     float amax = 0.0f;
     bool bad = false;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const size_t k = k0 + i;
-        v[i] = k < P.K ? to_f32(xr[k]) : 0.0f;
+        v[i] = (m < M && k < K) ? to_f32(xr[k]) : 0.0f;
         bad |= !isfinite(v[i]);
         amax = fmaxf(amax, fabsf(v[i]));
     }
@@ -118,13 +105,18 @@ __global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ 
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
     bad = __any_sync(0xFFFFFFFFu, bad);
 
-    int E = 0;
-    if (!bad && amax > 0.0f) frexpf(amax, &E);
+    // E from the exponent field (amax normal); 2^(27-E) is then a normal float for E >= -100,
+    // and x * 2^(27-E) is exact. Tiny or subnormal blocks take the library path.
+    const uint32_t abits = __float_as_uint(amax);
+    const bool fast = (abits >> 23) >= 27u;  // amax >= 2^-100
+    int E = (int)(abits >> 23) - 126;
+    if (!fast && !bad && amax > 0.0f) frexpf(amax, &E);
+    const float sc = __uint_as_float((uint32_t)(154 - E) << 23);
     uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
     if (!bad && amax > 0.0f) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int q = (int)rintf(ldexpf(v[i], 27 - E));
+            const int q = (int)rintf(fast ? v[i] * sc : ldexpf(v[i], 27 - E));
             const uint32_t mag = (uint32_t)(q < 0 ? -q : q);
 #pragma unroll
             for (int l = 0; l < 4; ++l) {
@@ -139,7 +131,7 @@ __global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ 
     const size_t sb = (size_t)b * 8 + sbi;
 #pragma unroll
     for (int l = 0; l < 4; ++l) {
-        uint2* dst = reinterpret_cast<uint2*>(P.xb + ((sb * NT + nt) * 32 + (colbase + l) * 4 + t) * 8);
+        uint2* dst = reinterpret_cast<uint2*>(xb + ((sb * NT + nt) * 32 + (colbase + l) * 4 + t) * 8);
         *dst = make_uint2(lo[l], hi[l]);
     }
     if (lane < 4) {
@@ -147,49 +139,80 @@ __global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ 
         if (bad) s = __int_as_float(0x7FC00000);
         else if (amax == 0.0f) s = 0.0f;
         else s = ldexpf(1.0f, E - 30 + 7 * lane);
-        P.colscale[(size_t)b * (NT * 8) + nt * 8 + colbase + lane] = s;
+        colscale[(size_t)b * (NT * 8) + nt * 8 + colbase + lane] = s;
     }
+}
+
+struct PrepItem {
+    const void* x;
+    uint8_t* xb;
+    float* colscale;
+    uint32_t K, nb, warp_begin, pad;
+};
+
+template <int CAP>
+struct PrepLaunch {
+    PrepItem item[CAP];
+    uint32_t count, M;
+};
+
+// One warp per (x item, token m < 2*NT, block b).
+template <typename XT, int NT, int CAP>
+__global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ PrepLaunch<CAP> L) {
+    // The GEMV may be scheduled at once: before its own wait it only builds its constant
+    // table and warms L2. x may be written by the previous kernel and the workspace may still
+    // be read by the previous GEMV, so wait for both before touching memory.
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    uint32_t it = 0;
+    while (it + 1 < L.count && L.item[it + 1].warp_begin <= wid) ++it;
+    const PrepItem& P = L.item[it];
+    const uint32_t local = wid - P.warp_begin;
+    if (local >= 2u * NT * P.nb) return;
+    limb_job<XT, NT>(static_cast<const XT*>(P.x), L.M, P.K, local / P.nb, local % P.nb, P.xb, P.colscale,
+                     lane);
 }
 
 // ---------------------------------------------------------------------------------------------
 struct GemvProblem {  // 64 bytes
     const uint8_t* qs;
     const uint8_t* sc;
-    const uint8_t* xb;
-    const float* colscale;
+    const uint8_t* xb;        // x fragments from the prep kernel (unused when fused)
+    const float* colscale;    // their column scales
     float* out;
-    uint32_t N, nb, row_groups, tb_begin;  // tb_begin: first tile-block (ROWS rows x 1 block)
-    uint32_t counter_base, pad;
+    uint32_t N, nb, tiles, tb_begin;  // tiles = ceil(N / ROWS); tb_begin: first tile-block (ROWS rows x 1 block)
+    uint32_t pad[2];
 };
 
 template <int CAP>
 struct GemvLaunch {
     GemvProblem prob[CAP];
     uint32_t count, M;
-    uint32_t total_steps;  // 8 sub-block steps per tile-block
-    uint32_t pad;
-    float* partial;        // [warps][2][ROWS * M]
-    uint32_t* counters;
+    const void* x;                          // fused: the activations [M, K] of the single projection
+    uint32_t K, clusters;
+    uint32_t cl_tb[MAX_CLUSTERS + 1];       // cluster c owns tile-blocks [cl_tb[c], cl_tb[c+1]) (whole tiles)
+    uint16_t cl_p[MAX_CLUSTERS];            // problem of the cluster's first tile
 };
 
-// Stream-K partition of [0, total) over W warps: the first r warps get q+1 steps, the rest q.
+// Stream-K partition of [base, base + 32q + r) over a cluster's 32 warps: the first r get q+1 steps.
 struct Partition {
-    uint32_t q, r;
-    __device__ __forceinline__ uint32_t begin(uint32_t w) const { return w * q + min(w, r); }
+    uint32_t q, r, base;
+    __device__ __forceinline__ uint32_t begin(uint32_t w) const { return base + w * q + min(w, r); }
     __device__ __forceinline__ uint32_t owner(uint32_t s) const {
-        const uint32_t big = r * (q + 1);
-        return s < big ? s / (q + 1) : r + (s - big) / q;
+        const uint32_t ls = s - base, big = r * (q + 1);
+        return ls < big ? ls / (q + 1) : r + (ls - big) / q;
     }
 };
 
-// Cursor over the tile-blocks (problem p, row group rg, block blk) of a launch, in order.
+// Cursor over the tile-blocks (problem p, tile rg, block blk) of a launch, in order.
 struct TbCursor {
     uint32_t tb, p, rg, blk;
 };
 
 template <int CAP>
-__device__ __forceinline__ void cursor_seek(const GemvLaunch<CAP>& L, uint32_t tb, TbCursor& c) {
-    uint32_t p = 0;
+__device__ __forceinline__ void cursor_seek(const GemvLaunch<CAP>& L, uint32_t p, uint32_t tb, TbCursor& c) {
     while (p + 1 < L.count && L.prob[p + 1].tb_begin <= tb) ++p;
     const uint32_t local = tb - L.prob[p].tb_begin;
     c.tb = tb;
@@ -203,11 +226,31 @@ __device__ __forceinline__ void cursor_next(const GemvLaunch<CAP>& L, TbCursor& 
     ++c.tb;
     if (++c.blk == L.prob[c.p].nb) {
         c.blk = 0;
-        if (++c.rg == L.prob[c.p].row_groups) {
+        if (++c.rg == L.prob[c.p].tiles) {
             c.rg = 0;
             ++c.p;
         }
     }
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory byte in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
 }
 
 // Per-lane decode constants. The table base is 64 KB-aligned, so every table address is
@@ -231,12 +274,13 @@ __device__ __forceinline__ void decode_group(const DecodeK& k, uint32_t aux_g, u
     hi = prmt(KPOS, KNEG, sel >> 16);
 }
 
-// One stage (a block of ROWS rows) of the decode: accumulate s32 sums per 256-block in I.
-// PARTIAL: only sub-blocks [s_lo, s_hi) count (the first/last stage of a warp's range).
-template <int NT, bool PARTIAL>
-__device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, const uint8_t* xbp,
-                                              const bool (&bact)[NT], uint32_t s_lo, uint32_t s_hi,
-                                              uint32_t rowbase, uint32_t swz,
+// One stage (a block of ROWS rows) of the decode: s32 sums per 256-block in I. The first
+// sub-block initialises I, so I needs no clearing. PARTIAL: only sub-blocks [s_lo, s_hi) count
+// (the first/last stage of a warp's range); the others see zero x fragments. FUSED: fragments
+// from shared memory (xsp: shared address), else from global memory (xbp).
+template <int NT, bool PARTIAL, bool FUSED>
+__device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, const uint8_t* xbp, uint32_t xsp,
+                                              uint32_t s_lo, uint32_t s_hi, uint32_t rowbase, uint32_t swz,
                                               int (&I)[GemvShape<NT>::T][NT][4]) {
     constexpr int T = GemvShape<NT>::T;
 #pragma unroll
@@ -256,12 +300,12 @@ __device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, 
             uint32_t bf[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                bool on = bact[nt];
-                if (PARTIAL) on = on && sb >= s_lo && sb < s_hi;  // other sub-blocks add 0
-                uint2 v = make_uint2(0u, 0u);
-                if (on) v = __ldg(reinterpret_cast<const uint2*>(xbp + (sb * NT + nt) * 256));
+                uint2 v;
+                if (FUSED) v = ld_shared_v2_const(xsp + (sb * NT + nt) * 256);
+                else v = __ldg(reinterpret_cast<const uint2*>(xbp + (sb * NT + nt) * 256));
                 bf[nt][0] = v.x;
                 bf[nt][1] = v.y;
+                if (PARTIAL && (sb < s_lo || sb >= s_hi)) bf[nt][0] = bf[nt][1] = 0u;
             }
 #pragma unroll
             for (int tt = 0; tt < T; ++tt) {
@@ -275,54 +319,91 @@ __device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, 
                 for (int nt = 0; nt < NT; ++nt) {
                     int d[4];
                     mma_s8_16832(d, w0, w1, w2, w3, bf[nt][0], bf[nt][1]);
-                    I[tt][nt][0] += c0 * d[0];
-                    I[tt][nt][1] += c0 * d[1];
-                    I[tt][nt][2] += c1 * d[2];
-                    I[tt][nt][3] += c1 * d[3];
+                    if (sb == 0) {
+                        I[tt][nt][0] = c0 * d[0];
+                        I[tt][nt][1] = c0 * d[1];
+                        I[tt][nt][2] = c1 * d[2];
+                        I[tt][nt][3] = c1 * d[3];
+                    } else {
+                        I[tt][nt][0] += c0 * d[0];
+                        I[tt][nt][1] += c0 * d[1];
+                        I[tt][nt][2] += c1 * d[2];
+                        I[tt][nt][3] += c1 * d[3];
+                    }
                 }
             }
         }
     }
 }
 
-template <int NT, int CAP>
+// XDT < 0: x fragments come from gemv_prep_kernel (workspace); XDT = 0/1/2: a single projection
+// whose f32/f16/bf16 x this kernel turns into limbs itself (kernel-side layout in shared memory).
+template <int NT, int CAP, int XDT>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvLaunch<CAP> L) {
     using S_ = GemvShape<NT>;
-    constexpr int T = S_::T, ROWS = S_::ROWS, STAGE_QS = S_::STAGE_QS;
+    constexpr bool FUSED = XDT >= 0;
+    constexpr int T = S_::T, ROWS = S_::ROWS, TOK = S_::TOK, STAGE_QS = S_::STAGE_QS;
     constexpr int STAGE_BYTES = S_::STAGE_BYTES, NSTAGES = S_::NSTAGES, RING_BYTES = S_::RING_BYTES;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
+    // The next call's kernels may be scheduled now; each waits for this grid to finish before
+    // it touches memory this one uses.
+    pdl_launch_dependents();
 
-    // ---- shared layout: table at the first 64 KB-aligned address, rings around it ----
+    // ---- shared layout: table at the first 64 KB-aligned address, rings around it, then the
+    // ---- partial slots and (fused) the x limbs and their scales
     const uint32_t base_s = smem_u32(smem);
     const uint32_t lut_s = (base_s + 0xFFFFu) & ~0xFFFFu;
     const uint32_t gap = lut_s - base_s;
-    const uint32_t gap_warps = gap / RING_BYTES;
+    const uint32_t gap_warps = min(gap / RING_BYTES, (uint32_t)GEMV_WARPS);
     const uint32_t ring_off = (uint32_t)warp < gap_warps
                                   ? (uint32_t)warp * RING_BYTES
                                   : gap + LUT_BYTES + ((uint32_t)warp - gap_warps) * RING_BYTES;
     uint8_t* ring = smem + ring_off;
     const uint32_t ring_s = base_s + ring_off;
+    const uint32_t part_off = gap + LUT_BYTES + (GEMV_WARPS - gap_warps) * RING_BYTES;
+    float* part = reinterpret_cast<float*>(smem + part_off);
+    const uint32_t part_s = base_s + part_off;
+    const uint32_t xs_off = part_off + S_::PART_BYTES;
+    const uint32_t xs_s = base_s + xs_off;
+    const uint32_t nbx = FUSED ? L.prob[0].nb : 0u;
+    const uint32_t cs_off = xs_off + (uint32_t)xs_bytes(nbx, NT);
+    (void)ring;
 
-    // This warp's step range [a, b) and the tile-blocks it touches [tb0, tb1).
-    const uint32_t W = gridDim.x * GEMV_WARPS;
-    const uint32_t w = blockIdx.x * GEMV_WARPS + warp;
-    const Partition part{L.total_steps / W, L.total_steps % W};
-    const uint32_t a = part.begin(w), b = part.begin(w + 1);
+    // This warp's step range [a, b) of its cluster and the tile-blocks it touches [tb0, tb1).
+    const uint32_t rank = cluster_rank();
+    const uint32_t cl = blockIdx.x / CLUSTER;
+    const uint32_t TB0 = L.cl_tb[cl], TB1 = L.cl_tb[cl + 1];
+    const uint32_t S = (TB1 - TB0) * 8;
+    const Partition part_{S / (CLUSTER * GEMV_WARPS), S % (CLUSTER * GEMV_WARPS), TB0 * 8};
+    const uint32_t wg = rank * GEMV_WARPS + warp;  // warp index within the cluster
+    const uint32_t a = part_.begin(wg), b = part_.begin(wg + 1);
     const uint32_t tb0 = a >> 3, tb1 = (b + 7) >> 3;
+    const uint32_t p0 = L.cl_p[cl];
 
-    // ---- the decode table: 64 KB image from global memory (one cp.async group) ----
+    // ---- the decode table, built from the 1.5 KB compact copy: row e = 32 copies (one per lane)
+    // ---- of the grid selector of code e, then (e < 128) 32 copies of the sign selector of index e
     {
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(&IQ2XXS_LUT_IMAGE);
-        for (int i = threadIdx.x; i < LUT_BYTES / 16; i += blockDim.x)
-            cp_async_16(lut_s + i * 16, src + i * 16, 16u);
-        cp_async_commit();
+        constexpr int PER_THREAD = LUT_BYTES / 16 / (GEMV_WARPS * 32);
+        uint32_t v[PER_THREAD];  // all loads first: one latency, not one per store
+#pragma unroll
+        for (int i = 0; i < PER_THREAD; ++i) {
+            const int c = threadIdx.x + i * GEMV_WARPS * 32;
+            const int row = c >> 4, half = (c >> 3) & 1;
+            v[i] = half == 0 ? __ldg(IQ2XXS_SEL_COMPACT + row)
+                             : (row < 128 ? __ldg(IQ2XXS_SEL_COMPACT + 256 + row) : 0u);
+        }
+#pragma unroll
+        for (int i = 0; i < PER_THREAD; ++i) {
+            const int c = threadIdx.x + i * GEMV_WARPS * 32;
+            *reinterpret_cast<uint4*>(smem + gap + c * 16) = make_uint4(v[i], v[i], v[i], v[i]);
+        }
     }
 
     // ---- issue side: cp.async stages of one tile-block each, NSTAGES ahead ----
     TbCursor ic;
-    if (a < b) cursor_seek(L, tb0, ic);
+    if (a < b) cursor_seek(L, p0, tb0, ic);
     int islot = 0;
     auto issue = [&]() {
         if (a < b && ic.tb < tb1) {
@@ -359,19 +440,36 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         islot = (islot + 1 == NSTAGES) ? 0 : islot + 1;
     };
 
-    // The first stages only read weights: start them before waiting for anything.
+    // Until the kernels before this one have finished, the weights may still be being written:
+    // only warm L2 with the first stage (a prefetch brings nothing into the SM, and L2 is
+    // coherent with every writer), then wait, then copy the stages for real.
+    if (a < b) {
+        const GemvProblem& P = L.prob[ic.p];
+        const uint32_t row = ic.rg * ROWS + lane;
+        if (lane < ROWS && row < P.N) {
+            const size_t blk_idx = (size_t)row * P.nb + ic.blk;
+            const uint8_t* q = P.qs + blk_idx * QS_BYTES;
+            prefetch_l2(q);
+            prefetch_l2(q + 32);
+            prefetch_l2(P.sc + blk_idx * SC_BYTES);
+        }
+    }
+    if constexpr (FUSED) {
+        constexpr uint32_t XB = XDT == 0 ? 4u : 2u;
+        const uint8_t* xp = static_cast<const uint8_t*>(L.x);
+        for (uint32_t o = threadIdx.x * 128u; o < L.M * L.K * XB; o += blockDim.x * 128u) prefetch_l2(xp + o);
+    }
+    // x (fused) or its fragments (prep kernel), and the outputs, may belong to earlier kernels.
+    pdl_wait();
 #pragma unroll
     for (int i = 0; i < NSTAGES; ++i) issue();
-    cp_async_wait<NSTAGES>();  // the table group (issued first) has landed
-    __syncthreads();
-    // x fragments, column scales, counters and outputs are produced by / shared with the prep
-    // kernel: wait for it here.
-    pdl_wait();
-    if (a >= b) {
-        cp_async_wait<0>();
-        pdl_launch_dependents();
-        return;
+    if constexpr (FUSED) {
+        using XT = typename std::conditional<XDT == 0, float, typename std::conditional<XDT == 1, __half, __nv_bfloat16>::type>::type;
+        for (uint32_t job = warp; job < TOK * nbx; job += GEMV_WARPS)
+            limb_job<XT, NT>(static_cast<const XT*>(L.x), L.M, L.K, job / nbx, job % nbx, smem + xs_off,
+                             reinterpret_cast<float*>(smem + cs_off), lane);
     }
+    __syncthreads();  // the table (and the fused limbs) are complete
 
     DecodeK dk;
     dk.gsrc = (lut_s & 0xFFFF0000u) | ((uint32_t)lane * 4u);
@@ -380,10 +478,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     dk.soff = lut_s | 128u | ((uint32_t)lane * 4u);
     const uint32_t swz = (uint32_t)((g >> 1) & 3);  // rows g, g+8, g+16, g+24 share it
     const uint32_t rowbase = (uint32_t)g * 64u;     // rows tt*16+g (+8): rowbase + tt*1024 (+512)
-
-    bool bact[NT];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) bact[nt] = (uint32_t)(nt * 2 + (g >> 2)) < L.M;
 
     float F[T][NT][4];
 #pragma unroll
@@ -394,37 +488,34 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
             for (int k = 0; k < 4; ++k) F[i][j][k] = 0.0f;
 
     TbCursor cc;
-    cursor_seek(L, tb0, cc);
+    if (a < b) cursor_seek(L, p0, tb0, cc);
+    else cc.tb = tb1;
     int slot = 0;
     for (; cc.tb < tb1;) {
         const GemvProblem& P = L.prob[cc.p];
         cp_async_wait<NSTAGES - 1>();
         __syncwarp();
         const uint32_t st_s = ring_s + slot * STAGE_BYTES;
-        const uint8_t* st = ring + slot * STAGE_BYTES;
         const uint32_t s_lo = cc.tb * 8 < a ? a - cc.tb * 8 : 0u;
         const uint32_t s_hi = min(8u, b - cc.tb * 8);
 
         int I[T][NT][4];
-#pragma unroll
-        for (int i = 0; i < T; ++i)
-#pragma unroll
-            for (int j = 0; j < NT; ++j)
-#pragma unroll
-                for (int k = 0; k < 4; ++k) I[i][j][k] = 0;
-
-        const uint8_t* xbp = P.xb + (size_t)cc.blk * 8 * NT * 256 + lane * 8;
+        const uint8_t* xbp = FUSED ? nullptr : P.xb + (size_t)cc.blk * 8 * NT * 256 + lane * 8;
+        const uint32_t xsp = xs_s + cc.blk * 8 * NT * 256 + lane * 8;
         if (s_lo == 0 && s_hi == 8)
-            stage_compute<NT, false>(dk, st_s, xbp, bact, s_lo, s_hi, rowbase, swz, I);
+            stage_compute<NT, false, FUSED>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
         else
-            stage_compute<NT, true>(dk, st_s, xbp, bact, s_lo, s_hi, rowbase, swz, I);
+            stage_compute<NT, true, FUSED>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
 
         // Block epilogue: s32 -> f32 with d (per row) and the limb scale (per column).
         {
             float2 cs[NT];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-                cs[nt] = __ldg(reinterpret_cast<const float2*>(P.colscale + (size_t)cc.blk * (NT * 8) + nt * 8 + 2 * t));
+            for (int nt = 0; nt < NT; ++nt) {
+                const uint32_t ci = cc.blk * (NT * 8) + nt * 8 + 2 * t;
+                if (FUSED) cs[nt] = *reinterpret_cast<const float2*>(smem + cs_off + ci * 4);
+                else cs[nt] = __ldg(reinterpret_cast<const float2*>(P.colscale + ci));
+            }
             const uint32_t row0 = cc.rg * ROWS;
 #pragma unroll
             for (int tt = 0; tt < T; ++tt) {
@@ -443,7 +534,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 }
             }
         }
-        (void)st;
 
         const uint32_t rg = cc.rg;
         const bool rg_done = (cc.blk + 1 == P.nb) || (cc.tb + 1 == tb1);
@@ -453,12 +543,13 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         slot = (slot + 1 == NSTAGES) ? 0 : slot + 1;
         if (!rg_done) continue;
 
-        // ---- row group epilogue: reduce limb columns to tokens; write out or a partial ----
+        // ---- tile epilogue: reduce limb columns to tokens; write out, or a partial for the
+        // ---- tile's first warp to finish after the cluster barrier
         const uint32_t rg_first = (P.tb_begin + rg * P.nb) * 8, rg_end = rg_first + P.nb * 8;
         const bool complete = a <= rg_first && b >= rg_end;
         const uint32_t row0 = rg * ROWS;
-        const uint32_t j = a >= rg_first ? 0u : 1u;  // this row group is my first (0) or last (1)
-        float* pslot = L.partial + ((size_t)w * 2 + j) * ROWS * L.M;
+        const uint32_t j = a >= rg_first ? 0u : 1u;  // this tile is my first (0) or last (1)
+        float* pslot = part + ((size_t)warp * 2 + j) * TOK * ROWS;
 #pragma unroll
         for (int tt = 0; tt < T; ++tt) {
 #pragma unroll
@@ -469,11 +560,13 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 v1 += __shfl_xor_sync(0xFFFFFFFFu, v1, 1);
                 const uint32_t m = nt * 2 + (t >> 1);
                 const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
-                if ((t & 1) == 0 && m < L.M) {
+                if ((t & 1) == 0) {
                     if (complete) {
-                        float* o = P.out + (size_t)m * P.N;
-                        if (row0 + r0 < P.N) o[row0 + r0] = v0;
-                        if (row0 + r1 < P.N) o[row0 + r1] = v1;
+                        if (m < L.M) {
+                            float* o = P.out + (size_t)m * P.N;
+                            if (row0 + r0 < P.N) o[row0 + r0] = v0;
+                            if (row0 + r1 < P.N) o[row0 + r1] = v1;
+                        }
                     } else {
                         pslot[m * ROWS + r0] = v0;
                         pslot[m * ROWS + r1] = v1;
@@ -482,32 +575,37 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 F[tt][nt][0] = F[tt][nt][1] = F[tt][nt][2] = F[tt][nt][3] = 0.0f;
             }
         }
-        if (!complete) {
-            const uint32_t w_first = part.owner(rg_first), w_last = part.owner(rg_end - 1);
-            const uint32_t count = w_last - w_first + 1;
-            __threadfence();
-            __syncwarp();
-            uint32_t prev = 0;
-            if (lane == 0) prev = atomicAdd(L.counters + P.counter_base + rg, 1u);
-            prev = __shfl_sync(0xFFFFFFFFu, prev, 0);
-            if (prev == count - 1) {
-                __threadfence();
-                for (uint32_t idx = lane; idx < (uint32_t)ROWS * L.M; idx += 32) {
-                    const uint32_t m = idx / ROWS, r = idx % ROWS;
-                    if (row0 + r >= P.N) continue;
-                    float acc = 0.0f;
-                    for (uint32_t ww = w_first; ww <= w_last; ++ww) {
-                        const uint32_t jj = part.begin(ww) >= rg_first ? 0u : 1u;
-                        acc += __ldcg(L.partial + ((size_t)ww * 2 + jj) * ROWS * L.M + m * ROWS + r);
-                    }
-                    P.out[(size_t)m * P.N + row0 + r] = acc;
+    }
+    cp_async_wait<0>();
+
+    // ---- tiles cut between warps: every partial is in shared memory after the barrier; the
+    // ---- tile's first warp adds them in warp order (the other CTA's through DSMEM)
+    cluster_sync();
+    if (a < b) {
+        TbCursor lc;
+        cursor_seek(L, p0, tb1 - 1, lc);  // this warp's last tile
+        const GemvProblem& P = L.prob[lc.p];
+        const uint32_t rg_first = (P.tb_begin + lc.rg * P.nb) * 8, rg_end = rg_first + P.nb * 8;
+        if (rg_end > b && rg_first >= a) {
+            const uint32_t w_last = part_.owner(rg_end - 1);
+            const uint32_t row0 = lc.rg * ROWS;
+            for (uint32_t idx = lane; idx < (uint32_t)ROWS * L.M; idx += 32) {
+                const uint32_t m = idx / ROWS, r = idx % ROWS;
+                if (row0 + r >= P.N) continue;
+                float acc = 0.0f;
+#pragma unroll 4
+                for (uint32_t ww = wg; ww <= w_last; ++ww) {
+                    const uint32_t jj = part_.begin(ww) >= rg_first ? 0u : 1u;
+                    const uint32_t off = (((ww % GEMV_WARPS) * 2 + jj) * TOK + m) * ROWS + r;
+                    const uint32_t addr = part_s + off * 4;
+                    acc += ld_cluster_f32(map_shared(addr, ww / GEMV_WARPS));
                 }
-                if (lane == 0) L.counters[P.counter_base + rg] = 0u;
+                P.out[(size_t)m * P.N + row0 + r] = acc;
             }
         }
     }
-    cp_async_wait<0>();
-    pdl_launch_dependents();
+    // keep this CTA's partials alive until the other CTA has read them (no data to publish)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -571,30 +669,77 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct GroupPlan {
     int nt, rows;
-    uint32_t warps;          // W = grid * GEMV_WARPS
-    uint32_t grid;
-    uint32_t total_steps;
-    size_t off_counters, off_partial, off_x, total;
+    bool fused;
+    uint32_t clusters;
+    std::vector<uint32_t> cl_tb;      // clusters + 1 tile-block boundaries (whole tiles)
+    std::vector<uint16_t> cl_p;       // problem of each cluster's first tile
+    std::vector<uint32_t> tb_begin, tiles, nb;
+    size_t total;
     std::vector<uint32_t> x_of;       // problem -> unique x index
     std::vector<const void*> xs;      // unique x pointers
     std::vector<uint32_t> xk;         // their K
     std::vector<size_t> off_xb, off_cs;
-    std::vector<uint32_t> counter_base;
+    size_t smem;
 };
 
-GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int num_sms) {
+template <int NT>
+size_t smem_for(bool fused, uint32_t nb) {
+    return GemvShape<NT>::SMEM + (fused ? xs_bytes(nb, NT) + cs_bytes(nb, NT) : 0);
+}
+
+size_t smem_for_nt(int nt, bool fused, uint32_t nb) {
+    switch (nt) {
+        case 1: return smem_for<1>(fused, nb);
+        case 2: return smem_for<2>(fused, nb);
+        case 4: return smem_for<4>(fused, nb);
+        default: return smem_for<8>(fused, nb);
+    }
+}
+
+// How many 2-CTA clusters of the GEMV (one CTA per SM) the current device runs at once; launching
+// more would make the surplus wait for a second wave. Asked once per device.
+int max_active_clusters(int num_sms) {
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return num_sms / CLUSTER;
+    if (cached[dev] > 0) return cached[dev];
+    int n = 0;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CLUSTER;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms);
+    cfg.blockDim = dim3(GEMV_WARPS * 32);
+    cfg.dynamicSmemBytes = SMEM_LIMIT;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaFuncSetAttribute(gemv_kernel<1, 1, -1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, gemv_kernel<1, 1, -1>, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = num_sms / CLUSTER;
+    }
+    if (n > num_sms / CLUSTER) n = num_sms / CLUSTER;
+    cached[dev] = n > 0 ? n : 1;
+    return cached[dev];
+}
+
+// max_cl: clusters the device can run at once (0 when only the workspace size is wanted).
+GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int max_cl) {
     GroupPlan pl;
     pl.nt = nt_for(m);
     pl.rows = rows_for(m);
-    uint64_t steps = 0;
-    uint32_t counters = 0;
-    pl.counter_base.resize(count);
+    uint64_t tbs = 0, total_tiles = 0;
     for (uint32_t i = 0; i < count; ++i) {
         const uint32_t nb = (probs[i].k + QK - 1) / QK;
-        const uint32_t rgs = (probs[i].n + pl.rows - 1) / pl.rows;
-        pl.counter_base[i] = counters;
-        counters += rgs;
-        steps += (uint64_t)rgs * nb * 8;
+        const uint32_t tiles = (probs[i].n + pl.rows - 1) / pl.rows;
+        pl.nb.push_back(nb);
+        pl.tiles.push_back(tiles);
+        pl.tb_begin.push_back((uint32_t)tbs);
+        tbs += (uint64_t)tiles * nb;
+        total_tiles += tiles;
         uint32_t xi = 0;
         while (xi < pl.xs.size() && !(pl.xs[xi] == probs[i].x && pl.xk[xi] == probs[i].k)) ++xi;
         if (xi == pl.xs.size()) {
@@ -603,108 +748,150 @@ GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, i
         }
         pl.x_of.push_back(xi);
     }
-    pl.total_steps = (uint32_t)steps;
-    // at least ~16 steps per warp, at most one CTA per SM
-    uint64_t ctas = (steps + (uint64_t)GEMV_WARPS * 16 - 1) / ((uint64_t)GEMV_WARPS * 16);
-    if (ctas < 1) ctas = 1;
-    if (ctas > (uint64_t)num_sms) ctas = num_sms;
-    pl.grid = (uint32_t)ctas;
-    pl.warps = pl.grid * GEMV_WARPS;
+    // one projection whose limbs fit in shared memory: the GEMV makes them itself
+    pl.fused = count == 1 && pl.nt <= 2 && smem_for_nt(pl.nt, true, pl.nb[0]) <= (size_t)SMEM_LIMIT;
+    pl.smem = smem_for_nt(pl.nt, pl.fused, count ? pl.nb[0] : 0);
+    // clusters: whole tiles, about equal numbers of tile-blocks each
+    uint64_t cl = (uint64_t)(max_cl > 0 ? max_cl : 1);
+    if (cl > MAX_CLUSTERS) cl = MAX_CLUSTERS;
+    if (cl > total_tiles) cl = total_tiles;
+    if (cl < 1) cl = 1;
+    pl.cl_tb.push_back(0);
+    pl.cl_p.push_back(0);
+    {
+        uint32_t p = 0, rg = 0;
+        uint64_t done = 0;
+        for (uint64_t c = 1; c < cl; ++c) {
+            const uint64_t target = tbs * c / cl;
+            // advance whole tiles while the boundary gets closer to the target
+            while (p < count) {
+                const uint64_t w = pl.nb[p];
+                if (done >= target || (done + w > target && done + w - target > target - done)) break;
+                done += w;
+                if (++rg == pl.tiles[p]) { rg = 0; ++p; }
+            }
+            if (done <= pl.cl_tb.back()) continue;  // empty cluster: merge
+            pl.cl_tb.push_back((uint32_t)done);
+            uint32_t pp = p;
+            while (pp < count && pl.tiles[pp] == 0) ++pp;
+            pl.cl_p.push_back((uint16_t)(pp < count ? pp : count - 1));
+        }
+        pl.cl_tb.push_back((uint32_t)tbs);
+    }
+    pl.clusters = (uint32_t)pl.cl_tb.size() - 1;
     size_t off = 0;
-    pl.off_counters = off;
-    off = align_up(off + (size_t)counters * sizeof(uint32_t), 256);
-    pl.off_partial = off;
-    off = align_up(off + (size_t)pl.warps * 2 * pl.rows * m * sizeof(float), 256);
-    pl.off_x = off;
-    for (size_t xi = 0; xi < pl.xs.size(); ++xi) {
-        const uint32_t nb = (pl.xk[xi] + QK - 1) / QK;
-        pl.off_xb.push_back(off);
-        off = align_up(off + (size_t)nb * 8 * pl.nt * 256, 256);
-        pl.off_cs.push_back(off);
-        off = align_up(off + (size_t)nb * pl.nt * 8 * sizeof(float), 256);
+    if (!pl.fused) {
+        for (size_t xi = 0; xi < pl.xs.size(); ++xi) {
+            const uint32_t nb = (pl.xk[xi] + QK - 1) / QK;
+            pl.off_xb.push_back(off);
+            off = align_up(off + xs_bytes(nb, pl.nt), 256);
+            pl.off_cs.push_back(off);
+            off = align_up(off + cs_bytes(nb, pl.nt), 256);
+        }
     }
     pl.total = off;
     return pl;
 }
 
-template <int NT, int CAP>
-cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
-                             uint8_t* ws, const GroupPlan& pl, cudaStream_t stream) {
-    using S_ = GemvShape<NT>;
-    // ---- prep launch (unique x's) ----
-    PrepLaunch<CAP> pre;
-    pre.count = (uint32_t)pl.xs.size();
-    pre.M = m;
-    pre.counters = reinterpret_cast<uint32_t*>(ws + pl.off_counters);
-    pre.ncounters = pl.counter_base.empty() ? 0u
-                                            : pl.counter_base.back() + (probs[count - 1].n + pl.rows - 1) / pl.rows;
-    uint32_t warps = 0;
-    for (uint32_t xi = 0; xi < pre.count; ++xi) {
-        PrepItem& it = pre.item[xi];
-        it.x = pl.xs[xi];
-        it.xb = ws + pl.off_xb[xi];
-        it.colscale = reinterpret_cast<float*>(ws + pl.off_cs[xi]);
-        it.K = pl.xk[xi];
-        it.nb = (pl.xk[xi] + QK - 1) / QK;
-        it.warp_begin = warps;
-        it.pad = 0;
-        warps += m * it.nb;
-    }
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((warps * 32 + 255) / 256);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e;
-    switch (x_dtype) {
-        case 0: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<float, NT, CAP>, pre); break;
-        case 1: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__half, NT, CAP>, pre); break;
-        default: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__nv_bfloat16, NT, CAP>, pre); break;
-    }
-    if (e != cudaSuccess) return e;
-
-    // ---- GEMV launch ----
+template <int NT, int CAP, int XDT>
+cudaError_t launch_gemv_kernel(const GemvLaunch<CAP>& L, const GroupPlan& pl, cudaStream_t stream) {
     static bool attr_set[64] = {};  // per device; an idempotent attribute, so a race is benign
     int dev = 0;
     cudaGetDevice(&dev);
+    cudaError_t e;
     if (dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemv_kernel<NT, CAP>, cudaFuncAttributeMaxDynamicSharedMemorySize, S_::SMEM);
+        e = cudaFuncSetAttribute(gemv_kernel<NT, CAP, XDT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT);
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set[dev] = true;
     }
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = CLUSTER;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pl.clusters * CLUSTER);
+    cfg.blockDim = dim3(GEMV_WARPS * 32);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<NT, CAP, XDT>, L);
+}
+
+template <int NT, int CAP>
+cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
+                             uint8_t* ws, const GroupPlan& pl, cudaStream_t stream) {
+    cudaError_t e;
+    if (!pl.fused) {
+        // ---- prep launch (unique x's) ----
+        PrepLaunch<CAP> pre;
+        pre.count = (uint32_t)pl.xs.size();
+        pre.M = m;
+        uint32_t warps = 0;
+        for (uint32_t xi = 0; xi < pre.count; ++xi) {
+            PrepItem& it = pre.item[xi];
+            it.x = pl.xs[xi];
+            it.xb = ws + pl.off_xb[xi];
+            it.colscale = reinterpret_cast<float*>(ws + pl.off_cs[xi]);
+            it.K = pl.xk[xi];
+            it.nb = (pl.xk[xi] + QK - 1) / QK;
+            it.warp_begin = warps;
+            it.pad = 0;
+            warps += 2u * NT * it.nb;
+        }
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((warps * 32 + 255) / 256);
+        cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        switch (x_dtype) {
+            case 0: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<float, NT, CAP>, pre); break;
+            case 1: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__half, NT, CAP>, pre); break;
+            default: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__nv_bfloat16, NT, CAP>, pre); break;
+        }
+        if (e != cudaSuccess) return e;
+    }
+
+    // ---- GEMV launch ----
     GemvLaunch<CAP> L;
+    memset(&L, 0, sizeof(L));
     L.count = count;
     L.M = m;
-    L.total_steps = pl.total_steps;
-    L.pad = 0;
-    L.partial = reinterpret_cast<float*>(ws + pl.off_partial);
-    L.counters = reinterpret_cast<uint32_t*>(ws + pl.off_counters);
-    uint32_t tb = 0;
+    L.x = probs[0].x;
+    L.K = probs[0].k;
+    L.clusters = pl.clusters;
+    for (uint32_t c = 0; c <= pl.clusters; ++c) L.cl_tb[c] = pl.cl_tb[c];
+    for (uint32_t c = 0; c < pl.clusters; ++c) L.cl_p[c] = pl.cl_p[c];
     for (uint32_t i = 0; i < count; ++i) {
         GemvProblem& P = L.prob[i];
-        const uint32_t nb = (probs[i].k + QK - 1) / QK;
         P.qs = probs[i].qs;
         P.sc = probs[i].sc;
-        P.xb = ws + pl.off_xb[pl.x_of[i]];
-        P.colscale = reinterpret_cast<const float*>(ws + pl.off_cs[pl.x_of[i]]);
+        P.xb = pl.fused ? nullptr : ws + pl.off_xb[pl.x_of[i]];
+        P.colscale = pl.fused ? nullptr : reinterpret_cast<const float*>(ws + pl.off_cs[pl.x_of[i]]);
         P.out = probs[i].out;
         P.N = probs[i].n;
-        P.nb = nb;
-        P.row_groups = (probs[i].n + pl.rows - 1) / pl.rows;
-        P.tb_begin = tb;
-        P.counter_base = pl.counter_base[i];
-        P.pad = 0;
-        tb += P.row_groups * nb;
+        P.nb = pl.nb[i];
+        P.tiles = pl.tiles[i];
+        P.tb_begin = pl.tb_begin[i];
     }
-    cfg.gridDim = dim3(pl.grid);
-    cfg.blockDim = dim3(GEMV_WARPS * 32);
-    cfg.dynamicSmemBytes = S_::SMEM;
-    e = cudaLaunchKernelEx(&cfg, gemv_kernel<NT, CAP>, L);
+    if (!pl.fused) e = launch_gemv_kernel<NT, CAP, -1>(L, pl, stream);
+    else if constexpr (NT <= 2 && CAP == 1) {
+        switch (x_dtype) {
+            case 0: e = launch_gemv_kernel<NT, CAP, 0>(L, pl, stream); break;
+            case 1: e = launch_gemv_kernel<NT, CAP, 1>(L, pl, stream); break;
+            default: e = launch_gemv_kernel<NT, CAP, 2>(L, pl, stream); break;
+        }
+    } else {
+        e = cudaErrorInvalidValue;  // the planner never fuses these
+    }
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -712,7 +899,7 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
 template <int NT>
 cudaError_t launch_group_nt(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
                             uint8_t* ws, const GroupPlan& pl, cudaStream_t stream) {
-    // parameter capacity: a single projection ships ~100 bytes of launch parameters, not 16 KB
+    // parameter capacity: a single projection ships ~1 KB of launch parameters, not 16 KB
     if (count <= 1) return launch_group_cap<NT, 1>(probs, count, m, x_dtype, ws, pl, stream);
     if (count <= 16) return launch_group_cap<NT, 16>(probs, count, m, x_dtype, ws, pl, stream);
     return launch_group_cap<NT, MAX_PROBLEMS>(probs, count, m, x_dtype, ws, pl, stream);
@@ -728,8 +915,9 @@ bool gemv_fast_path_ok(uint32_t m, uint32_t k, const uint8_t* qs, const uint8_t*
 uint32_t gemv_max_group() { return MAX_PROBLEMS; }
 
 size_t gemv_group_workspace_size(const GemvProblemHost* probs, uint32_t count, uint32_t m, int num_sms) {
+    (void)num_sms;
     if (count == 0) return 0;
-    return plan_group(probs, count, m, num_sms).total;
+    return plan_group(probs, count, m, 0).total;
 }
 
 size_t gemv_workspace_size(uint32_t m, uint32_t n, uint32_t k, int num_sms) {
@@ -740,7 +928,7 @@ size_t gemv_workspace_size(uint32_t m, uint32_t n, uint32_t k, int num_sms) {
 cudaError_t launch_gemv_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
                               void* workspace, int num_sms, cudaStream_t stream) {
     if (count == 0) return cudaSuccess;
-    const GroupPlan pl = plan_group(probs, count, m, num_sms);
+    const GroupPlan pl = plan_group(probs, count, m, max_active_clusters(num_sms));
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     switch (pl.nt) {
         case 1: return launch_group_nt<1>(probs, count, m, x_dtype, ws, pl, stream);

@@ -73,7 +73,7 @@ const char* iq2_last_error(void);
 /* IQ2_ABI_VERSION of the loaded library. */
 int iq2_abi_version(void);
 
-/* Bytes of device scratch iq2_matmul needs for this problem (0 is possible). */
+/* Bytes of device scratch iq2_matmul needs for this problem. 0 means none: workspace may then be NULL. */
 size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, int x_dtype,
                                  int variant);
 

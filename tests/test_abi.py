@@ -62,7 +62,8 @@ def test_error_message_is_per_call(lib):
 
 
 def test_workspace_query_needs_no_device(lib):
-    assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 0) > 0
+    assert lib.iq2_matmul_workspace_size(16, 4096, 4096, 0, 0) > 0  # x limbs go through the workspace
+    assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 0) == 0  # small K: limbs made in shared memory
     assert lib.iq2_matmul_workspace_size(0, 4096, 4096, 0, 0) == 0
     assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 1) == 0  # no kernels for other variants
 

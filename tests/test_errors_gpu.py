@@ -62,15 +62,17 @@ def test_other_variants_and_activation_modes():
 
 
 def test_c_abi_workspace_contract():
-    x, qs, sc = _setup(n=1024, k=4096, m=1)
+    # k = 14336 at m = 1: the x limbs go through the workspace (small k needs none)
+    x, qs, sc = _setup(n=1024, k=14336, m=1)
     lib = _lib.load()
     out = torch.empty((1, 1024), device="cuda")
-    need = lib.iq2_matmul_workspace_size(1, 1024, 4096, 0, 0)
+    need = lib.iq2_matmul_workspace_size(1, 1024, 14336, 0, 0)
     assert need > 0
+    assert lib.iq2_matmul_workspace_size(1, 1024, 4096, 0, 0) == 0
     ws = torch.empty(need, dtype=torch.uint8, device="cuda")
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     args = [ctypes.c_void_p(x.data_ptr()), 0, 1, ctypes.c_void_p(qs.data_ptr()), qs.numel(),
-            ctypes.c_void_p(sc.data_ptr()), sc.numel(), 1024, 4096, 0, ctypes.c_void_p(out.data_ptr())]
+            ctypes.c_void_p(sc.data_ptr()), sc.numel(), 1024, 14336, 0, ctypes.c_void_p(out.data_ptr())]
     assert lib.iq2_matmul(*args, None, 0, stream) == _lib.IQ2_ERR_WORKSPACE
     assert lib.iq2_matmul(*args, ctypes.c_void_p(ws.data_ptr()), need - 1, stream) == _lib.IQ2_ERR_WORKSPACE
     assert lib.iq2_matmul(*args, ctypes.c_void_p(ws.data_ptr()), need, stream) == _lib.IQ2_OK
