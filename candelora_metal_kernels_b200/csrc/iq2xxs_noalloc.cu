@@ -11,9 +11,10 @@
 // name is only a host-side stand-in, so its device address is obtained once per device with
 // cudaGetSymbolAddress (with that device current) during the first call on the device and
 // cached; make that first call outside any stream capture. All calls share the one array and it
-// keeps the previous call's contents: the x-limb prep kernel re-zeroes the split-K tickets on
-// every call, and nothing else is read before being written. Calls whose kernels overlap on the
-// GPU (different streams, or different host threads without ordering) race on the array.
+// keeps the previous call's contents. Nothing in it needs to start at zero: the x-limb prep
+// kernel writes every limb and scale before the GEMV reads them, and the GEMV keeps its partial
+// sums in shared memory. Calls whose kernels overlap on the GPU (different streams, or different
+// host threads without ordering) race on the array.
 #include <atomic>
 #include <cstdio>
 #include <mutex>
