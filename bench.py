@@ -128,7 +128,7 @@ class Workload:
             self.x_host[xo:xo + m * k].copy_(x.reshape(-1))
             key = (n_loc, k)
             if key not in ws_cache:  # one workspace per shape is enough: calls are stream-ordered
-                ws_cache[key] = torch.empty(max(workspace_bytes(m, n_loc, k, torch.float32), 1),
+                ws_cache[key] = torch.empty(workspace_bytes(m, n_loc, k, torch.float32),
                                             dtype=torch.uint8, device=device)
             self.calls.append((self.x_dev[xo:xo + m * k].view(m, k), qs, sc, n_loc, k,
                                self.out_dev[oo:oo + m * n_loc].view(m, n_loc), ws_cache[key], name))
@@ -156,8 +156,11 @@ class Workload:
             torch.distributed.all_gather_into_tensor(self.gathered, self.out_dev)
 
     def launches_per_step(self, grouped: bool = False) -> int:
-        # x-limb prep + decode GEMV per call (per 256 projections when grouped)
-        return 2 * ((len(self.calls) + 255) // 256) if grouped else 2 * len(self.calls)
+        # a call is one GEMV launch when it needs no workspace (x limbs made in-kernel), else the
+        # x-limb prep + the GEMV; a grouped call is prep + GEMV per 256 projections
+        if grouped:
+            return 2 * ((len(self.calls) + 255) // 256)
+        return sum(1 if ws.numel() <= 1 else 2 for (_, _, _, _, _, _, ws, _) in self.calls)
 
 
 def _time_graph(graph, steps: int, stream) -> float:
@@ -285,7 +288,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         n_loc, k = big[0][3], big[0][4]
         bytes_per_launch = synth.packed_bytes(n_loc, k)
         achieved = bytes_per_launch / (per_launch_ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "gemv_kernel<1> (+ its x-limb prep), 4096x14336 m=1",
+        roof = {"bound": "hbm", "kernel": "gemv_kernel<1,1,0> (x limbs in-kernel), 4096x14336 m=1, one launch per call",
                 "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peak_src,
                 "us_per_launch": round(per_launch_ms * 1e3, 3), "algorithmic_bytes": bytes_per_launch,
@@ -324,12 +327,14 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
 def _ncu_traffic(bytes_per_launch: int):
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "gemv_kernel_4096x14336_m1.json"
+    p = ROOT / "profiles" / "gemv_kernel_4096x14336_m1.md"
     try:
-        d = json.loads(p.read_text())
-        return d.get("dram_bytes_per_launch")
+        for line in p.read_text().splitlines():
+            if line.startswith("dram_bytes_per_launch:"):
+                return int(line.split(":")[1])
     except Exception:
-        return None
+        pass
+    return None
 
 
 # ---------------------------------------------------------------------------------------- GEMM
@@ -436,6 +441,34 @@ def run_reference(args, rank: int, world: int):
             "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ---------------------------------------------------------------------------------------- cases
+def run_case(args):
+    """Only the dominant kernel on its roofline shape, `--steps` times after two warm calls: the
+    command the profiler captures. gemv: 4096x14336 (K x N) at M=1, f32 x, two weight copies
+    (30 MB) in turn; gemm: M=2048 on the same projection, bf16 x."""
+    import candelora_metal_kernels_b200 as c
+    from candelora_metal_kernels_b200 import synth
+    torch.cuda.set_device(0)
+    n, k = 14336, 4096
+    m = 1 if args.case == "gemv" else 2048
+    dtype = torch.float32 if args.case == "gemv" else torch.bfloat16
+    ws_ = [tuple(t.cuda() for t in synth.iq2xxs_weights(n, k, seed=i)) for i in range(2)]
+    x = synth.activations(m, k, seed=1, dtype=dtype, device="cuda")
+    out = torch.empty(m, n, device="cuda")
+    ws = torch.empty(c.workspace_bytes(m, n, k, dtype), dtype=torch.uint8, device="cuda")
+    for i in range(2):
+        c.iq2_xxs_matmul(x, ws_[i % 2][0], ws_[i % 2][1], n, k, out=out, workspace=ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        c.iq2_xxs_matmul(x, ws_[i % 2][0], ws_[i % 2][1], n, k, out=out, workspace=ws)
+    e1.record()
+    e1.synchronize()
+    print(json.dumps({"case": args.case, "m": m, "k": k, "n": n, "calls": args.steps,
+                      "us_per_call": round(e0.elapsed_time(e1) * 1e3 / args.steps, 2)}), flush=True)
+
+
 # ---------------------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -448,7 +481,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--gemm-reps", type=int, default=5)
+    ap.add_argument("--case", choices=["gemv", "gemm"], default=None,
+                    help="run only the dominant kernel's shape (the profiler's small case) and exit")
     args = ap.parse_args()
+    if args.case:
+        run_case(args)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

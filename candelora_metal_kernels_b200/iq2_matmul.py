@@ -118,15 +118,19 @@ def _matmul(x, weight_bytes, weight_scales, out_dim, in_dim, variant, act_mode=_
             _bail(_lib.IQ2_ERR_INVALID_ARGUMENT, f"{op}: out must be a contiguous f32 [{m}, {out_dim}] tensor "
                                                  f"on {x.device}")
     ws_need = workspace_bytes(m, out_dim, in_dim, x2.dtype, Iq2MatmulVariant(int(variant))) if m else 0
-    if workspace is None or workspace.numel() < ws_need:
-        workspace = torch.empty(max(ws_need, 1), dtype=torch.uint8, device=x.device)
+    if ws_need == 0:
+        ws_ptr, ws_len = None, 0  # this call needs no scratch at all
+    else:
+        if workspace is None or workspace.numel() < ws_need:
+            workspace = torch.empty(ws_need, dtype=torch.uint8, device=x.device)
+        ws_ptr, ws_len = workspace.data_ptr(), workspace.numel()
     with torch.cuda.device(x.device):
         rc = lib.iq2_matmul_with_activation_quant(
             ctypes.c_void_p(x2.data_ptr()), _X_DTYPES[x2.dtype], m,
             ctypes.c_void_p(weight_bytes.data_ptr()), weight_bytes.numel(),
             ctypes.c_void_p(weight_scales.data_ptr()), weight_scales.numel(),
             out_dim, in_dim, int(variant), act_mode, int(bool(strict)),
-            ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(workspace.data_ptr()), workspace.numel(),
+            ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(ws_ptr), ws_len,
             _stream_handle(x.device))
     _lib.check(rc)
     return out.squeeze(0) if squeeze else out
