@@ -12,9 +12,11 @@
 //     bf16 sign bits by one multiply). This is bit-identical to rounding every weight's exact f32
 //     value (the dequant kernel's bf16). Tables are kept small (2 KB + 128 B) because the tensor
 //     core reads its operands through the same shared memory.
-//   * D: two 128 x 256 f32 accumulators in TMEM (all 512 columns): one CTA computes a tile of 256
-//     tokens x 256 weight rows, issuing per 64-k stage 2 x 4 tcgen05.mma (M=128, N=256, K=16)
-//     from one thread; tcgen05.commit frees each stage when the tensor core has read it.
+//   * D: two 128 x BN f32 accumulators in TMEM (512 columns allocated): one CTA computes a tile of
+//     256 tokens x BN weight rows (BN = 256, or 224 when that leaves fewer SMs idle in the last
+//     wave, e.g. 512 tiles instead of 448 on 148 SMs for N = 14336), issuing per 64-k stage
+//     2 x 4 tcgen05.mma (M=128, N=BN, K=16) from one thread; tcgen05.commit frees each stage when
+//     the tensor core has read it.
 //   * Pipeline: 3 stages of 64 KB, mbarriers for "x landed" (TMA transaction bytes), "weights
 //     written" (decode warps) and "stage free" (MMA commit). Every wait is bounded: on timeout
 //     the kernel records an error code, stops issuing work and still frees its TMEM.
@@ -32,7 +34,7 @@ namespace iq2 {
 namespace {
 
 constexpr int G_BM = 256;                       // tokens per CTA (two M=128 MMAs)
-constexpr int G_BN = 256;                       // weight rows per CTA (MMA N)
+constexpr int G_BN = 256;                       // weight rows per CTA (MMA N), at most; BN = 224 also used
 constexpr int G_BK = 64;                        // k per stage (one 128-byte swizzle row of bf16)
 constexpr int G_STAGES = 3;
 constexpr int G_DEC_WARPS = 16;                 // decode warps = epilogue warps
@@ -48,9 +50,11 @@ constexpr int G_SMEM = 1024 /*align*/ + G_STAGES * G_STAGE_BYTES + G_SEL_BYTES +
 constexpr uint32_t G_TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: only a broken pipeline waits that long
 
-// Instruction descriptor, kind::f16: F32 accumulate, BF16 A and B, both K-major, M=128, N=256.
-constexpr uint32_t G_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(G_BN >> 3) << 17) |
-                             ((uint32_t)(128 >> 4) << 24);
+// Instruction descriptor, kind::f16: F32 accumulate, BF16 A and B, both K-major, M=128, N=BN.
+template <int BN>
+constexpr uint32_t idesc_for() {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
 
 struct GemmParams {
     const uint8_t* qs;
@@ -164,8 +168,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 }
 
 // ---- the kernel ----
+// BN: weight rows per CTA (256, or 224 where that fills the last wave better); the stage
+// layout is always sized for 256 rows.
+template <int BN>
 __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                             const GemmParams p) {
+    static_assert(BN % 32 == 0 && BN <= G_BN, "BN");
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_s = smem_u32(smem_raw);
     const uint32_t base_s = (raw_s + 1023u) & ~1023u;  // SW128 tiles need 1024-byte alignment
@@ -182,7 +190,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
     volatile uint32_t* abort_flag = tmem_addr_word + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t n0 = blockIdx.x * G_BN, m0 = blockIdx.y * G_BM;
+    const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * G_BM;
     const uint32_t KT = (p.K + G_BK - 1) / G_BK;
 
     // decode tables -> shared memory: per grid entry the four 16-bit prmt selectors packed in two
@@ -248,8 +256,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
                 for (int ks = 0; ks < G_BK / 16; ++ks) {
                     const uint64_t bd = sw128_desc(b_s + ks * 32);
                     const uint32_t acc = (kt | ks) ? 1u : 0u;
-                    tc_mma(tmem, sw128_desc(a_s + ks * 32), bd, G_IDESC, acc);
-                    tc_mma(tmem + 256, sw128_desc(a_s + G_A_HALF + ks * 32), bd, G_IDESC, acc);
+                    tc_mma(tmem, sw128_desc(a_s + ks * 32), bd, idesc_for<BN>(), acc);
+                    tc_mma(tmem + 256, sw128_desc(a_s + G_A_HALF + ks * 32), bd, idesc_for<BN>(), acc);
                 }
                 tc_commit(empty(s));  // the stage is free once these MMAs have read it
             }
@@ -260,7 +268,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
         // thread = (tile row r, sub-block h of the stage's two)
         const uint32_t r = threadIdx.x & 255u, hh = threadIdx.x >> 8;
         const uint32_t row = n0 + r;
-        const bool rok = row < p.N;
+        const bool rok = r < (uint32_t)BN && row < p.N;  // rows past BN: zeros the MMA never reads
         const uint8_t* qrow = p.qs + (size_t)(rok ? row : 0) * p.nb * QS_BYTES;
         const uint8_t* srow = p.sc + (size_t)(rok ? row : 0) * p.nb * SC_BYTES;
         const uint32_t row_swz = r & 7u;
@@ -331,7 +339,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
             float* orow = p.out + (size_t)token * p.N;
             const bool vec = (p.N % 4) == 0;
 #pragma unroll 1
-            for (int c = chalf * (G_BN / 64); c < (chalf + 1) * (G_BN / 64); ++c) {
+            for (int c = (int)chalf; c < BN / 32; c += 2) {
                 uint32_t v[32];
                 tmem_ld32(tmem + ((quad * 32u) << 16) + acc * 256u + c * 32u, v);
                 if (token < p.M) {
@@ -409,7 +417,6 @@ size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype) {
 
 cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc, uint32_t n,
                         uint32_t k, float* out, void* workspace, int num_sms, cudaStream_t stream) {
-    (void)num_sms;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     uint32_t* err = reinterpret_cast<uint32_t*>(ws);
     cudaError_t e = cudaMemsetAsync(err, 0, 4, stream);
@@ -438,7 +445,9 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+        e = cudaFuncSetAttribute(gemm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_kernel<224>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set[dev] = true;
     }
@@ -451,8 +460,18 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     p.N = n;
     p.K = k;
     p.nb = (k + QK - 1) / QK;
-    dim3 grid((n + G_BN - 1) / G_BN, (m + G_BM - 1) / G_BM);
-    gemm_kernel<<<grid, G_THREADS, G_SMEM, stream>>>(map, p);
+    // the tile width whose last wave of CTAs (one per SM) is fullest
+    const int sms = num_sms > 0 ? num_sms : 148;
+    auto wave_fill = [&](uint32_t bn) {
+        const uint64_t tiles = (uint64_t)((n + bn - 1) / bn) * ((m + G_BM - 1) / G_BM);
+        const uint64_t waves = (tiles + sms - 1) / sms;
+        return (double)tiles / (double)(waves * sms);
+    };
+    const bool narrow = wave_fill(224) > wave_fill(256) + 0.02;
+    const uint32_t bn = narrow ? 224u : 256u;
+    dim3 grid((n + bn - 1) / bn, (m + G_BM - 1) / G_BM);
+    if (narrow) gemm_kernel<224><<<grid, G_THREADS, G_SMEM, stream>>>(map, p);
+    else gemm_kernel<256><<<grid, G_THREADS, G_SMEM, stream>>>(map, p);
     return cudaGetLastError();
 }
 
