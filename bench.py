@@ -1,25 +1,28 @@
 #!/usr/bin/env python3
 """Benchmark: IQ2_XXS matmul weight GB/s at M=1 (decode GEMV) on Llama-3-8B-shaped projections.
 
-Workload (benchmark configuration 1 at M=1): the 7 projections of a Llama-3-8B layer
-(q 4096x4096, k/v 4096x1024, o 4096x4096, gate/up 4096x14336, down 14336x4096; K x N), IQ2_XXS
-weights with the benchmark block distribution, f32 N(0,1) activations, repeated over 32
-distinct layers (1.80 GB of packed weights, > 14x the 126 MB L2, so no step reads weights from
-L2). One step = the 224 projections, each through the library's public call. Synthetic data.
+Workload (benchmark configuration 1, "batched decode GEMV", at M=1): the 7 projections of a
+Llama-3-8B layer (q 4096x4096, k/v 4096x1024, o 4096x4096, gate/up 4096x14336, down 14336x4096;
+K x N), IQ2_XXS weights with the benchmark block distribution, f32 N(0,1) activations, repeated
+over 32 distinct layers (1.80 GB of packed weights, > 14x the 126 MB L2, so no step reads weights
+from L2). Synthetic data.
 
-  value   = packed weight bytes per step / device time per step (CUDA events on the launch stream
-            around K back-to-back replays of a CUDA graph holding one step; inputs resident)
-  e2e     = the same metric, each step also copying every projection's x host->device from
-            pinned memory and every output device->host (stream-ordered, inside the timed region)
-  roofline: the dominant kernel (the decode GEMV of a 4096x14336 gate/up projection) timed alone
-            with CUDA events (64 distinct matrices in rotation, > L2), against measured HBM BW.
+  value    = packed weight bytes per step / device time per step, the step being all 224
+             projections in one batched call (iq2_matmul_grouped; CUDA events on the launch
+             stream around K back-to-back replays of a CUDA graph holding one step; inputs resident)
+  per_call = the same step as 224 reference-shaped iq2_xxs_matmul calls
+  e2e      = the per-call step through the public API with every projection's x copied host->device
+             from pinned memory and every output device->host inside the timed region
+  roofline: the dominant kernel (the decode GEMV of a 4096x14336 gate/up projection, one call)
+            timed alone with CUDA events (64 distinct matrices in rotation, > L2), against measured HBM.
   cpu_baseline: the reference's own kernels (compiled from source for the host, all threads) on
             a bounded sample of the same workload.
 
---gpus N > 1 (launched by torchrun, one rank per GPU): every projection is column-sharded over
-the N ranks (rank r computes output columns [r*N/g, (r+1)*N/g) from its contiguous slice of the
-weight rows), and the output slices of the step are all-gathered with NCCL over NVLink and put
-back in [m, N] order -- strong scaling of the same workload; value = whole-job weight bytes/s.
+--gpus N > 1 (launched by torchrun, one rank per GPU): every projection is column-sharded over the
+N ranks (rank r holds weight rows [r*N/g, (r+1)*N/g), a contiguous slice), and every rank ends
+with the full outputs through NCCL all-gathers over NVLink (one per step in the batched call, one
+per projection in the per-call path) -- strong scaling of the same workload; value = whole-job
+weight bytes/s, the max over ranks of the device time.
 
 --impl reference: the reference's own kernels on the host cores (see above), same metric.
 """
@@ -99,22 +102,20 @@ class ClockSampler:
 class Workload:
     """Device-resident weights, inputs, outputs and workspaces of one step, optionally sharded."""
 
-    def __init__(self, m: int, layers: int, rank: int, world: int, device: torch.device):
-        from candelora_metal_kernels_b200 import synth, workspace_bytes
-        self.m, self.device, self.rank, self.world = m, device, rank, world
-        self.calls = []  # (x_view, qs, sc, n_local, k, out_view, ws)
+    def __init__(self, m: int, layers: int, rank: int, world: int, device: torch.device, comm=None):
+        from candelora_metal_kernels_b200 import grouped_workspace_bytes, synth, workspace_bytes
+        from candelora_metal_kernels_b200.sharded import sharded_workspace_bytes
+        self.m, self.device, self.rank, self.world, self.comm = m, device, rank, world, comm
+        self.calls = []  # (x_view, qs, sc, n, k, out_view, ws, name): qs/sc = this rank's row slice
         self.weight_bytes = 0        # whole-job packed bytes per step
-        self.local_weight_bytes = 0
         x_elems = out_elems = 0
         specs = []
         for layer in range(layers):
             for pi, (name, k, n) in enumerate(synth.LLAMA3_8B_PROJECTIONS):
-                n_loc = n // world
-                specs.append((layer, pi, name, k, n, n_loc, x_elems, out_elems))
+                specs.append((layer, pi, name, k, n, n // world, x_elems, out_elems))
                 x_elems += m * k
-                out_elems += m * n_loc
+                out_elems += m * n  # every rank ends with the full outputs
                 self.weight_bytes += synth.packed_bytes(n, k)
-                self.local_weight_bytes += synth.packed_bytes(n_loc, k)
         self.x_dev = torch.empty(x_elems, dtype=torch.float32, device=device)
         self.out_dev = torch.empty(out_elems, dtype=torch.float32, device=device)
         self.x_host = torch.empty(x_elems, dtype=torch.float32, pin_memory=True)
@@ -126,41 +127,50 @@ class Workload:
                                           row_end=(rank + 1) * n_loc)
             x = synth.activations(m, k, seed=10_000 + seed)
             self.x_host[xo:xo + m * k].copy_(x.reshape(-1))
-            key = (n_loc, k)
+            xv = self.x_dev[xo:xo + m * k].view(m, k)
+            key = (n, k)
             if key not in ws_cache:  # one workspace per shape is enough: calls are stream-ordered
-                ws_cache[key] = torch.empty(workspace_bytes(m, n_loc, k, torch.float32),
-                                            dtype=torch.uint8, device=device)
-            self.calls.append((self.x_dev[xo:xo + m * k].view(m, k), qs, sc, n_loc, k,
-                               self.out_dev[oo:oo + m * n_loc].view(m, n_loc), ws_cache[key], name))
+                need = (workspace_bytes(m, n, k, torch.float32) if world == 1
+                        else sharded_workspace_bytes(comm, [(xv, qs, sc, n, k)]))
+                ws_cache[key] = torch.empty(need, dtype=torch.uint8, device=device)
+            self.calls.append((xv, qs, sc, n, k, self.out_dev[oo:oo + m * n].view(m, n), ws_cache[key], name))
         self.x_dev.copy_(self.x_host)
-        self.gathered = None
-        if world > 1:
-            self.gathered = torch.empty(world * out_elems, dtype=torch.float32, device=device)
-            self.full_out = torch.empty(world * out_elems, dtype=torch.float32, device=device)
-
-        from candelora_metal_kernels_b200 import grouped_workspace_bytes
         self.problems = [(x, qs, sc, n, k, out) for (x, qs, sc, n, k, out, _, _) in self.calls]
-        self.grouped_ws = torch.empty(max(grouped_workspace_bytes(self.problems), 1), dtype=torch.uint8,
-                                      device=device)
+        need = (grouped_workspace_bytes(self.problems) if world == 1
+                else sharded_workspace_bytes(comm, self.problems))
+        self.grouped_ws = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
 
     def step(self, grouped: bool = False):
-        """One step: every projection through iq2_xxs_matmul (the reference-shaped call), or all of
-        them through one iq2_matmul_grouped call."""
+        """One step: every projection through the per-projection call (iq2_xxs_matmul, the
+        reference-shaped call; column-sharded with one all-gather per call on N > 1 GPUs), or all
+        of them through one grouped call (one all-gather per step on N > 1 GPUs)."""
         from candelora_metal_kernels_b200 import iq2_matmul_grouped, iq2_xxs_matmul
-        if grouped:
-            iq2_matmul_grouped(self.problems, workspace=self.grouped_ws)
+        from candelora_metal_kernels_b200.sharded import iq2_matmul_grouped_sharded, iq2_matmul_sharded
+        if self.world == 1:
+            if grouped:
+                iq2_matmul_grouped(self.problems, workspace=self.grouped_ws)
+            else:
+                for (x, qs, sc, n, k, out, ws, _) in self.calls:
+                    iq2_xxs_matmul(x, qs, sc, n, k, out=out, workspace=ws)
+        elif grouped:
+            iq2_matmul_grouped_sharded(self.comm, self.problems, workspace=self.grouped_ws)
         else:
             for (x, qs, sc, n, k, out, ws, _) in self.calls:
-                iq2_xxs_matmul(x, qs, sc, n, k, out=out, workspace=ws)
-        if self.world > 1:
-            torch.distributed.all_gather_into_tensor(self.gathered, self.out_dev)
+                iq2_matmul_sharded(self.comm, x, qs, sc, n, k, out=out, workspace=ws)
 
     def launches_per_step(self, grouped: bool = False) -> int:
-        # a call is one GEMV launch when it needs no workspace (x limbs made in-kernel), else the
-        # x-limb prep + the GEMV; a grouped call is prep + GEMV per 256 projections
+        """This library's kernels per step (NCCL's all-gather kernels not counted): a GEMV launch,
+        plus the x-limb prep when the call has a workspace for it (per 256 projections when
+        grouped), plus on N > 1 GPUs the scatter kernel (not needed for one projection at m = 1)."""
+        from candelora_metal_kernels_b200 import workspace_bytes
         if grouped:
-            return 2 * ((len(self.calls) + 255) // 256)
-        return sum(1 if ws.numel() <= 1 else 2 for (_, _, _, _, _, _, ws, _) in self.calls)
+            return 2 * ((len(self.calls) + 255) // 256) + (1 if self.world > 1 else 0)
+        total = 0
+        for (_, _, _, n, k, _, _, _) in self.calls:
+            total += 1 if workspace_bytes(self.m, n // self.world, k, torch.float32) == 0 else 2
+            if self.world > 1 and self.m > 1:
+                total += 1
+        return total
 
 
 def _time_graph(graph, steps: int, stream) -> float:
@@ -182,7 +192,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     from candelora_metal_kernels_b200 import synth
     c._lib.load()
     dist = world > 1
-    wl = Workload(args.m, args.layers, rank, world, device)
+    comm = None
+    if dist:
+        from candelora_metal_kernels_b200.sharded import Iq2Comm
+        comm = Iq2Comm()  # the library's NCCL communicator; the NCCL process group carries its id
+    wl = Workload(args.m, args.layers, rank, world, device, comm)
     stream = torch.cuda.Stream(device)
     torch.cuda.synchronize()
 
@@ -204,51 +218,55 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         wl.step(grouped=True)
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
-            graph.replay()
+            ggraph.replay()
     torch.cuda.synchronize()
 
-    # ---- timed region: K steps, barrier + sync on both sides, max over ranks
+    def max_over_ranks(ms: float) -> float:
+        if not dist:
+            return ms
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- timed region (value): K steps of the batched call, barrier + sync on both sides, max over ranks
     if dist:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     with ClockSampler(device.index) as clocks:
-        ms = _time_graph(graph, args.steps, stream)
+        ms = _time_graph(ggraph, args.steps, stream)
         # keep sampling a little longer when the timed region is shorter than a sample period
-        if ms < 300:
-            _time_graph(graph, max(1, int(args.steps * 300 / max(ms, 1e-3))), stream)
+        # (every rank replays the same number of times: the step holds collectives)
+        extra = torch.tensor([max(1, int(args.steps * 300 / max(ms, 1e-3))) if ms < 300 else 0], device=device)
+        if dist:
+            torch.distributed.all_reduce(extra, op=torch.distributed.ReduceOp.MAX)
+        if int(extra.item()) > 0:
+            _time_graph(ggraph, int(extra.item()), stream)
     torch.cuda.synchronize()
     if dist:
         torch.distributed.barrier()
-        t = torch.tensor([ms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms)
     ms_per_step = ms / args.steps
     value = wl.weight_bytes / (ms_per_step * 1e-3) / 1e9
+
+    # ---- the same step as 224 reference-shaped per-projection calls, inputs resident
     with torch.cuda.stream(stream):
         for _ in range(3):
-            ggraph.replay()
+            graph.replay()
     if dist:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    gms = _time_graph(ggraph, args.steps, stream)
-    if dist:
-        t = torch.tensor([gms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        gms = float(t.item())
-    grouped = {"value": round(wl.weight_bytes / (gms / args.steps * 1e-3) / 1e9, 2), "unit": "GB/s",
-               "ms_per_step": round(gms / args.steps, 4),
-               "path": "the same 224 projections in one iq2_matmul_grouped call per step",
-               "gpu_launches": wl.launches_per_step(True) * args.steps}
+    pms = max_over_ranks(_time_graph(graph, args.steps, stream))
+    per_call = {"value": round(wl.weight_bytes / (pms / args.steps * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(pms / args.steps, 4),
+                "path": ("224 iq2_xxs_matmul calls per step" if not dist else
+                         "224 column-sharded calls per step, one all-gather each"),
+                "gpu_launches": wl.launches_per_step(False) * args.steps}
 
     # ---- end to end: host x -> device, the step through the public API, outputs -> host
     def e2e_step():
         wl.x_dev.copy_(wl.x_host, non_blocking=True)
         graph.replay()
-        if dist:
-            wl.full_out.copy_(wl.gathered)
-            wl.out_host.copy_(wl.out_dev, non_blocking=True)
-        else:
-            wl.out_host.copy_(wl.out_dev, non_blocking=True)
+        wl.out_host.copy_(wl.out_dev, non_blocking=True)
 
     with torch.cuda.stream(stream):
         for _ in range(3):
@@ -263,32 +281,31 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             e2e_step()
         s1.record(stream)
     s1.synchronize()
-    e2e_ms = s0.elapsed_time(s1)
-    if dist:
-        t = torch.tensor([e2e_ms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(s0.elapsed_time(s1))
     e2e_value = wl.weight_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
 
     # ---- roofline of the dominant kernel: 4096x14336 decode GEMV alone, 64 matrices in rotation
     peaks, peak_src = _peaks()
     roof = None
     if rank == 0:
+        # single-GPU calls on this rank's rows (all of them on one GPU)
         big = [cl for cl in wl.calls if cl[7] in ("gate", "up")]
+        n_loc, k = big[0][3] // world, big[0][4]
+        out1 = torch.empty(args.m, n_loc, device=device)
+        ws1 = torch.empty(c.workspace_bytes(args.m, n_loc, k, torch.float32), dtype=torch.uint8, device=device)
         g2 = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g2, stream=stream):
             for (x, qs, sc, n, k, out, ws, _) in big:
-                c.iq2_xxs_matmul(x, qs, sc, n, k, out=out, workspace=ws)
+                c.iq2_xxs_matmul(x, qs, sc, n // world, k, out=out1, workspace=ws1)
         with torch.cuda.stream(stream):
             for _ in range(3):
                 g2.replay()
         reps = max(3, args.steps // 4)
         ms_big = _time_graph(g2, reps, stream)
         per_launch_ms = ms_big / (reps * len(big))
-        n_loc, k = big[0][3], big[0][4]
         bytes_per_launch = synth.packed_bytes(n_loc, k)
         achieved = bytes_per_launch / (per_launch_ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "gemv_kernel<1,1,0> (x limbs in-kernel), 4096x14336 m=1, one launch per call",
+        roof = {"bound": "hbm", "kernel": f"gemv_kernel<1,1,0> (x limbs in-kernel), 4096x{n_loc} m=1, one launch per call",
                 "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peak_src,
                 "us_per_launch": round(per_launch_ms * 1e3, 3), "algorithmic_bytes": bytes_per_launch,
@@ -296,6 +313,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         del g2
 
     del graph, ggraph
+    if comm is not None:
+        torch.cuda.synchronize()
+        comm.close()
     line = None
     if rank == 0:
         line = {
@@ -308,13 +328,18 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                        "weight_bytes_per_step": wl.weight_bytes,
                        "parallelism": f"column-shard over {world} GPUs + NCCL all-gather" if world > 1 else "1 GPU",
                        "l2": "no flush needed: 1.80 GB of distinct weights per step vs 126 MB L2",
+                       "step": ("the 224 projections in one iq2_matmul_grouped call" if world == 1 else
+                                "the 224 projections column-sharded in one iq2_matmul_grouped_sharded call "
+                                "(one NCCL all-gather per step)"),
                        "timing": "CUDA events around K replays of a CUDA graph of one step"},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": wl.x_host.numel() * 4,
                     "d2h_bytes_per_step": wl.out_host.numel() * 4,
-                    "path": "pinned host x -> device, 224 public-API calls, outputs -> pinned host"},
-            "gpu_launches": wl.launches_per_step() * args.steps,
-            "grouped": grouped,
+                    "path": ("pinned host x -> device, 224 reference-shaped iq2_matmul calls"
+                             + (" (column-sharded, one all-gather each)" if dist else "")
+                             + ", outputs -> pinned host")},
+            "gpu_launches": wl.launches_per_step(True) * args.steps,
+            "per_call": per_call,
             "clocks": clocks.summary(),
             "roofline": roof,
         }

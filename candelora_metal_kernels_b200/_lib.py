@@ -21,6 +21,8 @@ IQ2_ERR_TOO_SMALL = 6
 IQ2_ERR_UNSUPPORTED = 7
 IQ2_ERR_WORKSPACE = 8
 IQ2_ERR_CUDA = 9
+IQ2_ERR_COMM = 10
+IQ2_COMM_ID_BYTES = 128
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 ACT_QUANT_OFF, ACT_QUANT_W8A8, ACT_QUANT_W4A8 = 0, 1, 2
@@ -39,6 +41,11 @@ SIGNATURES = {
     "iq2_matmul_noalloc": ([_vp, _int, _u32, _vp, _sz, _vp, _sz, _u32, _u32, _vp, _vp], _int),
     "iq2_dequantize": ([_vp, _sz, _vp, _sz, _u32, _u32, _int, _vp, _int, _vp], _int),
     "iq2_gather_columns": ([_vp, _u32, _u32, _u32, _vp, _vp], _int),
+    "iq2_comm_unique_id": ([_vp], _int),
+    "iq2_comm_init": ([_vp, _int, _int, _vp], _int),
+    "iq2_comm_destroy": ([_vp], _int),
+    "iq2_matmul_grouped_sharded_workspace_size": ([_vp, _u32, _u32, _int, _int], _sz),
+    "iq2_matmul_grouped_sharded": ([_vp, _vp, _u32, _u32, _int, _vp, _sz, _vp], _int),
 }
 
 

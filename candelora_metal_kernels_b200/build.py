@@ -18,7 +18,8 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libcandelora_iq2.so"
-SOURCES = ["iq2xxs_capi.cu", "iq2xxs_gemv.cu", "iq2xxs_gemm.cu", "iq2xxs_dequant.cu", "iq2xxs_noalloc.cu"]
+SOURCES = ["iq2xxs_capi.cu", "iq2xxs_gemv.cu", "iq2xxs_gemm.cu", "iq2xxs_dequant.cu", "iq2xxs_noalloc.cu",
+           "iq2xxs_sharded.cu"]
 HEADERS = ["iq2xxs_common.cuh", "iq2xxs_codebook.h", "iq2xxs_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -66,7 +67,7 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     if failed:
         raise RuntimeError("nvcc failed:\n" + "\n".join(failed))
     tmp = LIB.with_suffix(".so.tmp")
-    link = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs)]
+    link = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs), "-lnccl"]
     subprocess.run(link, check=True)
     os.replace(tmp, LIB)
     return LIB

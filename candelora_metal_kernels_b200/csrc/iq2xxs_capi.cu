@@ -252,6 +252,11 @@ int capi_fail(int code, const char* fmt, ...) {
 
 int capi_cuda_fail(const char* what, cudaError_t e) { return cuda_fail(what, e); }
 
+int capi_ok() {
+    g_last_error.clear();
+    return IQ2_OK;
+}
+
 int capi_num_sms() { return num_sms_for_current_device(); }
 
 // The checks iq2_matmul makes before choosing a kernel (clears the thread's error message first).

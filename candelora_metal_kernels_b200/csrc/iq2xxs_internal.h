@@ -39,9 +39,10 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
                         uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,
                         cudaStream_t stream);
 
-// C ABI helpers (iq2xxs_capi.cu) used by the no-allocation entry point (iq2xxs_noalloc.cu).
+// C ABI helpers (iq2xxs_capi.cu) used by iq2xxs_noalloc.cu and iq2xxs_sharded.cu.
 int capi_fail(int code, const char* fmt, ...);
 int capi_cuda_fail(const char* what, cudaError_t e);
+int capi_ok();  // clears the thread's error message
 int capi_num_sms();
 int capi_validate_matmul(const char* op, const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
                          size_t weight_bytes_len, const uint8_t* weight_scales, size_t weight_scales_len,

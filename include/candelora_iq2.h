@@ -49,7 +49,8 @@ enum iq2_status {
     IQ2_ERR_TOO_SMALL = 6,        /* "weight_bytes too small" / "weight_scales too small" :246-259  */
     IQ2_ERR_UNSUPPORTED = 7,      /* W4A8 in strict mode :300-302, :581-589; variant not built      */
     IQ2_ERR_WORKSPACE = 8,        /* workspace NULL or smaller than the *_workspace_size query      */
-    IQ2_ERR_CUDA = 9              /* a CUDA runtime call failed                                     */
+    IQ2_ERR_CUDA = 9,             /* a CUDA runtime call failed                                     */
+    IQ2_ERR_COMM = 10             /* an NCCL call of the sharded path failed                        */
 };
 
 /* Activation dtypes (the reference dispatches on x.dtype(), src/iq2_matmul.rs:59-75). */
@@ -165,6 +166,32 @@ int iq2_dequantize(const uint8_t* weight_bytes, size_t weight_bytes_len,
  */
 int iq2_gather_columns(const float* gathered, uint32_t shards, uint32_t m, uint32_t shard_cols,
                        float* out, iq2_stream_t stream);
+
+/*
+ * Column sharding over the GPUs of one node (no reference counterpart: the reference is
+ * single-device; this is the multi-GPU layout the benchmark specification asks for). Rank r of a
+ * world of g holds rows [r*N/g, (r+1)*N/g) of each projection's weights, a contiguous slice of
+ * both weight tensors (weight_bytes from byte r*(N/g)*ceil(K/256)*64, weight_scales from byte
+ * r*(N/g)*ceil(K/256)*2); every rank gets the full [m, N] output through one NCCL all-gather.
+ * One process per GPU: rank 0 makes the id, every rank passes the same id to iq2_comm_init with
+ * its own device current.
+ */
+#define IQ2_COMM_ID_BYTES 128
+typedef struct iq2_comm_s* iq2_comm_t;
+int iq2_comm_unique_id(uint8_t* id /* IQ2_COMM_ID_BYTES */);
+int iq2_comm_init(const uint8_t* id, int world, int rank, iq2_comm_t* comm);
+int iq2_comm_destroy(iq2_comm_t comm);
+
+/* Workspace for iq2_matmul_grouped_sharded: the problems describe the rank's slices, with
+ * out_dim the full N (a multiple of world) and out the full [m, N] output. */
+size_t iq2_matmul_grouped_sharded_workspace_size(const iq2_matmul_problem* problems, uint32_t count,
+                                                 uint32_t m, int x_dtype, int world);
+/* Up to 256 projections: their slices through one grouped call, one ncclAllGather of all of them
+ * on `stream`, one scatter kernel into the outputs. Stream-ordered, collective: every rank makes
+ * the same call with the same shapes. */
+int iq2_matmul_grouped_sharded(iq2_comm_t comm, const iq2_matmul_problem* problems, uint32_t count,
+                               uint32_t m, int x_dtype, void* workspace, size_t workspace_bytes,
+                               iq2_stream_t stream);
 
 #ifdef __cplusplus
 }
