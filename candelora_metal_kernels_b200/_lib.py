@@ -36,6 +36,7 @@ SIGNATURES = {
     "iq2_matmul": ([_vp, _int, _u32, _vp, _sz, _vp, _sz, _u32, _u32, _int, _vp, _vp, _sz, _vp], _int),
     "iq2_matmul_with_activation_quant": (
         [_vp, _int, _u32, _vp, _sz, _vp, _sz, _u32, _u32, _int, _int, _int, _vp, _vp, _sz, _vp], _int),
+    "iq2_matmul_with_activation_quant_workspace_size": ([_u32, _u32, _u32, _int, _int, _int], _sz),
     "iq2_matmul_grouped_workspace_size": ([_vp, _u32, _u32, _int], _sz),
     "iq2_matmul_grouped": ([_vp, _u32, _u32, _int, _vp, _sz, _vp], _int),
     "iq2_matmul_noalloc": ([_vp, _int, _u32, _vp, _sz, _vp, _sz, _u32, _u32, _vp, _vp], _int),

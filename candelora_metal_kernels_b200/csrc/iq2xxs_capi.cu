@@ -317,8 +317,31 @@ int iq2_matmul_with_activation_quant(const void* x, int x_dtype, uint32_t m,
     switch (act_mode) {
         case IQ2_ACT_QUANT_OFF:
             break;
-        case IQ2_ACT_QUANT_W8A8:
-            return fail(IQ2_ERR_UNSUPPORTED, "W8A8 kernel path is not implemented in this build");
+        case IQ2_ACT_QUANT_W8A8: {
+            // the reference's W8A8 kernels (src/iq2_matmul.rs:572-580 -> iq2_matmul.metal:437-499):
+            // each x row quantised to int8 and back, then the float matmul of those values
+            const char* op = "iq2_matmul";
+            int rc = check_args(op, out_dim, in_dim, variant);
+            if (rc != IQ2_OK) return rc;
+            if (variant != IQ2_VARIANT_IQ2_XXS)
+                return matmul_impl(op, x, x_dtype, m, weight_bytes, weight_bytes_len, weight_scales,
+                                   weight_scales_len, out_dim, in_dim, variant, out, workspace, workspace_bytes,
+                                   stream);  // reports the missing variant like the Off path
+            rc = iq2::capi_validate_matmul(op, x, x_dtype, m, weight_bytes, weight_bytes_len, weight_scales,
+                                           weight_scales_len, out_dim, in_dim, out);
+            if (rc != IQ2_OK || m == 0) return rc;
+            const size_t xq_bytes = ((size_t)m * in_dim * sizeof(float) + 255) / 256 * 256;
+            const size_t need = xq_bytes + workspace_for(m, out_dim, in_dim, IQ2_DTYPE_F32, num_sms_for_current_device());
+            if (workspace == nullptr || workspace_bytes < need)
+                return fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
+                            workspace ? workspace_bytes : (size_t)0);
+            float* xq = static_cast<float*>(workspace);
+            const cudaError_t e = iq2::launch_qdq_w8a8(x, x_dtype, m, in_dim, xq, reinterpret_cast<cudaStream_t>(stream));
+            if (e != cudaSuccess) return cuda_fail(op, e);
+            return matmul_impl(op, xq, IQ2_DTYPE_F32, m, weight_bytes, weight_bytes_len, weight_scales,
+                               weight_scales_len, out_dim, in_dim, variant, out,
+                               static_cast<uint8_t*>(workspace) + xq_bytes, workspace_bytes - xq_bytes, stream);
+        }
         case IQ2_ACT_QUANT_W4A8:
             if (strict)
                 return fail(IQ2_ERR_UNSUPPORTED,
@@ -331,6 +354,14 @@ int iq2_matmul_with_activation_quant(const void* x, int x_dtype, uint32_t m,
     return matmul_impl("iq2_matmul", x, x_dtype, m, weight_bytes, weight_bytes_len, weight_scales,
                        weight_scales_len, out_dim, in_dim, variant, out, workspace, workspace_bytes,
                        stream);
+}
+
+size_t iq2_matmul_with_activation_quant_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim,
+                                                      int x_dtype, int variant, int act_mode) {
+    if (act_mode != IQ2_ACT_QUANT_W8A8) return iq2_matmul_workspace_size(m, out_dim, in_dim, x_dtype, variant);
+    if (m == 0 || out_dim == 0 || in_dim == 0 || variant != IQ2_VARIANT_IQ2_XXS) return 0;
+    return ((size_t)m * in_dim * sizeof(float) + 255) / 256 * 256 +
+           workspace_for(m, out_dim, in_dim, IQ2_DTYPE_F32, num_sms_for_current_device());
 }
 
 size_t iq2_matmul_grouped_workspace_size(const iq2_matmul_problem* problems, uint32_t count,

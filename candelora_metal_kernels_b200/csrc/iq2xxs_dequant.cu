@@ -101,7 +101,44 @@ __global__ void gather_columns_kernel(const float* __restrict__ gathered, uint32
     }
 }
 
+// W8A8 activation quant-dequant of one token (row) per CTA, as the reference's W8A8 kernels do it
+// (row_inv_scale_w8a8 / qdq_w8a8, src/metal_src/iq2_matmul.metal:85-102): inv = 127 / max|x| over
+// the row (1 when max|x| < 1e-8), xq = clamp(round(x * inv), -127, 127) / inv, round half away
+// from zero, f32 multiply and IEEE division.
+template <typename XT>
+__global__ void __launch_bounds__(256) qdq_w8a8_kernel(const XT* __restrict__ x, uint32_t K, float* __restrict__ xq) {
+    __shared__ float red[8];
+    const XT* xr = x + (size_t)blockIdx.x * K;
+    float* qr = xq + (size_t)blockIdx.x * K;
+    float mx = 0.0f;
+    for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(to_f32(xr[k])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+    const float inv = mx < 1e-8f ? 1.0f : 127.0f / mx;
+    for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) {
+        const float q = fminf(fmaxf(roundf(__fmul_rn(to_f32(xr[k]), inv)), -127.0f), 127.0f);
+        qr[k] = __fdiv_rn(q, inv);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_qdq_w8a8(const void* x, int x_dtype, uint32_t m, uint32_t k, float* xq, cudaStream_t stream) {
+    if (m == 0 || k == 0) return cudaSuccess;
+    switch (x_dtype) {
+        case 0: qdq_w8a8_kernel<float><<<m, 256, 0, stream>>>(static_cast<const float*>(x), k, xq); break;
+        case 1: qdq_w8a8_kernel<__half><<<m, 256, 0, stream>>>(static_cast<const __half*>(x), k, xq); break;
+        default:
+            qdq_w8a8_kernel<__nv_bfloat16><<<m, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), k, xq);
+            break;
+    }
+    return cudaGetLastError();
+}
 
 cudaError_t launch_dequant(const uint8_t* qs, const uint8_t* sc, uint32_t n, uint32_t k, void* out,
                            int out_dtype, int num_sms, cudaStream_t stream) {

@@ -51,6 +51,7 @@ int capi_validate_matmul(const char* op, const void* x, int x_dtype, uint32_t m,
 // Dequantisation and the sharding gather (iq2xxs_dequant.cu).
 cudaError_t launch_dequant(const uint8_t* qs, const uint8_t* sc, uint32_t n, uint32_t k, void* out,
                            int out_dtype, int num_sms, cudaStream_t stream);
+cudaError_t launch_qdq_w8a8(const void* x, int x_dtype, uint32_t m, uint32_t k, float* xq, cudaStream_t stream);
 cudaError_t launch_gather_columns(const float* gathered, uint32_t shards, uint32_t m,
                                   uint32_t shard_cols, float* out, int num_sms, cudaStream_t stream);
 

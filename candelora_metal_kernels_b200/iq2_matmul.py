@@ -117,7 +117,8 @@ def _matmul(x, weight_bytes, weight_scales, out_dim, in_dim, variant, act_mode=_
                 or out.device != x.device:
             _bail(_lib.IQ2_ERR_INVALID_ARGUMENT, f"{op}: out must be a contiguous f32 [{m}, {out_dim}] tensor "
                                                  f"on {x.device}")
-    ws_need = workspace_bytes(m, out_dim, in_dim, x2.dtype, Iq2MatmulVariant(int(variant))) if m else 0
+    ws_need = int(lib.iq2_matmul_with_activation_quant_workspace_size(m, out_dim, in_dim, _X_DTYPES[x2.dtype],
+                                                                      int(variant), int(act_mode))) if m else 0
     if ws_need == 0:
         ws_ptr, ws_len = None, 0  # this call needs no scratch at all
     else:
@@ -148,7 +149,8 @@ def iq2_matmul_with_activation_quant(x, weight_bytes, weight_scales, out_dim, in
                                      variant: Iq2MatmulVariant,
                                      activation_quant: ActivationQuantConfig, *, out=None, workspace=None):
     """src/iq2_matmul.rs:555-591. Off -> iq2_matmul. W4A8 -> error if strict, else iq2_matmul.
-    W8A8 -> error (no W8A8 kernel in this build)."""
+    W8A8 -> the reference's W8A8 numerics (each x row quantised to int8 with 127/max|x| and back,
+    src/metal_src/iq2_matmul.metal:85-102), then the matmul."""
     mode = ActivationQuantMode(activation_quant.mode)
     return _matmul(x, weight_bytes, weight_scales, out_dim, in_dim, variant, act_mode=int(mode),
                    strict=activation_quant.strict, out=out, workspace=workspace)

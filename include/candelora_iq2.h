@@ -95,7 +95,9 @@ int iq2_matmul(const void* x, int x_dtype, uint32_t m, const uint8_t* weight_byt
 /*
  * iq2_matmul with an activation-quant contract. Replaces iq2_matmul_with_activation_quant
  * (src/iq2_matmul.rs:555-591): OFF -> iq2_matmul; W4A8 -> IQ2_ERR_UNSUPPORTED when strict,
- * else iq2_matmul; W8A8 -> IQ2_ERR_UNSUPPORTED in this version (no W8A8 kernel yet).
+ * else iq2_matmul; W8A8 -> the reference's W8A8 numerics (src/metal_src/iq2_matmul.metal:85-102,
+ * :437-499): every x row quantised to int8 with inv = 127/max|x| and back, then the matmul of
+ * those values. W8A8 needs the workspace of iq2_matmul_with_activation_quant_workspace_size.
  */
 int iq2_matmul_with_activation_quant(const void* x, int x_dtype, uint32_t m,
                                      const uint8_t* weight_bytes, size_t weight_bytes_len,
@@ -103,6 +105,10 @@ int iq2_matmul_with_activation_quant(const void* x, int x_dtype, uint32_t m,
                                      uint32_t out_dim, uint32_t in_dim, int variant, int act_mode,
                                      int strict, float* out, void* workspace,
                                      size_t workspace_bytes, iq2_stream_t stream);
+
+/* Workspace for iq2_matmul_with_activation_quant with this act_mode (W8A8 adds m*in_dim floats). */
+size_t iq2_matmul_with_activation_quant_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim,
+                                                      int x_dtype, int variant, int act_mode);
 
 /* One projection of a grouped call (see iq2_matmul_grouped). */
 typedef struct iq2_matmul_problem {

@@ -7,10 +7,12 @@ calls them on:
   ref_parity.npz   the reference test fixture of parity_case(Iq2Xxs) (src/iq2_matmul.rs:1065-1100:
                    m=2, out_dim=7, in_dim=320, LCG bytes 0xA11CE5ED / scales 0xC0FFEE12, every d
                    forced to 1.0, last byte 0x5A, x = deterministic_x) with x in f32, f16 and bf16,
-                   plus the f16 dequantisation;
+                   plus the f16 dequantisation and the W8A8 outputs (f32 and f16 x; the
+                   fixture of parity_case_w8a8, src/iq2_matmul.rs:1181-1253);
   baseline_small.npz  benchmark-distribution inputs (non-unit d ~U[1e-3,1e-2], N(0,1) x) that the
                    reference tests never cover: matmul m=3 x 4096 -> 33 (f32 x), m=2 x 1000 -> 9
-                   (bf16 x, ragged K), and the f16 dequantisation of the 9 x 1000 matrix.
+                   (bf16 x, ragged K), the f16 dequantisation of the 9 x 1000 matrix, and the W8A8
+                   output of the first case.
 Needs oracle/_ref/libiq2ref.so (make -C oracle ref). Run from the repository root.
 """
 import sys
@@ -45,6 +47,8 @@ def main():
     out["y_f16"] = ref.matmul(out["x_f16_bits"], wb, ws, 7, 320, "f16")
     out["y_bf16"] = ref.matmul(out["x_bf16_bits"], wb, ws, 7, 320, "bf16")
     out["deq_f16_bits"] = ref.dequantize_f16(wb, ws, 7, 320)
+    out["y_w8a8_f32"] = ref.matmul(x, wb, ws, 7, 320, "f32", w8a8=True)
+    out["y_w8a8_f16"] = ref.matmul(out["x_f16_bits"], wb, ws, 7, 320, "f16", w8a8=True)
     np.savez_compressed(OUT / "ref_parity.npz", **out)
 
     # --- benchmark-distribution cases (non-unit d)
@@ -53,6 +57,7 @@ def main():
     xa = synth.activations(3, 4096, seed=12)
     b["a_weight_bytes"], b["a_weight_scales"], b["a_x_f32"] = qs.numpy(), sc.numpy(), xa.numpy()
     b["a_y"] = ref.matmul(b["a_x_f32"], b["a_weight_bytes"], b["a_weight_scales"], 33, 4096, "f32")
+    b["a_y_w8a8"] = ref.matmul(b["a_x_f32"], b["a_weight_bytes"], b["a_weight_scales"], 33, 4096, "f32", w8a8=True)
     qs, sc = synth.iq2xxs_weights(9, 1000, seed=13)
     xb = synth.activations(2, 1000, seed=14, dtype=torch.bfloat16)
     b["b_weight_bytes"], b["b_weight_scales"], b["b_x_bf16_bits"] = qs.numpy(), sc.numpy(), bits16(xb)

@@ -71,7 +71,14 @@ def test_workspace_query_needs_no_device(lib):
 def test_activation_quant_modes_without_device(lib):
     args = (None, 0, 1, None, 0, None, 0, 4, 256, 0)
     tail = (None, None, 0, None)
-    assert lib.iq2_matmul_with_activation_quant(*args, 1, 0, *tail) == _lib.IQ2_ERR_UNSUPPORTED
+    assert lib.iq2_matmul_with_activation_quant(*args, 1, 0, *tail) == _lib.IQ2_ERR_DEVICE  # W8A8 runs
     assert lib.iq2_matmul_with_activation_quant(*args, 2, 1, *tail) == _lib.IQ2_ERR_UNSUPPORTED
     assert b"strict" in lib.iq2_last_error()
     assert lib.iq2_matmul_with_activation_quant(*args, 7, 0, *tail) == _lib.IQ2_ERR_INVALID_ARGUMENT
+
+
+def test_w8a8_workspace_query_needs_no_device(lib):
+    off = lib.iq2_matmul_workspace_size(3, 4096, 4096, 0, 0)
+    w8 = lib.iq2_matmul_with_activation_quant_workspace_size(3, 4096, 4096, 0, 0, 1)
+    assert w8 >= off + 3 * 4096 * 4
+    assert lib.iq2_matmul_with_activation_quant_workspace_size(3, 4096, 4096, 0, 0, 0) == off

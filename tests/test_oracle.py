@@ -134,3 +134,18 @@ def test_tables_match_reference_source():
                         "--out", f"{d}/c.h"], check=True)
         assert Path(f"{d}/c.h").read_text() == (root / "candelora_metal_kernels_b200" / "csrc" /
                                                 "iq2xxs_codebook.h").read_text()
+
+
+def test_oracle_w8a8_matches_reference_golden(oracle, golden):
+    """W8A8 (src/metal_src/iq2_matmul.metal:85-102, :437-499): the restated row quant-dequant
+    followed by the restated f32 matmul equals the reference's W8A8 kernel bit for bit, on the
+    reference's parity fixture and on benchmark-distribution weights."""
+    g = golden["ref_parity"]
+    xq = oracle.rowwise_qdq_w8a8(g["x_f32"])
+    assert np.array_equal(oracle.matmul(xq, g["weight_bytes"], g["weight_scales"], 7, 320), g["y_w8a8_f32"])
+    x16 = g["x_f16_bits"].view(np.float16).astype(np.float32)
+    xq16 = oracle.rowwise_qdq_w8a8(x16)
+    assert np.array_equal(oracle.matmul(xq16, g["weight_bytes"], g["weight_scales"], 7, 320), g["y_w8a8_f16"])
+    b = golden["baseline_small"]
+    xq = oracle.rowwise_qdq_w8a8(b["a_x_f32"])
+    assert np.array_equal(oracle.matmul(xq, b["a_weight_bytes"], b["a_weight_scales"], 33, 4096), b["a_y_w8a8"])
