@@ -19,8 +19,8 @@ CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libcandelora_iq2.so"
 SOURCES = ["iq2xxs_capi.cu", "iq2xxs_gemv.cu", "iq2xxs_gemm.cu", "iq2xxs_dequant.cu", "iq2xxs_noalloc.cu",
-           "iq2xxs_sharded.cu"]
-HEADERS = ["iq2xxs_common.cuh", "iq2xxs_codebook.h", "iq2xxs_internal.h"]
+           "iq2xxs_sharded.cu", "iq2_variants.cu"]
+HEADERS = ["iq2xxs_common.cuh", "iq2xxs_codebook.h", "iq2xxs_internal.h", "iq2_variant_grids.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -53,16 +53,6 @@ int num_sms_for_current_device() {
     return v;
 }
 
-const char* variant_name(int v) {
-    switch (v) {
-        case IQ2_VARIANT_IQ2_XXS: return "Iq2Xxs";
-        case IQ2_VARIANT_IQ2_XS: return "Iq2Xs";
-        case IQ2_VARIANT_IQ2_S: return "Iq2S";
-        case IQ2_VARIANT_IQ3_S: return "Iq3S";
-        default: return "?";
-    }
-}
-
 // Where a pointer lives: -1 = not device memory, otherwise the device ordinal.
 int pointer_device(const void* p) {
     cudaPointerAttributes a;
@@ -99,7 +89,9 @@ int check_weights(const char* op, const uint8_t* weight_bytes, size_t weight_byt
                     where(db).c_str(), where(ds).c_str());
     }
     const uint64_t blocks_per_row = ((uint64_t)in_dim + 255u) / 256u;
-    const uint64_t per_block_bytes = 64, per_block_scales = 2;  // IQ2_XXS (src/iq2_matmul.rs:14-17)
+    // bytes / scale bytes per block (src/iq2_matmul.rs:14-29)
+    static const uint64_t kBytes[4] = {64, 64, 72, 104}, kScales[4] = {2, 10, 10, 6};
+    const uint64_t per_block_bytes = kBytes[variant], per_block_scales = kScales[variant];
     const uint64_t nblocks = (uint64_t)out_dim * blocks_per_row;  // < 2^56, cannot overflow
     const uint64_t expected_bytes = nblocks * per_block_bytes;
     const uint64_t expected_scales = nblocks * per_block_scales;
@@ -110,9 +102,6 @@ int check_weights(const char* op, const uint8_t* weight_bytes, size_t weight_byt
     if (weight_scales_len < expected_scales)
         return fail(IQ2_ERR_TOO_SMALL, "%s weight_scales too small: got %zu expected at least %" PRIu64, op,
                     weight_scales_len, expected_scales);
-    if (variant != IQ2_VARIANT_IQ2_XXS)
-        return fail(IQ2_ERR_UNSUPPORTED, "%s: variant %s has no CUDA kernel in this build", op,
-                    variant_name(variant));
     return IQ2_OK;
 }
 
@@ -164,7 +153,9 @@ int matmul_impl(const char* op, const void* x, int x_dtype, uint32_t m, const ui
         return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: x/out not aligned to their element size", op);
     const int sms = num_sms_for_current_device();
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (m <= 16) {
+    if (variant != IQ2_VARIANT_IQ2_XXS) {  // the other formats: one generic kernel, no workspace
+        e = iq2::launch_variant_matmul(variant, x, x_dtype, m, weight_bytes, weight_scales, out_dim, in_dim, out, sms, s);
+    } else if (m <= 16) {
         if (iq2::gemv_fast_path_ok(m, in_dim, weight_bytes, weight_scales)) {
             const size_t need = iq2::gemv_workspace_size(m, out_dim, in_dim, sms);
             if (need > 0 && (workspace == nullptr || workspace_bytes < need))
@@ -262,15 +253,15 @@ int capi_num_sms() { return num_sms_for_current_device(); }
 // The checks iq2_matmul makes before choosing a kernel (clears the thread's error message first).
 int capi_validate_matmul(const char* op, const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
                          size_t weight_bytes_len, const uint8_t* weight_scales, size_t weight_scales_len,
-                         uint32_t out_dim, uint32_t in_dim, const float* out) {
+                         uint32_t out_dim, uint32_t in_dim, const float* out, int variant) {
     g_last_error.clear();
-    int rc = check_args(op, out_dim, in_dim, IQ2_VARIANT_IQ2_XXS);
+    int rc = check_args(op, out_dim, in_dim, variant);
     if (rc != IQ2_OK) return rc;
     int dev = 0;
     if ((rc = current_device(op, &dev)) != IQ2_OK) return rc;
     if (m > 0 && x == nullptr) return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL x", op);
     rc = check_weights(op, weight_bytes, weight_bytes_len, weight_scales, weight_scales_len, out_dim, in_dim,
-                       IQ2_VARIANT_IQ2_XXS, dev, m > 0 ? x : nullptr);
+                       variant, dev, m > 0 ? x : nullptr);
     if (rc != IQ2_OK) return rc;
     if (x_dtype < IQ2_DTYPE_F32 || x_dtype > IQ2_DTYPE_BF16)
         return fail(IQ2_ERR_DTYPE, "%s unsupported x dtype: %d", op, x_dtype);
@@ -323,15 +314,13 @@ int iq2_matmul_with_activation_quant(const void* x, int x_dtype, uint32_t m,
             const char* op = "iq2_matmul";
             int rc = check_args(op, out_dim, in_dim, variant);
             if (rc != IQ2_OK) return rc;
-            if (variant != IQ2_VARIANT_IQ2_XXS)
-                return matmul_impl(op, x, x_dtype, m, weight_bytes, weight_bytes_len, weight_scales,
-                                   weight_scales_len, out_dim, in_dim, variant, out, workspace, workspace_bytes,
-                                   stream);  // reports the missing variant like the Off path
             rc = iq2::capi_validate_matmul(op, x, x_dtype, m, weight_bytes, weight_bytes_len, weight_scales,
-                                           weight_scales_len, out_dim, in_dim, out);
+                                           weight_scales_len, out_dim, in_dim, out, variant);
             if (rc != IQ2_OK || m == 0) return rc;
             const size_t xq_bytes = ((size_t)m * in_dim * sizeof(float) + 255) / 256 * 256;
-            const size_t need = xq_bytes + workspace_for(m, out_dim, in_dim, IQ2_DTYPE_F32, num_sms_for_current_device());
+            const size_t need = xq_bytes + (variant == IQ2_VARIANT_IQ2_XXS
+                                                ? workspace_for(m, out_dim, in_dim, IQ2_DTYPE_F32, num_sms_for_current_device())
+                                                : 0);
             if (workspace == nullptr || workspace_bytes < need)
                 return fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
                             workspace ? workspace_bytes : (size_t)0);
@@ -359,9 +348,10 @@ int iq2_matmul_with_activation_quant(const void* x, int x_dtype, uint32_t m,
 size_t iq2_matmul_with_activation_quant_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim,
                                                       int x_dtype, int variant, int act_mode) {
     if (act_mode != IQ2_ACT_QUANT_W8A8) return iq2_matmul_workspace_size(m, out_dim, in_dim, x_dtype, variant);
-    if (m == 0 || out_dim == 0 || in_dim == 0 || variant != IQ2_VARIANT_IQ2_XXS) return 0;
+    if (m == 0 || out_dim == 0 || in_dim == 0 || variant < IQ2_VARIANT_IQ2_XXS || variant > IQ2_VARIANT_IQ3_S) return 0;
     return ((size_t)m * in_dim * sizeof(float) + 255) / 256 * 256 +
-           workspace_for(m, out_dim, in_dim, IQ2_DTYPE_F32, num_sms_for_current_device());
+           (variant == IQ2_VARIANT_IQ2_XXS ? workspace_for(m, out_dim, in_dim, IQ2_DTYPE_F32, num_sms_for_current_device())
+                                           : 0);
 }
 
 size_t iq2_matmul_grouped_workspace_size(const iq2_matmul_problem* problems, uint32_t count,
@@ -422,8 +412,12 @@ int iq2_dequantize(const uint8_t* weight_bytes, size_t weight_bytes_len,
     const size_t esize = out_dtype == IQ2_DTYPE_F32 ? 4 : 2;
     if (reinterpret_cast<uintptr_t>(out) % esize != 0)
         return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: out not aligned to its element size", op);
-    e = iq2::launch_dequant(weight_bytes, weight_scales, out_dim, in_dim, out, out_dtype,
-                            num_sms_for_current_device(), reinterpret_cast<cudaStream_t>(stream));
+    if (variant == IQ2_VARIANT_IQ2_XXS)
+        e = iq2::launch_dequant(weight_bytes, weight_scales, out_dim, in_dim, out, out_dtype,
+                                num_sms_for_current_device(), reinterpret_cast<cudaStream_t>(stream));
+    else
+        e = iq2::launch_variant_dequant(variant, weight_bytes, weight_scales, out_dim, in_dim, out, out_dtype,
+                                        num_sms_for_current_device(), reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(op, e);
     return IQ2_OK;
 }

@@ -46,11 +46,17 @@ int capi_ok();  // clears the thread's error message
 int capi_num_sms();
 int capi_validate_matmul(const char* op, const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
                          size_t weight_bytes_len, const uint8_t* weight_scales, size_t weight_scales_len,
-                         uint32_t out_dim, uint32_t in_dim, const float* out);
+                         uint32_t out_dim, uint32_t in_dim, const float* out, int variant = 0);
 
 // Dequantisation and the sharding gather (iq2xxs_dequant.cu).
 cudaError_t launch_dequant(const uint8_t* qs, const uint8_t* sc, uint32_t n, uint32_t k, void* out,
                            int out_dtype, int num_sms, cudaStream_t stream);
+// The IQ2_XS / IQ2_S / IQ3_S formats (iq2_variants.cu); variant = IQ2_VARIANT_* of the C ABI.
+cudaError_t launch_variant_matmul(int variant, const void* x, int x_dtype, uint32_t m, const uint8_t* qs,
+                                  const uint8_t* sc, uint32_t n, uint32_t k, float* out, int num_sms,
+                                  cudaStream_t stream);
+cudaError_t launch_variant_dequant(int variant, const uint8_t* qs, const uint8_t* sc, uint32_t n, uint32_t k,
+                                   void* out, int out_dtype, int num_sms, cudaStream_t stream);
 cudaError_t launch_qdq_w8a8(const void* x, int x_dtype, uint32_t m, uint32_t k, float* xq, cudaStream_t stream);
 cudaError_t launch_gather_columns(const float* gathered, uint32_t shards, uint32_t m,
                                   uint32_t shard_cols, float* out, int num_sms, cudaStream_t stream);

@@ -84,8 +84,9 @@ size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, 
  * ActivationQuantMode::Off, and through it iq2_xxs_matmul (:604-619).
  * m == 0 is valid and launches nothing (the reference returns an empty [0, out_dim] tensor).
  * weight_*_len are the element counts of the caller's buffers (checked like :246-259).
- * Routing (not part of the contract): m <= 16 runs the decode GEMV (int8 tensor-core decode,
- * f32-accurate); larger m runs the tcgen05 GEMM (bf16 operands, f32 accumulate).
+ * Routing (not part of the contract): IQ2_XXS with m <= 16 runs the decode GEMV (int8 tensor-core
+ * decode, f32-accurate), larger m the tcgen05 GEMM (bf16 operands, f32 accumulate); IQ2_XS, IQ2_S
+ * and IQ3_S run a generic f32 kernel (src/iq2_matmul.rs:884-1016 numerics, FMA accumulate).
  */
 int iq2_matmul(const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
                size_t weight_bytes_len, const uint8_t* weight_scales, size_t weight_scales_len,

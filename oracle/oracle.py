@@ -28,6 +28,8 @@ REF_SO = HERE / "_ref" / "libiq2ref.so"
 QK = 256
 DTYPE_CODE = {"f32": 0, "f16": 1, "bf16": 2}
 VARIANT_CODE = {"iq2_xxs": 0, "iq2_xs": 1, "iq2_s": 2, "iq3_s": 3}
+# (weight bytes, scale bytes) per 256-weight block (src/iq2_matmul.rs:15-29)
+BLOCK_BYTES = {"iq2_xxs": (64, 2), "iq2_xs": (64, 10), "iq2_s": (72, 10), "iq3_s": (104, 6)}
 
 _c_f32p = ctypes.POINTER(ctypes.c_float)
 _c_u8p = ctypes.POINTER(ctypes.c_uint8)
@@ -76,14 +78,15 @@ def force_f16_one_per_block(scales: np.ndarray, scales_per_block: int) -> np.nda
 
 
 def reference_parity_fixture(m=2, out_dim=7, in_dim=320, bytes_seed=0xA11CE5ED,
-                             scales_seed=0xC0FFEE12, last_byte=0x5A):
-    """The inputs of the reference's parity_case for IQ2_XXS (src/iq2_matmul.rs:1065-1100):
-    LCG weight bytes and scales, every d forced to 1.0, last weight byte forced, x from
+                             scales_seed=0xC0FFEE12, last_byte=0x5A, variant="iq2_xxs"):
+    """The inputs of the reference's parity_case(variant) (src/iq2_matmul.rs:1065-1100): LCG
+    weight bytes and scales, every d forced to 1.0, last weight byte forced, x from
     deterministic_x. Returns (x f32 [m,in_dim], weight_bytes u8, weight_scales u8)."""
     nb = (in_dim + QK - 1) // QK
     nblocks = out_dim * nb
-    wb = lcg_fill(nblocks * 64, bytes_seed)
-    ws = force_f16_one_per_block(lcg_fill(nblocks * 2, scales_seed), 2)
+    bpb, spb = BLOCK_BYTES[variant]
+    wb = lcg_fill(nblocks * bpb, bytes_seed)
+    ws = force_f16_one_per_block(lcg_fill(nblocks * spb, scales_seed), spb)
     if last_byte is not None and len(wb):
         wb[-1] = last_byte
     return deterministic_x(m, in_dim), wb, ws
@@ -103,6 +106,11 @@ class Oracle:
         lib.oracle_iq2xxs_dequantize.argtypes = [_c_u8p, _c_u8p, ctypes.c_size_t, ctypes.c_size_t,
                                                  ctypes.c_int, ctypes.c_void_p, ctypes.c_int]
         lib.oracle_widen_x.argtypes = [_c_u16p, ctypes.c_int, ctypes.c_size_t, _c_f32p]
+        lib.oracle_iq2_matmul_f32.argtypes = [ctypes.c_int, _c_f32p, ctypes.c_size_t, ctypes.c_size_t,
+                                              ctypes.c_size_t, _c_u8p, _c_u8p, _c_i64p, ctypes.c_size_t,
+                                              _c_f32p, ctypes.c_int]
+        lib.oracle_iq2_dequantize.argtypes = [ctypes.c_int, _c_u8p, _c_u8p, ctypes.c_size_t, ctypes.c_size_t,
+                                              ctypes.c_int, ctypes.c_void_p, ctypes.c_int]
         lib.oracle_rowwise_qdq_w8a8.argtypes = [_c_f32p, ctypes.c_size_t, ctypes.c_size_t, _c_f32p]
         lib.oracle_f32_to_f16.argtypes = [ctypes.c_float]
         lib.oracle_f32_to_f16.restype = ctypes.c_uint16
@@ -111,10 +119,11 @@ class Oracle:
         self.lib = lib
 
     @staticmethod
-    def _check(wb, ws, out_dim, in_dim):
+    def _check(wb, ws, out_dim, in_dim, variant="iq2_xxs"):
         nb = (in_dim + QK - 1) // QK
+        bpb, spb = BLOCK_BYTES[variant]
         assert wb.dtype == np.uint8 and ws.dtype == np.uint8
-        assert wb.size >= out_dim * nb * 64 and ws.size >= out_dim * nb * 2
+        assert wb.size >= out_dim * nb * bpb and ws.size >= out_dim * nb * spb
 
     def widen_x(self, x16: np.ndarray, dtype: str) -> np.ndarray:
         """f16/bf16 bit patterns (uint16) -> f32, as the reference kernels' float(x)."""
@@ -124,10 +133,10 @@ class Oracle:
         return out
 
     def matmul(self, x: np.ndarray, wb: np.ndarray, ws: np.ndarray, out_dim: int, in_dim: int,
-               cols=None, threads: int = 0, x_dtype: str = "f32") -> np.ndarray:
+               cols=None, threads: int = 0, x_dtype: str = "f32", variant: str = "iq2_xxs") -> np.ndarray:
         """Reference matmul: x [m, in_dim] (f32, or uint16 bit patterns for f16/bf16) -> f32
         [m, out_dim] (or [m, len(cols)] for a column sample)."""
-        self._check(wb, ws, out_dim, in_dim)
+        self._check(wb, ws, out_dim, in_dim, variant)
         if x_dtype != "f32":
             x = self.widen_x(x, x_dtype)
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, in_dim)
@@ -143,18 +152,19 @@ class Oracle:
             out = np.empty((m, out_dim), dtype=np.float32)
             cp, nc = None, 0
         threads = threads or (os.cpu_count() or 1)
-        self.lib.oracle_iq2xxs_matmul_f32(_ptr(x, _c_f32p), m, out_dim, in_dim, _ptr(wb, _c_u8p),
-                                          _ptr(ws, _c_u8p), cp, nc, _ptr(out, _c_f32p), threads)
+        self.lib.oracle_iq2_matmul_f32(VARIANT_CODE[variant], _ptr(x, _c_f32p), m, out_dim, in_dim,
+                                       _ptr(wb, _c_u8p), _ptr(ws, _c_u8p), cp, nc, _ptr(out, _c_f32p), threads)
         return out
 
-    def dequantize(self, wb, ws, out_dim, in_dim, out_dtype="f16", threads: int = 0) -> np.ndarray:
+    def dequantize(self, wb, ws, out_dim, in_dim, out_dtype="f16", threads: int = 0,
+                   variant: str = "iq2_xxs") -> np.ndarray:
         """Dense [out_dim, in_dim]: f32 values, or f16/bf16 RNE bit patterns (uint16)."""
-        self._check(wb, ws, out_dim, in_dim)
+        self._check(wb, ws, out_dim, in_dim, variant)
         code = DTYPE_CODE[out_dtype]
         out = np.empty((out_dim, in_dim), dtype=np.float32 if code == 0 else np.uint16)
-        self.lib.oracle_iq2xxs_dequantize(_ptr(np.ascontiguousarray(wb), _c_u8p),
-                                          _ptr(np.ascontiguousarray(ws), _c_u8p), out_dim, in_dim,
-                                          code, out.ctypes.data, threads or (os.cpu_count() or 1))
+        self.lib.oracle_iq2_dequantize(VARIANT_CODE[variant], _ptr(np.ascontiguousarray(wb), _c_u8p),
+                                       _ptr(np.ascontiguousarray(ws), _c_u8p), out_dim, in_dim,
+                                       code, out.ctypes.data, threads or (os.cpu_count() or 1))
         return out
 
     def rowwise_qdq_w8a8(self, x: np.ndarray) -> np.ndarray:

@@ -12,7 +12,9 @@ calls them on:
   baseline_small.npz  benchmark-distribution inputs (non-unit d ~U[1e-3,1e-2], N(0,1) x) that the
                    reference tests never cover: matmul m=3 x 4096 -> 33 (f32 x), m=2 x 1000 -> 9
                    (bf16 x, ragged K), the f16 dequantisation of the 9 x 1000 matrix, and the W8A8
-                   output of the first case.
+                   output of the first case;
+  ref_variants.npz the parity_case fixture for IQ2_XS, IQ2_S and IQ3_S (d = 1) and the same bytes
+                   with non-unit d: f32 matmul and f16 dequantisation.
 Needs oracle/_ref/libiq2ref.so (make -C oracle ref). Run from the repository root.
 """
 import sys
@@ -64,7 +66,26 @@ def main():
     b["b_y"] = ref.matmul(b["b_x_bf16_bits"], b["b_weight_bytes"], b["b_weight_scales"], 9, 1000, "bf16")
     b["b_deq_f16_bits"] = ref.dequantize_f16(b["b_weight_bytes"], b["b_weight_scales"], 9, 1000)
     np.savez_compressed(OUT / "baseline_small.npz", **b)
-    print("wrote", OUT / "ref_parity.npz", OUT / "baseline_small.npz")
+
+    # --- the other variants: the reference's parity_case(variant) fixture (d = 1) and the same
+    # --- bytes with non-unit d ~U[1e-3, 1e-2] (f16), f32 matmul and f16 dequantisation
+    v = {}
+    rng = np.random.default_rng(17)
+    for name in ("iq2_xs", "iq2_s", "iq3_s"):
+        x, wb, ws = reference_parity_fixture(variant=name)
+        v[f"{name}_x"], v[f"{name}_weight_bytes"], v[f"{name}_weight_scales"] = x, wb, ws
+        v[f"{name}_y"] = ref.matmul(x, wb, ws, 7, 320, "f32", variant=name)
+        v[f"{name}_deq_f16_bits"] = ref.dequantize_f16(wb, ws, 7, 320, variant=name)
+        spb = {"iq2_xs": 10, "iq2_s": 10, "iq3_s": 6}[name]
+        ws2 = ws.copy()
+        d = rng.uniform(1e-3, 1e-2, ws2.size // spb).astype(np.float16).view(np.uint16)
+        ws2.reshape(-1, spb)[:, 0] = (d & 0xFF).astype(np.uint8)
+        ws2.reshape(-1, spb)[:, 1] = (d >> 8).astype(np.uint8)
+        v[f"{name}_weight_scales_d"] = ws2
+        v[f"{name}_y_d"] = ref.matmul(x, wb, ws2, 7, 320, "f32", variant=name)
+        v[f"{name}_deq_d_f16_bits"] = ref.dequantize_f16(wb, ws2, 7, 320, variant=name)
+    np.savez_compressed(OUT / "ref_variants.npz", **v)
+    print("wrote", OUT / "ref_parity.npz", OUT / "baseline_small.npz", OUT / "ref_variants.npz")
 
 
 if __name__ == "__main__":

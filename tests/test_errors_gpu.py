@@ -49,10 +49,14 @@ def test_dtype_and_shape_errors():
 
 def test_other_variants_and_activation_modes():
     x, qs, sc = _setup()
-    with pytest.raises(c.Iq2Error, match="no CUDA kernel") as e:
+    # IQ2_XS: its own block geometry (64 + 10 bytes per block); too-small scales are rejected
+    with pytest.raises(c.Iq2Error, match="weight_scales too small") as e:
         c.iq2_xs_matmul(x, torch.zeros(16 * 2 * 64, dtype=torch.uint8, device="cuda"),
+                        torch.zeros(16 * 2 * 2, dtype=torch.uint8, device="cuda"), 16, 512)
+    assert e.value.code == _lib.IQ2_ERR_TOO_SMALL
+    y = c.iq2_xs_matmul(x, torch.zeros(16 * 2 * 64, dtype=torch.uint8, device="cuda"),
                         torch.zeros(16 * 2 * 10, dtype=torch.uint8, device="cuda"), 16, 512)
-    assert e.value.code == _lib.IQ2_ERR_UNSUPPORTED
+    assert torch.equal(y, torch.zeros_like(y))  # d = 0 everywhere
     strict = c.ActivationQuantConfig(c.ActivationQuantMode.W4A8, strict=True)
     with pytest.raises(c.Iq2Error, match="strict mode"):
         c.iq2_matmul_with_activation_quant(x, qs, sc, 16, 512, c.Iq2MatmulVariant.Iq2Xxs, strict)
