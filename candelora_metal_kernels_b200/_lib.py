@@ -42,6 +42,7 @@ SIGNATURES = {
     "iq2_matmul_noalloc": ([_vp, _int, _u32, _vp, _sz, _vp, _sz, _u32, _u32, _vp, _vp], _int),
     "iq2_dequantize": ([_vp, _sz, _vp, _sz, _u32, _u32, _int, _vp, _int, _vp], _int),
     "iq2_gather_columns": ([_vp, _u32, _u32, _u32, _vp, _vp], _int),
+    "iq2_split_interleaved": ([_vp, _sz, ctypes.c_uint64, _int, _vp, _vp, _vp], _int),
     "iq2_comm_unique_id": ([_vp], _int),
     "iq2_comm_init": ([_vp, _int, _int, _vp], _int),
     "iq2_comm_destroy": ([_vp], _int),

@@ -422,6 +422,31 @@ int iq2_dequantize(const uint8_t* weight_bytes, size_t weight_bytes_len,
     return IQ2_OK;
 }
 
+int iq2_split_interleaved(const uint8_t* blocks, size_t blocks_len, uint64_t nblocks, int variant,
+                          uint8_t* weight_bytes, uint8_t* weight_scales, iq2_stream_t stream) {
+    g_last_error.clear();
+    const char* op = "iq2_split_interleaved";
+    if (variant < IQ2_VARIANT_IQ2_XXS || variant > IQ2_VARIANT_IQ3_S)
+        return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: unknown variant %d", op, variant);
+    if (nblocks == 0) return IQ2_OK;
+    static const uint32_t kBytes[4] = {64, 64, 72, 104}, kScales[4] = {2, 10, 10, 6};
+    const uint64_t need = nblocks * (uint64_t)(kBytes[variant] + kScales[variant]);
+    if (blocks == nullptr || weight_bytes == nullptr || weight_scales == nullptr)
+        return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL pointer", op);
+    if (blocks_len < need)
+        return fail(IQ2_ERR_TOO_SMALL, "%s: blocks too small: got %zu expected at least %" PRIu64, op, blocks_len, need);
+    int dev = 0;
+    int rc = current_device(op, &dev);
+    if (rc != IQ2_OK) return rc;
+    if (pointer_device(blocks) != dev || pointer_device(weight_bytes) != dev || pointer_device(weight_scales) != dev)
+        return fail(IQ2_ERR_DEVICE, "%s: buffers are not memory of Cuda(%d)", op, dev);
+    const cudaError_t e = iq2::launch_split_interleaved(blocks, nblocks, kBytes[variant], kScales[variant], weight_bytes,
+                                                        weight_scales, num_sms_for_current_device(),
+                                                        reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(op, e);
+    return IQ2_OK;
+}
+
 int iq2_gather_columns(const float* gathered, uint32_t shards, uint32_t m, uint32_t shard_cols,
                        float* out, iq2_stream_t stream) {
     g_last_error.clear();

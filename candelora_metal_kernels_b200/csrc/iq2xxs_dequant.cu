@@ -126,7 +126,37 @@ __global__ void __launch_bounds__(256) qdq_w8a8_kernel(const XT* __restrict__ x,
     }
 }
 
+// ggml's interleaved blocks (d, then the packed weights, then the format's extra scale bytes) ->
+// the reference's split tensors (weight_bytes: the packed weights; weight_scales: d, then the
+// extra scale bytes). One thread per interleaved byte: coalesced reads, near-coalesced writes.
+__global__ void __launch_bounds__(256) split_interleaved_kernel(const uint8_t* __restrict__ blocks, uint64_t total,
+                                                                uint32_t ib, uint32_t bpb, uint32_t spb,
+                                                                uint8_t* __restrict__ wb, uint8_t* __restrict__ ws) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t blk = i / ib;
+        const uint32_t off = (uint32_t)(i % ib);
+        const uint8_t v = blocks[i];
+        if (off < 2) ws[blk * spb + off] = v;
+        else if (off < 2 + bpb) wb[blk * bpb + off - 2] = v;
+        else ws[blk * spb + 2 + (off - 2 - bpb)] = v;
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_split_interleaved(const uint8_t* blocks, uint64_t nblocks, uint32_t bytes_per_block,
+                                     uint32_t scales_per_block, uint8_t* wb, uint8_t* ws, int num_sms,
+                                     cudaStream_t stream) {
+    const uint32_t ib = bytes_per_block + scales_per_block;
+    const uint64_t total = nblocks * ib;
+    if (total == 0) return cudaSuccess;
+    uint64_t grid = (total + 255) / 256;
+    const uint64_t cap = (uint64_t)(num_sms > 0 ? num_sms : 148) * 16;
+    if (grid > cap) grid = cap;
+    split_interleaved_kernel<<<(unsigned)grid, 256, 0, stream>>>(blocks, total, ib, bytes_per_block, scales_per_block,
+                                                                 wb, ws);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_qdq_w8a8(const void* x, int x_dtype, uint32_t m, uint32_t k, float* xq, cudaStream_t stream) {
     if (m == 0 || k == 0) return cudaSuccess;

@@ -57,6 +57,9 @@ cudaError_t launch_variant_matmul(int variant, const void* x, int x_dtype, uint3
                                   cudaStream_t stream);
 cudaError_t launch_variant_dequant(int variant, const uint8_t* qs, const uint8_t* sc, uint32_t n, uint32_t k,
                                    void* out, int out_dtype, int num_sms, cudaStream_t stream);
+cudaError_t launch_split_interleaved(const uint8_t* blocks, uint64_t nblocks, uint32_t bytes_per_block,
+                                     uint32_t scales_per_block, uint8_t* wb, uint8_t* ws, int num_sms,
+                                     cudaStream_t stream);
 cudaError_t launch_qdq_w8a8(const void* x, int x_dtype, uint32_t m, uint32_t k, float* xq, cudaStream_t stream);
 cudaError_t launch_gather_columns(const float* gathered, uint32_t shards, uint32_t m,
                                   uint32_t shard_cols, float* out, int num_sms, cudaStream_t stream);

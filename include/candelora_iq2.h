@@ -175,6 +175,18 @@ int iq2_gather_columns(const float* gathered, uint32_t shards, uint32_t m, uint3
                        float* out, iq2_stream_t stream);
 
 /*
+ * ggml / GGUF block layout -> the split tensors this library (and the reference) take. No
+ * reference counterpart: the reference only reads split tensors; this is the ingest of the
+ * on-disk format they come from. `blocks` holds nblocks interleaved ggml blocks of `variant`
+ * (block_iq2_xxs 66 B: d, qs[64]; block_iq2_xs 74 B: d, qs[64], scales[8]; block_iq2_s 82 B:
+ * d, qs[64], qh[8], scales[8]; block_iq3_s 110 B: d, qs[64], qh[8], signs[32], scales[4]);
+ * weight_bytes receives nblocks * {64, 64, 72, 104} bytes, weight_scales nblocks * {2, 10, 10, 6}
+ * (d, then the block's scale bytes). Device pointers, stream-ordered.
+ */
+int iq2_split_interleaved(const uint8_t* blocks, size_t blocks_len, uint64_t nblocks, int variant,
+                          uint8_t* weight_bytes, uint8_t* weight_scales, iq2_stream_t stream);
+
+/*
  * Column sharding over the GPUs of one node (no reference counterpart: the reference is
  * single-device; this is the multi-GPU layout the benchmark specification asks for). Rank r of a
  * world of g holds rows [r*N/g, (r+1)*N/g) of each projection's weights, a contiguous slice of
