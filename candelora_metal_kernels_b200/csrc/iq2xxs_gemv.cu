@@ -409,10 +409,30 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         if (a < b && ic.tb < tb1) {
             const GemvProblem& P = L.prob[ic.p];
             const uint32_t st_s = ring_s + islot * STAGE_BYTES;
+            const uint32_t row0 = ic.rg * ROWS;
+            if (ic.tb * 8 >= a && ic.tb * 8 + 8 <= b && row0 + ROWS <= P.N) {
+                // the common case: every sub-block and every row of the stage is needed
+                const size_t row_bytes = (size_t)P.nb * QS_BYTES;
+                const uint8_t* qrow = P.qs + ((size_t)row0 * P.nb + ic.blk) * QS_BYTES +
+                                      (size_t)(lane >> 2) * row_bytes + (lane & 3) * 16;
+#pragma unroll
+                for (int c = 0; c < ROWS * 4 / 32; ++c) {
+                    const int r = c * 8 + (lane >> 2), ch = lane & 3;
+                    cp_async_16(st_s + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4), qrow + (size_t)c * 8 * row_bytes, 16u);
+                }
+                if (lane < ROWS) {
+                    const size_t e = ((size_t)(row0 + lane) * P.nb + ic.blk) * SC_BYTES;
+                    const size_t ea = e & ~(size_t)3, total = (size_t)P.N * P.nb * SC_BYTES;
+                    cp_async_4(st_s + STAGE_QS + lane * 4, P.sc + ea, (uint32_t)min((size_t)4, total - ea));
+                }
+                cursor_next(L, ic);
+                cp_async_commit();
+                islot = (islot + 1 == NSTAGES) ? 0 : islot + 1;
+                return;
+            }
             const uint32_t s_lo = ic.tb * 8 < a ? a - ic.tb * 8 : 0u;        // first sub-block needed
             const uint32_t s_hi = min(8u, b - ic.tb * 8);                     // one past the last
             const uint32_t ch_lo = s_lo >> 1, ch_hi = (s_hi + 1) >> 1;        // 16-byte chunks needed
-            const uint32_t row0 = ic.rg * ROWS;
             const uint8_t* qrow = P.qs + ((size_t)row0 * P.nb + ic.blk) * QS_BYTES;
             const size_t row_bytes = (size_t)P.nb * QS_BYTES;
 #pragma unroll
