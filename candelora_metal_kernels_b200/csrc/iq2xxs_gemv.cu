@@ -536,15 +536,16 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 if (FUSED) cs[nt] = *reinterpret_cast<const float2*>(smem + cs_off + ci * 4);
                 else cs[nt] = __ldg(reinterpret_cast<const float2*>(P.colscale + ci));
             }
-            const uint32_t row0 = cc.rg * ROWS;
+            // d sits in the high half of its aligned word when row*nb + blk is odd; this lane's
+            // rows all have the parity of g (tiles start at multiples of 16 rows)
+            const uint32_t dsel = ((cc.blk ^ ((uint32_t)g & P.nb)) & 1u) ? 0x3232u : 0x1010u;
 #pragma unroll
             for (int tt = 0; tt < T; ++tt) {
                 const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
                 const uint32_t w0 = ld_shared_u32_volatile(st_s + STAGE_QS + r0 * 4);
                 const uint32_t w1 = ld_shared_u32_volatile(st_s + STAGE_QS + r1 * 4);
-                const uint32_t o0 = ((row0 + r0) * P.nb + cc.blk) & 1u, o1 = ((row0 + r1) * P.nb + cc.blk) & 1u;
-                const float d0 = half_bits_to_float(o0 ? (w0 >> 16) : w0);
-                const float d1 = half_bits_to_float(o1 ? (w1 >> 16) : w1);
+                const float d0 = half_bits_to_float(prmt(w0, 0u, dsel));
+                const float d1 = half_bits_to_float(prmt(w1, 0u, dsel));
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     F[tt][nt][0] = fmaf((float)I[tt][nt][0], d0 * cs[nt].x, F[tt][nt][0]);
