@@ -313,6 +313,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         del g2
 
     del graph, ggraph
+    models = None
+    if not args.no_models:
+        models = {"forward": forward_bench(args, wl, device, stream, comm, dist),
+                  "ffn70b": ffn70b_bench(args, device, stream, comm, rank, world, _peaks()[0])}
     if comm is not None:
         torch.cuda.synchronize()
         comm.close()
@@ -343,6 +347,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "clocks": clocks.summary(),
             "roofline": roof,
         }
+        if models is not None:
+            line["config4_forward"] = models["forward"]
+            line["config3_ffn70b"] = models["ffn70b"]
         if not args.no_gemm:
             line["gemm"] = gemm_bench(args, device, stream, peaks, peak_src)
         if not args.no_cpu_baseline:
@@ -360,6 +367,127 @@ def _ncu_traffic(bytes_per_launch: int):
     except Exception:
         pass
     return None
+
+
+# ---------------------------------------------------------------------------------------- models
+def forward_bench(args, wl, device, stream, comm, dist):
+    """Benchmark configuration 4: the 32-layer Llama-3-8B linear stack as one forward pass, with
+    a fixed dataflow (q, k, v, gate, up on x in one grouped call; o on q; down on up; the next
+    layer's x = RMS-normalised down output), RMS-normalised N(0,1) input rows, M in {1, 32}
+    (decode GEMV, tensor-core GEMM). Column-sharded over the ranks when N > 1. Device time per
+    forward, max over ranks."""
+    import candelora_metal_kernels_b200 as c
+    from candelora_metal_kernels_b200 import synth
+    from candelora_metal_kernels_b200.sharded import iq2_matmul_grouped_sharded
+    layers = [wl.calls[i:i + 7] for i in range(0, len(wl.calls), 7)]
+    res = {}
+    for m in (1, 32):
+        x0 = synth.activations(m, 4096, seed=4242, device=device, rms_normalize=True)
+        outs = {name: torch.empty(m, n, device=device) for (_, _, _, n, _, _, _, name) in layers[0]}
+
+        def matmuls(probs):
+            if dist:
+                iq2_matmul_grouped_sharded(comm, probs)
+            else:
+                c.iq2_matmul_grouped(probs)
+
+        def forward():
+            x = x0
+            for lay in layers:
+                w = {name: (qs, sc, n, k) for (_, qs, sc, n, k, _, _, name) in lay}
+                matmuls([(x, *w[nm][:2], w[nm][2], w[nm][3], outs[nm]) for nm in ("q", "k", "v", "gate", "up")])
+                matmuls([(outs["q"], *w["o"][:2], w["o"][2], w["o"][3], outs["o"])])
+                matmuls([(outs["up"], *w["down"][:2], w["down"][2], w["down"][3], outs["down"])])
+                d = outs["down"]
+                x = d * torch.rsqrt((d * d).mean(dim=1, keepdim=True) + 1e-6)
+            return x
+
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                forward()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            y = forward()
+        with torch.cuda.stream(stream):
+            g.replay()
+        if dist:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        reps = max(3, args.steps // 10)
+        ms = _time_graph(g, reps, stream) / reps
+        if dist:
+            t = torch.tensor([ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        finite = bool(torch.isfinite(y).all().item())
+        del g
+        res[f"m{m}"] = {"ms_per_forward": round(ms, 4), "weight_gbs": round(wl.weight_bytes / (ms * 1e-3) / 1e9, 1),
+                        "finite": finite}
+    return {"workload": "config4: 32-layer Llama-3-8B linear stack, RMS-normalised input rows, "
+                        "3 calls per layer (q,k,v,gate,up grouped; o; down) + RMS norm between layers",
+            **res}
+
+
+def ffn70b_bench(args, device, stream, comm, rank, world, peaks):
+    """Benchmark configuration 3: Llama-3-70B FFN projections (gate/up 8192x28672, down
+    28672x8192) at M=1 (one grouped call, weight GB/s) and M=2048 (bf16 x, TFLOPS),
+    column-sharded over the ranks when N > 1. Device time, max over ranks."""
+    import candelora_metal_kernels_b200 as c
+    from candelora_metal_kernels_b200 import synth
+    from candelora_metal_kernels_b200.sharded import iq2_matmul_grouped_sharded
+    dist = world > 1
+    ws = []
+    total_bytes = flops_per_m = 0
+    for i, (name, k, n) in enumerate(synth.LLAMA3_70B_FFN):
+        n_loc = n // world
+        qs, sc = synth.iq2xxs_weights(n, k, seed=700 + i, device=device, row_begin=rank * n_loc,
+                                      row_end=(rank + 1) * n_loc)
+        ws.append((qs, sc, n, k))
+        total_bytes += synth.packed_bytes(n, k)
+        flops_per_m += 2 * n * k
+    res = {}
+    for m, dtype in ((1, torch.float32), (2048, torch.bfloat16)):
+        probs = []
+        for i, (qs, sc, n, k) in enumerate(ws):
+            x = synth.activations(m, k, seed=800 + i, dtype=dtype, device=device)
+            probs.append((x, qs, sc, n, k, torch.empty(m, n, device=device)))
+
+        def run():
+            if dist:
+                iq2_matmul_grouped_sharded(comm, probs)
+            else:
+                c.iq2_matmul_grouped(probs)
+
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                run()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            run()
+        with torch.cuda.stream(stream):
+            g.replay()
+        if dist:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        reps = 20 if m == 1 else 3
+        ms = _time_graph(g, reps, stream) / reps
+        if dist:
+            t = torch.tensor([ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        del g, probs
+        if m == 1:
+            gbs = total_bytes / (ms * 1e-3) / 1e9
+            res["m1"] = {"ms": round(ms, 4), "weight_gbs": round(gbs, 1),
+                         "frac_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4)}
+        else:
+            tf = flops_per_m * m / (ms * 1e-3) / 1e12
+            res["m2048"] = {"ms": round(ms, 3), "tflops": round(tf, 1),
+                            "frac_bf16_per_gpu": round(tf / world / peaks["bf16_tflops"], 4)}
+    return {"workload": "config3: Llama-3-70B FFN gate/up 8192x28672, down 28672x8192, one grouped call"
+                        + (f", column-sharded over {world} GPUs + NCCL all-gather" if dist else ""), **res}
 
 
 # ---------------------------------------------------------------------------------------- GEMM
@@ -505,6 +633,7 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
+    ap.add_argument("--no-models", action="store_true", help="skip the configuration 3 and 4 measurements")
     ap.add_argument("--gemm-reps", type=int, default=5)
     ap.add_argument("--case", choices=["gemv", "gemm"], default=None,
                     help="run only the dominant kernel's shape (the profiler's small case) and exit")
