@@ -127,7 +127,7 @@ int current_device(const char* op, int* dev) {
 size_t workspace_for(uint32_t m, uint32_t out_dim, uint32_t in_dim, int x_dtype, int num_sms) {
     if (m == 0 || out_dim == 0 || in_dim == 0) return 0;
     if (m <= 16) return iq2::gemv_workspace_size(m, out_dim, in_dim, num_sms);
-    return iq2::gemm_workspace_size(m, out_dim, in_dim, x_dtype);
+    return iq2::gemm_workspace_size(m, out_dim, in_dim, x_dtype, num_sms);
 }
 
 int matmul_impl(const char* op, const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
@@ -168,7 +168,7 @@ int matmul_impl(const char* op, const void* x, int x_dtype, uint32_t m, const ui
                                          out, sms, s);
         }
     } else if (iq2::gemm_path_ok(m, out_dim, in_dim, x, x_dtype, weight_bytes, weight_scales, out)) {
-        const size_t need = iq2::gemm_workspace_size(m, out_dim, in_dim, x_dtype);
+        const size_t need = iq2::gemm_workspace_size(m, out_dim, in_dim, x_dtype, sms);
         if (need > 0 && (workspace == nullptr || workspace_bytes < need))
             return fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
                         workspace ? workspace_bytes : (size_t)0);

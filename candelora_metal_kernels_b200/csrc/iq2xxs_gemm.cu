@@ -8,10 +8,10 @@
 //   * B = W, dequantised to bf16 in shared memory by 8 decode warps, directly in the canonical
 //     SW128 K-major layout the MMA reads. Each weight is bf16(d*(2s+1)/8 * g) for g in {8,25,43}:
 //     the three products of a 32-weight sub-block are rounded once and a `prmt` picks the bf16
-//     pairs by grid code (IQ2XXS_BF16_SEL), an XOR applies the signs (the sign byte spread to the
-//     bf16 sign bits by one multiply). This is bit-identical to rounding every weight's exact f32
-//     value (the dequant kernel's bf16). Tables are kept small (2 KB + 128 B) because the tensor
-//     core reads its operands through the same shared memory.
+//     pairs by grid code (IQ2XXS_BF16_SEL), an XOR applies the signs (the 7 stored sign bits and
+//     their parity spread to the bf16 sign bits by one multiply per pair). This is bit-identical to
+//     rounding every weight's exact f32 value (the dequant kernel's bf16). The table is kept small
+//     (2 KB) because the tensor core reads its operands through the same shared memory.
 //   * D: two 128 x BN f32 accumulators in TMEM (512 columns allocated): one CTA computes a tile of
 //     256 tokens x BN weight rows (BN = 256, or 224 when that leaves fewer SMs idle in the last
 //     wave, e.g. 512 tiles instead of 448 on 148 SMs for N = 14336), issuing per 64-k stage
@@ -45,7 +45,7 @@ constexpr int G_A_HALF = 128 * G_BK * 2;        // 16 KB: one 128-token box
 constexpr int G_A_BYTES = 2 * G_A_HALF;         // 32 KB
 constexpr int G_B_BYTES = G_BN * G_BK * 2;      // 32 KB
 constexpr int G_STAGE_BYTES = G_A_BYTES + G_B_BYTES;
-constexpr int G_SEL_BYTES = 256 * 8 + 128;      // decode tables: selector pairs, sign bytes
+constexpr int G_SEL_BYTES = 256 * 8;            // decode table: selector pairs per grid code
 constexpr int G_SMEM = 1024 /*align*/ + G_STAGES * G_STAGE_BYTES + G_SEL_BYTES + 256 /*barriers*/;
 constexpr uint32_t G_TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: only a broken pipeline waits that long
@@ -59,9 +59,10 @@ constexpr uint32_t idesc_for() {
 struct GemmParams {
     const uint8_t* qs;
     const uint8_t* sc;
-    float* out;
+    float* out;     // [M, N]; with splits > 1 the [splits, M, N] partial sums instead
     uint32_t* err;  // error word (0 = ok); set on a pipeline timeout
     uint32_t M, N, K, nb;
+    uint32_t splits;  // K split into this many ranges of whole 256-blocks (blockIdx.z)
 };
 
 // ---- mbarrier / tcgen05 / TMA wrappers (inline PTX) ----
@@ -167,6 +168,49 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// One 32-weight sub-block (8 bytes: aux_g, aux_s) of one row -> 32 bf16 weights, written as four
+// 16-byte chunks at dst ^ (t << 4) (dst: the row's first chunk of the sub-block in the SW128 tile,
+// its low 7 bits the swizzled chunk; t < 4 only flips bits 4-5). Each weight is
+// bf16(d*(2s+1)/8 * g) with g in {8, 25, 43}: the three products are rounded once and a `prmt`
+// picks the bf16 pairs by grid code (sel_s: IQ2XXS_BF16_SEL packed as two words per entry); an
+// XOR applies the signs. TAIL: zero the weights at k >= K (k_lo = the sub-block's first k).
+template <bool TAIL>
+__device__ __forceinline__ void decode_sub(uint2 q, float d, uint32_t sel_s, uint32_t dst, uint32_t k_lo,
+                                           uint32_t K) {
+    const uint32_t aux_g = q.x, aux_s = q.y;
+    const float dl = d * (float)((aux_s >> 27) | 1u) * 0.125f;  // d*(2s+1)/8, exact
+    const uint32_t qlo = cvt_bf16x2(dl * 8.0f, dl * 25.0f);     // {bf16(8dl), bf16(25dl)}
+    const uint32_t qhi = cvt_bf16x2(dl * 43.0f, 0.0f);          // {bf16(43dl), 0}
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const uint32_t gi = (aux_g >> (8 * t)) & 0xFFu, si = (aux_s >> (7 * t)) & 0x7Fu;
+        const uint2 sel = ld_shared_v2_const(sel_s + gi * 8);
+        // the 8 sign bits (bit j: weight j negative): 7 stored, the 8th makes their parity even
+        const uint32_t S = si | ((__popc(si) & 1u) << 7);
+        // (S * K_i) & 0x80008000 puts sign bits 2i and 2i+1 at bits 15 and 31 (the two bf16 sign
+        // bits of pair i): the shifted copies of S never overlap, no carries.
+        uint4 w;
+        w.x = prmt(qlo, qhi, sel.x) ^ ((S * 0x40008000u) & 0x80008000u);
+        w.y = prmt(qlo, qhi, sel.x >> 16) ^ ((S * 0x10002000u) & 0x80008000u);
+        w.z = prmt(qlo, qhi, sel.y) ^ ((S * 0x04000800u) & 0x80008000u);
+        w.w = prmt(qlo, qhi, sel.y >> 16) ^ ((S * 0x01000200u) & 0x80008000u);
+        if (TAIL && k_lo + t * 8 + 8 > K) {  // weights past in_dim contribute 0
+            const uint32_t k0 = k_lo + t * 8;
+            const uint32_t keep = k0 >= K ? 0u : K - k0;  // 0..7 weights kept
+            w.x = keep >= 2 ? w.x : (keep == 1 ? (w.x & 0xFFFFu) : 0u);
+            w.y = keep >= 4 ? w.y : (keep == 3 ? (w.y & 0xFFFFu) : 0u);
+            w.z = keep >= 6 ? w.z : (keep == 5 ? (w.z & 0xFFFFu) : 0u);
+            w.w = keep >= 8 ? w.w : (keep == 7 ? (w.w & 0xFFFFu) : 0u);
+        }
+        st_shared_v4(dst ^ ((uint32_t)t << 4), w);
+    }
+}
+
 // ---- the kernel ----
 // BN: weight rows per CTA (256, or 224 where that fills the last wave better); the stage
 // layout is always sized for 256 rows.
@@ -179,8 +223,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
     const uint32_t base_s = (raw_s + 1023u) & ~1023u;  // SW128 tiles need 1024-byte alignment
     uint8_t* base = smem_raw + (base_s - raw_s);
     const uint32_t sel_s = base_s + G_STAGES * G_STAGE_BYTES;
-    const uint32_t sgn_s = sel_s + 256 * 8;
-    const uint32_t bar_s = sgn_s + 128;
+    const uint32_t bar_s = sel_s + G_SEL_BYTES;
     // barriers: full_a[S], full_b[S], empty[S], acc_full; then the TMEM address word; abort flag
     auto full_a = [&](int s) { return bar_s + 8u * s; };
     auto full_b = [&](int s) { return bar_s + 8u * (G_STAGES + s); };
@@ -191,15 +234,20 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * G_BM;
-    const uint32_t KT = (p.K + G_BK - 1) / G_BK;
+    // this CTA's share of K: the 256-blocks [b0, b1) of split blockIdx.z, i.e. the 64-k stages
+    // [kt0, kt0 + NKT) (at least one: the host never makes more splits than blocks)
+    const uint32_t b0 = (uint32_t)((uint64_t)blockIdx.z * p.nb / p.splits);
+    const uint32_t b1 = (uint32_t)((uint64_t)(blockIdx.z + 1) * p.nb / p.splits);
+    const uint32_t kt0 = b0 * (QK / G_BK);
+    const uint32_t NKT = min(b1 * (QK / G_BK), (p.K + G_BK - 1) / G_BK) - kt0;
+    const bool upper = m0 + 128 < p.M;  // the tile's second 128-token half holds tokens
 
-    // decode tables -> shared memory: per grid entry the four 16-bit prmt selectors packed in two
-    // words, and the 8-bit sign masks (ksigns)
+    // decode table -> shared memory: per grid entry the four 16-bit prmt selectors packed in two
+    // words
     for (int i = threadIdx.x; i < 256 * 2; i += blockDim.x) {
         const uint32_t* e = IQ2XXS_BF16_SEL[i >> 1];
         reinterpret_cast<uint32_t*>(base + (sel_s - base_s))[i] = (i & 1) ? (e[2] | (e[3] << 16)) : (e[0] | (e[1] << 16));
     }
-    for (int i = threadIdx.x; i < 128; i += blockDim.x) base[(sgn_s - base_s) + i] = IQ2_KSIGNS[i];
     if (threadIdx.x == 0) {
         for (int s = 0; s < G_STAGES; ++s) {
             mbar_init(full_a(s), 1);
@@ -225,26 +273,27 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
     if (warp == G_TMA_WARP) {
         // ---------------- x producer ----------------
         if (lane == 0) {
-            for (uint32_t kt = 0; kt < KT; ++kt) {
-                const int s = kt % G_STAGES;
-                if (kt >= G_STAGES && !mbar_wait(empty(s), ((kt / G_STAGES) - 1) & 1, p.err, 1u)) {
+            for (uint32_t i = 0; i < NKT; ++i) {
+                const int s = i % G_STAGES;
+                if (i >= G_STAGES && !mbar_wait(empty(s), ((i / G_STAGES) - 1) & 1, p.err, 1u)) {
                     *abort_flag = 1u;
                     break;
                 }
                 if (*abort_flag) break;
                 const uint32_t a_s = base_s + s * G_STAGE_BYTES;
-                mbar_expect_tx(full_a(s), G_A_BYTES);
-                tma_load_2d(a_s, &tmap_x, full_a(s), (int)(kt * G_BK), (int)m0);
-                tma_load_2d(a_s + G_A_HALF, &tmap_x, full_a(s), (int)(kt * G_BK), (int)(m0 + 128));
+                const int kx = (int)((kt0 + i) * G_BK);
+                mbar_expect_tx(full_a(s), upper ? G_A_BYTES : G_A_HALF);
+                tma_load_2d(a_s, &tmap_x, full_a(s), kx, (int)m0);
+                if (upper) tma_load_2d(a_s + G_A_HALF, &tmap_x, full_a(s), kx, (int)(m0 + 128));
             }
         }
     } else if (warp == G_MMA_WARP) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             bool ok = true;
-            for (uint32_t kt = 0; kt < KT && ok; ++kt) {
-                const int s = kt % G_STAGES;
-                const uint32_t ph = (kt / G_STAGES) & 1;
+            for (uint32_t i = 0; i < NKT && ok; ++i) {
+                const int s = i % G_STAGES;
+                const uint32_t ph = (i / G_STAGES) & 1;
                 ok = mbar_wait(full_a(s), ph, p.err, 2u) && mbar_wait(full_b(s), ph, p.err, 4u);
                 if (!ok || *abort_flag) {
                     *abort_flag = 1u;
@@ -255,9 +304,9 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
 #pragma unroll
                 for (int ks = 0; ks < G_BK / 16; ++ks) {
                     const uint64_t bd = sw128_desc(b_s + ks * 32);
-                    const uint32_t acc = (kt | ks) ? 1u : 0u;
+                    const uint32_t acc = (i | ks) ? 1u : 0u;
                     tc_mma(tmem, sw128_desc(a_s + ks * 32), bd, idesc_for<BN>(), acc);
-                    tc_mma(tmem + 256, sw128_desc(a_s + G_A_HALF + ks * 32), bd, idesc_for<BN>(), acc);
+                    if (upper) tc_mma(tmem + 256, sw128_desc(a_s + G_A_HALF + ks * 32), bd, idesc_for<BN>(), acc);
                 }
                 tc_commit(empty(s));  // the stage is free once these MMAs have read it
             }
@@ -265,78 +314,71 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
         }
     } else {
         // ---------------- weight decode (warps 0..15), then epilogue ----------------
-        // thread = (tile row r, sub-block h of the stage's two)
+        // thread = (tile row r, sub-block hh of the stage's two). Rows past BN or N are never
+        // stored, so they are left undecoded (whatever the stage holds there only reaches
+        // accumulator columns the epilogue skips).
         const uint32_t r = threadIdx.x & 255u, hh = threadIdx.x >> 8;
         const uint32_t row = n0 + r;
-        const bool rok = r < (uint32_t)BN && row < p.N;  // rows past BN: zeros the MMA never reads
-        const uint8_t* qrow = p.qs + (size_t)(rok ? row : 0) * p.nb * QS_BYTES;
+        const bool rok = r < (uint32_t)BN && row < p.N;
+        const uint8_t* qp = p.qs + (size_t)(rok ? row : 0) * p.nb * QS_BYTES + (size_t)kt0 * 16 + hh * 8;
         const uint8_t* srow = p.sc + (size_t)(rok ? row : 0) * p.nb * SC_BYTES;
-        const uint32_t row_swz = r & 7u;
-        const uint32_t row_off = (r >> 3) * 1024u + (r & 7u) * 128u;
-        uint2 qn = rok ? __ldg(reinterpret_cast<const uint2*>(qrow + hh * 8)) : make_uint2(0, 0);
-        uint32_t dbits = rok ? (uint32_t)srow[0] | ((uint32_t)srow[1] << 8) : 0u;
-        for (uint32_t kt = 0; kt < KT; ++kt) {
-            const int s = kt % G_STAGES;
-            const uint2 q = qn;
-            const uint32_t blk = kt >> 2;
-            if ((kt & 3) == 0 && kt > 0)
-                dbits = rok ? (uint32_t)srow[blk * 2] | ((uint32_t)srow[blk * 2 + 1] << 8) : 0u;
-            if (kt + 1 < KT && rok) qn = __ldg(reinterpret_cast<const uint2*>(qrow + (kt + 1) * 16 + hh * 8));
-            if (kt >= G_STAGES) {
+        // this thread's 16-byte chunks of a stage: row r of the SW128 tile, chunk (hh*4 + t) ^ (r%8)
+        const uint32_t brow = base_s + G_A_BYTES + (r >> 3) * 1024u + (r & 7u) * 128u +
+                              ((((hh * 4u) ^ (r & 7u))) << 4);
+        const uint32_t kt_full = p.K / G_BK;  // stages below this one have no K tail
+        // loads run ahead of the decode: the sub-block two stages on, the block scale one block on
+        const uint32_t kt_end = kt0 + NKT;
+        auto ld_q = [&](uint32_t kt, const uint8_t* ptr) {
+            return rok && kt < kt_end ? __ldg(reinterpret_cast<const uint2*>(ptr)) : make_uint2(0, 0);
+        };
+        auto ld_d = [&](uint32_t blk) {
+            return rok && blk < b1 ? (uint32_t)srow[blk * 2] | ((uint32_t)srow[blk * 2 + 1] << 8) : 0u;
+        };
+        uint2 q1 = ld_q(kt0, qp), q2 = ld_q(kt0 + 1, qp + 16);
+        uint32_t dbits = ld_d(b0), dnext = ld_d(b0 + 1);
+        uint32_t s = 0, ph = 0;  // stage slot and the parity of its current use
+        for (uint32_t i = 0; i < NKT; ++i) {
+            const uint32_t kt = kt0 + i;
+            const uint2 q = q1;
+            q1 = q2;
+            q2 = ld_q(kt + 2, qp + 32);
+            qp += 16;
+            if ((kt & 3) == 0 && i > 0) {
+                dbits = dnext;
+                dnext = ld_d((kt >> 2) + 1);
+            }
+            if (i >= G_STAGES) {
                 bool ok = true;
-                if (lane == 0) ok = mbar_wait(empty(s), ((kt / G_STAGES) - 1) & 1, p.err, 8u);
+                if (lane == 0) ok = mbar_wait(empty(s), ph ^ 1u, p.err, 8u);
                 ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
                 if (!ok) *abort_flag = 1u;
             }
             if (*abort_flag) break;
-            const float d = half_bits_to_float(dbits);
-            uint8_t* bt = base + s * G_STAGE_BYTES + G_A_BYTES + row_off;
-            {  // this thread's 32-weight sub-block of the stage
-                const uint32_t h = hh;
-                const uint32_t aux_g = q.x, aux_s = q.y;
-                const float dl = d * (float)((aux_s >> 27) | 1u) * 0.125f;  // d*(2s+1)/8, exact
-                const uint32_t qlo = cvt_bf16x2(dl * 8.0f, dl * 25.0f);     // {bf16(8dl), bf16(25dl)}
-                const uint32_t qhi = cvt_bf16x2(dl * 43.0f, 0.0f);          // {bf16(43dl), 0}
-                const uint32_t k_lo = kt * G_BK + h * 32;                  // first k of the sub-block
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const uint32_t gi = (aux_g >> (8 * t)) & 0xFFu, si = (aux_s >> (7 * t)) & 0x7Fu;
-                    const uint2 sel = *reinterpret_cast<const uint2*>(base + (sel_s - base_s) + gi * 8);
-                    const uint32_t S = base[(sgn_s - base_s) + si];  // bit j: weight j negative
-                    // (S * K_i) & 0x80008000 puts sign bits 2i and 2i+1 at bits 15 and 31 (the two
-                    // bf16 sign bits of pair i): the shifted copies of S never overlap, no carries.
-                    uint4 w;
-                    w.x = prmt(qlo, qhi, sel.x) ^ ((S * 0x40008000u) & 0x80008000u);
-                    w.y = prmt(qlo, qhi, sel.x >> 16) ^ ((S * 0x10002000u) & 0x80008000u);
-                    w.z = prmt(qlo, qhi, sel.y) ^ ((S * 0x04000800u) & 0x80008000u);
-                    w.w = prmt(qlo, qhi, sel.y >> 16) ^ ((S * 0x01000200u) & 0x80008000u);
-                    if (k_lo + t * 8 + 8 > p.K) {  // the K tail: weights past in_dim contribute 0
-                        const uint32_t k0 = k_lo + t * 8;
-                        const uint32_t keep = k0 >= p.K ? 0u : p.K - k0;  // 0..7 weights kept
-                        w.x = keep >= 2 ? w.x : (keep == 1 ? (w.x & 0xFFFFu) : 0u);
-                        w.y = keep >= 4 ? w.y : (keep == 3 ? (w.y & 0xFFFFu) : 0u);
-                        w.z = keep >= 6 ? w.z : (keep == 5 ? (w.z & 0xFFFFu) : 0u);
-                        w.w = keep >= 8 ? w.w : (keep == 7 ? (w.w & 0xFFFFu) : 0u);
-                    }
-                    const uint32_t chunk = (uint32_t)(h * 4 + t);  // 16-byte chunk along k
-                    *reinterpret_cast<uint4*>(bt + ((chunk ^ row_swz) << 4)) = w;
-                }
+            if (rok) {
+                const float d = half_bits_to_float(dbits);
+                const uint32_t dst = brow + s * G_STAGE_BYTES;
+                if (kt < kt_full) decode_sub<false>(q, d, sel_s, dst, 0, p.K);
+                else decode_sub<true>(q, d, sel_s, dst, kt * G_BK + hh * 32, p.K);
             }
             fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
             __syncwarp();
             if (lane == 0) mbar_arrive(full_b(s));
+            if (++s == G_STAGES) {
+                s = 0;
+                ph ^= 1u;
+            }
         }
 
         // ---------------- epilogue: TMEM -> registers -> global ----------------
         bool ok = true;
         if (lane == 0) ok = mbar_wait(acc_full, 0, p.err, 16u);
         ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
-        if (ok && !*abort_flag) {
+        // accumulator, TMEM lane quadrant (fixed by the warp's rank in its group of 4), column half
+        const uint32_t acc = (warp >> 2) & 1, quad = warp & 3, chalf = warp >> 3;
+        if (ok && !*abort_flag && (acc == 0 || upper)) {
             tc_fence_after();
-            // accumulator, TMEM lane quadrant (fixed by the warp's rank in its group of 4), column half
-            const uint32_t acc = (warp >> 2) & 1, quad = warp & 3, chalf = warp >> 3;
             const uint32_t token = m0 + acc * 128 + quad * 32 + lane;
-            float* orow = p.out + (size_t)token * p.N;
+            float* orow = p.out + (size_t)blockIdx.z * p.M * p.N + (size_t)token * p.N;
             const bool vec = (p.N % 4) == 0;
 #pragma unroll 1
             for (int c = (int)chalf; c < BN / 32; c += 2) {
@@ -376,6 +418,35 @@ __global__ void __launch_bounds__(256) to_bf16_kernel(const XT* __restrict__ x, 
         y[i] = __float2bfloat16_rn(to_f32(x[i]));
 }
 
+// out = the sum of the K splits' partial products, in split order (deterministic).
+template <bool V4>
+__global__ void __launch_bounds__(256) splitk_sum_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                                         size_t mn, uint32_t splits) {
+    const size_t step = (size_t)gridDim.x * blockDim.x;
+    if (V4) {
+        const float4* p4 = reinterpret_cast<const float4*>(part);
+        float4* o4 = reinterpret_cast<float4*>(out);
+        const size_t n4 = mn / 4;
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += step) {
+            float4 a = p4[i];
+            for (uint32_t z = 1; z < splits; ++z) {
+                const float4 b = p4[z * n4 + i];
+                a.x += b.x;
+                a.y += b.y;
+                a.z += b.z;
+                a.w += b.w;
+            }
+            o4[i] = a;
+        }
+    } else {
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += step) {
+            float a = part[i];
+            for (uint32_t z = 1; z < splits; ++z) a += part[z * mn + i];
+            out[i] = a;
+        }
+    }
+}
+
 // Driver entry point for cuTensorMapEncodeTiled (no link-time dependency on libcuda).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -395,6 +466,38 @@ EncodeTiledFn encode_fn() {
 
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
+struct GemmPlan {
+    uint32_t bn;      // weight rows per CTA: 256 or 224
+    uint32_t splits;  // K splits (blockIdx.z)
+};
+
+// Tile width and K split. With at least one CTA per SM the tile width whose last wave is fullest
+// and no split; with fewer tiles than SMs (small m x n) K is split into ranges of whole 256-blocks,
+// at least two per range, so that one wave fills as many SMs as it can: the decode of the weight
+// tile, not the tensor core, bounds a CTA, and it runs only on the SMs that hold one.
+GemmPlan gemm_plan(uint32_t m, uint32_t n, uint32_t k, int num_sms) {
+    const uint64_t sms = num_sms > 0 ? (uint64_t)num_sms : 148u;
+    const uint64_t mt = (m + G_BM - 1) / G_BM, nb = (k + QK - 1) / QK;
+    auto tiles = [&](uint32_t bn) { return (uint64_t)((n + bn - 1) / bn) * mt; };
+    auto fill = [&](uint64_t ctas) {
+        const uint64_t waves = (ctas + sms - 1) / sms;
+        return (double)ctas / (double)(waves * sms);
+    };
+    if (tiles(G_BN) >= sms) return {fill(tiles(224)) > fill(tiles(G_BN)) + 0.02 ? 224u : (uint32_t)G_BN, 1u};
+    GemmPlan best{(uint32_t)G_BN, 1u};
+    double best_fill = -1.0;
+    for (uint32_t bn : {(uint32_t)G_BN, 224u}) {
+        const uint64_t t = tiles(bn);
+        const uint64_t sp = std::max<uint64_t>(1, std::min<uint64_t>(sms / t, nb / 2));
+        const double f = fill(t * sp);
+        if (f > best_fill + 1e-9) {
+            best_fill = f;
+            best = {bn, (uint32_t)sp};
+        }
+    }
+    return best;
+}
+
 }  // namespace
 
 bool gemm_path_ok(uint32_t m, uint32_t n, uint32_t k, const void* x, int x_dtype, const uint8_t* qs,
@@ -408,10 +511,11 @@ bool gemm_path_ok(uint32_t m, uint32_t n, uint32_t k, const void* x, int x_dtype
            reinterpret_cast<uintptr_t>(qs) % 16 == 0 && encode_fn() != nullptr;
 }
 
-size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype) {
-    (void)n;
+size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype, int num_sms) {
     size_t ws = 256;  // error word
-    if (x_dtype != kDtypeBf16) ws += align256((size_t)m * k * 2);
+    if (x_dtype != kDtypeBf16) ws += align256((size_t)m * k * 2);  // bf16 copy of x
+    const GemmPlan pl = gemm_plan(m, n, k, num_sms);
+    if (pl.splits > 1) ws += align256((size_t)pl.splits * m * n * sizeof(float));  // partial sums
     return ws;
 }
 
@@ -422,8 +526,10 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     cudaError_t e = cudaMemsetAsync(err, 0, 4, stream);
     if (e != cudaSuccess) return e;
     const void* xb = x;
+    size_t ws_off = 256;
     if (x_dtype != kDtypeBf16) {
-        __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(ws + 256);
+        __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(ws + ws_off);
+        ws_off += align256((size_t)m * k * 2);
         const size_t total = (size_t)m * k;
         const unsigned blocks = (unsigned)std::min<size_t>((total + 255) / 256, 148 * 16);
         if (x_dtype == 0) to_bf16_kernel<float><<<blocks, 256, 0, stream>>>(static_cast<const float*>(x), y, total);
@@ -460,18 +566,21 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     p.N = n;
     p.K = k;
     p.nb = (k + QK - 1) / QK;
-    // the tile width whose last wave of CTAs (one per SM) is fullest
-    const int sms = num_sms > 0 ? num_sms : 148;
-    auto wave_fill = [&](uint32_t bn) {
-        const uint64_t tiles = (uint64_t)((n + bn - 1) / bn) * ((m + G_BM - 1) / G_BM);
-        const uint64_t waves = (tiles + sms - 1) / sms;
-        return (double)tiles / (double)(waves * sms);
-    };
-    const bool narrow = wave_fill(224) > wave_fill(256) + 0.02;
-    const uint32_t bn = narrow ? 224u : 256u;
-    dim3 grid((n + bn - 1) / bn, (m + G_BM - 1) / G_BM);
-    if (narrow) gemm_kernel<224><<<grid, G_THREADS, G_SMEM, stream>>>(map, p);
+    const GemmPlan pl = gemm_plan(m, n, k, num_sms);
+    p.splits = pl.splits;
+    float* part = reinterpret_cast<float*>(ws + ws_off);
+    if (pl.splits > 1) p.out = part;
+    dim3 grid((n + pl.bn - 1) / pl.bn, (m + G_BM - 1) / G_BM, pl.splits);
+    if (pl.bn == 224) gemm_kernel<224><<<grid, G_THREADS, G_SMEM, stream>>>(map, p);
     else gemm_kernel<256><<<grid, G_THREADS, G_SMEM, stream>>>(map, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || pl.splits == 1) return e;
+    const size_t mn = (size_t)m * n;
+    const bool v4 = mn % 4 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
+    const int sms = num_sms > 0 ? num_sms : 148;
+    const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((mn / (v4 ? 4 : 1) + 255) / 256, (size_t)sms * 8));
+    if (v4) splitk_sum_kernel<true><<<blocks, 256, 0, stream>>>(part, out, mn, pl.splits);
+    else splitk_sum_kernel<false><<<blocks, 256, 0, stream>>>(part, out, mn, pl.splits);
     return cudaGetLastError();
 }
 

@@ -34,7 +34,7 @@ cudaError_t launch_gemv_generic(const void* x, int x_dtype, uint32_t m, const ui
 // Tensor-core GEMM (iq2xxs_gemm.cu), m > 16.
 bool gemm_path_ok(uint32_t m, uint32_t n, uint32_t k, const void* x, int x_dtype, const uint8_t* qs,
                   const uint8_t* sc, const float* out);
-size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype);
+size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype, int num_sms);
 cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
                         uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,
                         cudaStream_t stream);
