@@ -46,6 +46,8 @@ SIGNATURES = {
     "iq2_comm_unique_id": ([_vp], _int),
     "iq2_comm_init": ([_vp, _int, _int, _vp], _int),
     "iq2_comm_destroy": ([_vp], _int),
+    "iq2_comm_symmetric_alloc": ([_vp, _sz, _vp], _int),
+    "iq2_comm_check": ([_vp], _int),
     "iq2_matmul_grouped_sharded_workspace_size": ([_vp, _u32, _u32, _int, _int], _sz),
     "iq2_matmul_grouped_sharded": ([_vp, _vp, _u32, _u32, _int, _vp, _sz, _vp], _int),
 }

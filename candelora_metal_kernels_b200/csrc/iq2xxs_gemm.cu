@@ -347,13 +347,13 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
                 dbits = dnext;
                 dnext = ld_d((kt >> 2) + 1);
             }
-            if (i >= G_STAGES) {
-                bool ok = true;
-                if (lane == 0) ok = mbar_wait(empty(s), ph ^ 1u, p.err, 8u);
-                ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
-                if (!ok) *abort_flag = 1u;
+            bool go = true;
+            if (lane == 0) go = (i < G_STAGES || mbar_wait(empty(s), ph ^ 1u, p.err, 8u)) && !*abort_flag;
+            go = __shfl_sync(0xFFFFFFFFu, go ? 1 : 0, 0) != 0;  // one decision for the whole warp
+            if (!go) {
+                *abort_flag = 1u;
+                break;
             }
-            if (*abort_flag) break;
             if (rok) {
                 const float d = half_bits_to_float(dbits);
                 const uint32_t dst = brow + s * G_STAGE_BYTES;
@@ -371,11 +371,11 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
 
         // ---------------- epilogue: TMEM -> registers -> global ----------------
         bool ok = true;
-        if (lane == 0) ok = mbar_wait(acc_full, 0, p.err, 16u);
-        ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
+        if (lane == 0) ok = mbar_wait(acc_full, 0, p.err, 16u) && !*abort_flag;
+        ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;  // the TMEM loads below are warp-wide
         // accumulator, TMEM lane quadrant (fixed by the warp's rank in its group of 4), column half
         const uint32_t acc = (warp >> 2) & 1, quad = warp & 3, chalf = warp >> 3;
-        if (ok && !*abort_flag && (acc == 0 || upper)) {
+        if (ok && (acc == 0 || upper)) {
             tc_fence_after();
             const uint32_t token = m0 + acc * 128 + quad * 32 + lane;
             float* orow = p.out + (size_t)blockIdx.z * p.M * p.N + (size_t)token * p.N;

@@ -183,7 +183,8 @@ struct GemvProblem {  // 64 bytes
     const float* colscale;    // their column scales
     float* out;
     uint32_t N, nb, tiles, tb_begin;  // tiles = ceil(N / ROWS); tb_begin: first tile-block (ROWS rows x 1 block)
-    uint32_t pad[2];
+    uint32_t ldo;                     // elements between output rows
+    uint32_t pad;
 };
 
 template <int CAP>
@@ -194,7 +195,14 @@ struct GemvLaunch {
     uint32_t K, clusters;
     uint32_t cl_tb[MAX_CLUSTERS + 1];       // cluster c owns tile-blocks [cl_tb[c], cl_tb[c+1]) (whole tiles)
     uint16_t cl_p[MAX_CLUSTERS];            // problem of the cluster's first tile
+    GemvPeers peers;                        // peer-memory outputs (P2P launches only)
 };
+
+constexpr unsigned long long PEER_WAIT_NS = 1000000000ull;  // 1 s: a rank that never arrives
+
+__device__ __forceinline__ SymmHeader* peer_header(const GemvPeers& pe, int r) {
+    return reinterpret_cast<SymmHeader*>(reinterpret_cast<char*>(pe.hdr) + pe.delta[r]);
+}
 
 // Stream-K partition of [base, base + 32q + r) over a cluster's 32 warps: the first r get q+1 steps.
 struct Partition {
@@ -338,7 +346,9 @@ __device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, 
 
 // XDT < 0: x fragments come from gemv_prep_kernel (workspace); XDT = 0/1/2: a single projection
 // whose f32/f16/bf16 x this kernel turns into limbs itself (kernel-side layout in shared memory).
-template <int NT, int CAP, int XDT>
+// P2P: every output is stored at the same offset of every rank's symmetric region (the
+// column-sharded call's all-gather done by the epilogue), ordered by the header words.
+template <int NT, int CAP, int XDT, bool P2P = false>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvLaunch<CAP> L) {
     using S_ = GemvShape<NT>;
     constexpr bool FUSED = XDT >= 0;
@@ -481,6 +491,65 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     }
     // x (fused) or its fragments (prep kernel), and the outputs, may belong to earlier kernels.
     pdl_wait();
+    // P2P entry: this rank has started call `epoch` (everything before it on this stream is
+    // done, so no earlier kernel still reads the outputs); block 0 tells every rank at once. The
+    // wait for the others is off the compute path: the first warp that is about to store takes
+    // it on (go_owner), waits until every rank has entered, and opens `go` for the rest.
+    unsigned long long epoch = 0;
+    if constexpr (P2P) {
+        const GemvPeers& pe = L.peers;
+        epoch = *reinterpret_cast<volatile unsigned long long*>(&pe.hdr->epoch) + 1ull;
+        if (blockIdx.x == 0 && threadIdx.x == 0)
+            for (int r = 0; r < pe.world; ++r) st_relaxed_sys_u64(peer_header(pe, r)->entry + pe.rank, epoch);
+    }
+    // Before its first store a warp sees `go` (one lane waits, bounded); if it never opens the
+    // outputs stay local and the error bit is set.
+    bool go_seen = !P2P, peers_ok = P2P;
+    auto wait_go = [&]() {
+        if constexpr (P2P) {
+            if (go_seen) return;
+            int ok = 1;
+            if (lane == 0) {
+                const GemvPeers& pe = L.peers;
+                const unsigned long long t0 = gtimer_ns();
+                if (ld_acquire_gpu_u64(&pe.hdr->go) < epoch &&
+                    atomicCAS(&pe.hdr->go_owner, epoch - 1ull, epoch) == epoch - 1ull) {
+                    for (int r = 0; r < pe.world && ok; ++r)
+                        while (ld_acquire_sys_u64(pe.hdr->entry + r) < epoch) {
+                            if (gtimer_ns() - t0 > PEER_WAIT_NS) {
+                                ok = 0;
+                                break;
+                            }
+                            __nanosleep(32);
+                        }
+                    if (ok) st_release_gpu_u64(&pe.hdr->go, epoch);
+                    else atomicOr(&pe.hdr->err, 1u);
+                } else {
+                    while (ld_acquire_gpu_u64(&pe.hdr->go) < epoch) {
+                        if (gtimer_ns() - t0 > 2 * PEER_WAIT_NS) {
+                            ok = 0;
+                            break;
+                        }
+                        __nanosleep(32);
+                    }
+                }
+            }
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+            __syncwarp();
+            go_seen = true;
+            peers_ok = ok != 0;
+        }
+    };
+    auto put = [&](float* o, float v) {
+        if constexpr (P2P) {
+            if (peers_ok) {
+                for (int r = 0; r < L.peers.world; ++r)
+                    *reinterpret_cast<float*>(reinterpret_cast<char*>(o) + L.peers.delta[r]) = v;
+                return;
+            }
+        }
+        *o = v;
+    };
 #pragma unroll
     for (int i = 0; i < NSTAGES; ++i) issue();
     if constexpr (FUSED) {
@@ -571,6 +640,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         const uint32_t row0 = rg * ROWS;
         const uint32_t j = a >= rg_first ? 0u : 1u;  // this tile is my first (0) or last (1)
         float* pslot = part + ((size_t)warp * 2 + j) * TOK * ROWS;
+        if (complete) wait_go();
 #pragma unroll
         for (int tt = 0; tt < T; ++tt) {
 #pragma unroll
@@ -584,9 +654,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 if ((t & 1) == 0) {
                     if (complete) {
                         if (m < L.M) {
-                            float* o = P.out + (size_t)m * P.N;
-                            if (row0 + r0 < P.N) o[row0 + r0] = v0;
-                            if (row0 + r1 < P.N) o[row0 + r1] = v1;
+                            float* o = P.out + (size_t)m * P.ldo;
+                            if (row0 + r0 < P.N) put(o + row0 + r0, v0);
+                            if (row0 + r1 < P.N) put(o + row0 + r1, v1);
                         }
                     } else {
                         pslot[m * ROWS + r0] = v0;
@@ -608,6 +678,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         const GemvProblem& P = L.prob[lc.p];
         const uint32_t rg_first = (P.tb_begin + lc.rg * P.nb) * 8, rg_end = rg_first + P.nb * 8;
         if (rg_end > b && rg_first >= a) {
+            wait_go();
             const uint32_t w_last = part_.owner(rg_end - 1);
             const uint32_t row0 = lc.rg * ROWS;
             for (uint32_t idx = lane; idx < (uint32_t)ROWS * L.M; idx += 32) {
@@ -621,12 +692,45 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                     const uint32_t addr = part_s + off * 4;
                     acc += ld_cluster_f32(map_shared(addr, ww / GEMV_WARPS));
                 }
-                P.out[(size_t)m * P.N + row0 + r] = acc;
+                put(P.out + (size_t)m * P.ldo + row0 + r, acc);
             }
         }
     }
     // keep this CTA's partials alive until the other CTA has read them (no data to publish)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+
+    // P2P exit: the last CTA to finish tells every rank that this rank's outputs are stored,
+    // waits (bounded) until every rank has said so, then closes the call. The CTAs count in with
+    // GPU-scope release; the last one's system-scope fence is cumulative, so one fence orders
+    // every CTA's peer stores before the flags.
+    if constexpr (P2P) {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const GemvPeers& pe = L.peers;
+            __threadfence();
+            const unsigned prev = atomicAdd(&pe.hdr->done, 1u);
+            if (prev == gridDim.x - 1) {
+                __threadfence();
+                if (ld_acquire_gpu_u64(&pe.hdr->go) >= epoch) {
+                    fence_acq_rel_sys();
+                    for (int r = 0; r < pe.world; ++r) st_relaxed_sys_u64(peer_header(pe, r)->data + pe.rank, epoch);
+                    bool ok = true;
+                    const unsigned long long t0 = gtimer_ns();
+                    for (int r = 0; r < pe.world && ok; ++r)
+                        while (ld_acquire_sys_u64(pe.hdr->data + r) < epoch) {
+                            if (gtimer_ns() - t0 > PEER_WAIT_NS) {
+                                ok = false;
+                                break;
+                            }
+                            __nanosleep(64);
+                        }
+                    if (!ok) atomicOr(&pe.hdr->err, 2u);
+                }
+                *reinterpret_cast<volatile unsigned*>(&pe.hdr->done) = 0u;
+                st_release_gpu_u64(&pe.hdr->epoch, epoch);
+            }
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -814,14 +918,15 @@ GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, i
     return pl;
 }
 
-template <int NT, int CAP, int XDT>
+template <int NT, int CAP, int XDT, bool P2P>
 cudaError_t launch_gemv_kernel(const GemvLaunch<CAP>& L, const GroupPlan& pl, cudaStream_t stream) {
     static bool attr_set[64] = {};  // per device; an idempotent attribute, so a race is benign
     int dev = 0;
     cudaGetDevice(&dev);
     cudaError_t e;
     if (dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemv_kernel<NT, CAP, XDT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT);
+        e = cudaFuncSetAttribute(gemv_kernel<NT, CAP, XDT, P2P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 SMEM_LIMIT);
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set[dev] = true;
     }
@@ -839,12 +944,17 @@ cudaError_t launch_gemv_kernel(const GemvLaunch<CAP>& L, const GroupPlan& pl, cu
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<NT, CAP, XDT>, L);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<NT, CAP, XDT, P2P>, L);
+}
+
+template <int NT, int CAP, int XDT>
+cudaError_t launch_gemv_kernel_p(const GemvLaunch<CAP>& L, const GroupPlan& pl, bool p2p, cudaStream_t stream) {
+    return p2p ? launch_gemv_kernel<NT, CAP, XDT, true>(L, pl, stream) : launch_gemv_kernel<NT, CAP, XDT, false>(L, pl, stream);
 }
 
 template <int NT, int CAP>
 cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
-                             uint8_t* ws, const GroupPlan& pl, cudaStream_t stream) {
+                             uint8_t* ws, const GroupPlan& pl, cudaStream_t stream, const GemvPeers* peers) {
     cudaError_t e;
     if (!pl.fused) {
         // ---- prep launch (unique x's) ----
@@ -902,13 +1012,16 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
         P.nb = pl.nb[i];
         P.tiles = pl.tiles[i];
         P.tb_begin = pl.tb_begin[i];
+        P.ldo = probs[i].ldo ? probs[i].ldo : probs[i].n;
     }
-    if (!pl.fused) e = launch_gemv_kernel<NT, CAP, -1>(L, pl, stream);
+    const bool p2p = peers != nullptr;
+    if (p2p) L.peers = *peers;
+    if (!pl.fused) e = launch_gemv_kernel_p<NT, CAP, -1>(L, pl, p2p, stream);
     else if constexpr (NT <= 2 && CAP == 1) {
         switch (x_dtype) {
-            case 0: e = launch_gemv_kernel<NT, CAP, 0>(L, pl, stream); break;
-            case 1: e = launch_gemv_kernel<NT, CAP, 1>(L, pl, stream); break;
-            default: e = launch_gemv_kernel<NT, CAP, 2>(L, pl, stream); break;
+            case 0: e = launch_gemv_kernel_p<NT, CAP, 0>(L, pl, p2p, stream); break;
+            case 1: e = launch_gemv_kernel_p<NT, CAP, 1>(L, pl, p2p, stream); break;
+            default: e = launch_gemv_kernel_p<NT, CAP, 2>(L, pl, p2p, stream); break;
         }
     } else {
         e = cudaErrorInvalidValue;  // the planner never fuses these
@@ -919,11 +1032,11 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
 
 template <int NT>
 cudaError_t launch_group_nt(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
-                            uint8_t* ws, const GroupPlan& pl, cudaStream_t stream) {
+                            uint8_t* ws, const GroupPlan& pl, cudaStream_t stream, const GemvPeers* peers) {
     // parameter capacity: a single projection ships ~1 KB of launch parameters, not 16 KB
-    if (count <= 1) return launch_group_cap<NT, 1>(probs, count, m, x_dtype, ws, pl, stream);
-    if (count <= 16) return launch_group_cap<NT, 16>(probs, count, m, x_dtype, ws, pl, stream);
-    return launch_group_cap<NT, MAX_PROBLEMS>(probs, count, m, x_dtype, ws, pl, stream);
+    if (count <= 1) return launch_group_cap<NT, 1>(probs, count, m, x_dtype, ws, pl, stream, peers);
+    if (count <= 16) return launch_group_cap<NT, 16>(probs, count, m, x_dtype, ws, pl, stream, peers);
+    return launch_group_cap<NT, MAX_PROBLEMS>(probs, count, m, x_dtype, ws, pl, stream, peers);
 }
 
 }  // namespace
@@ -947,15 +1060,15 @@ size_t gemv_workspace_size(uint32_t m, uint32_t n, uint32_t k, int num_sms) {
 }
 
 cudaError_t launch_gemv_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
-                              void* workspace, int num_sms, cudaStream_t stream) {
+                              void* workspace, int num_sms, cudaStream_t stream, const GemvPeers* peers) {
     if (count == 0) return cudaSuccess;
     const GroupPlan pl = plan_group(probs, count, m, max_active_clusters(num_sms));
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     switch (pl.nt) {
-        case 1: return launch_group_nt<1>(probs, count, m, x_dtype, ws, pl, stream);
-        case 2: return launch_group_nt<2>(probs, count, m, x_dtype, ws, pl, stream);
-        case 4: return launch_group_nt<4>(probs, count, m, x_dtype, ws, pl, stream);
-        default: return launch_group_nt<8>(probs, count, m, x_dtype, ws, pl, stream);
+        case 1: return launch_group_nt<1>(probs, count, m, x_dtype, ws, pl, stream, peers);
+        case 2: return launch_group_nt<2>(probs, count, m, x_dtype, ws, pl, stream, peers);
+        case 4: return launch_group_nt<4>(probs, count, m, x_dtype, ws, pl, stream, peers);
+        default: return launch_group_nt<8>(probs, count, m, x_dtype, ws, pl, stream, peers);
     }
 }
 

@@ -17,12 +17,43 @@ struct GemvProblemHost {
     const uint8_t* sc;
     uint32_t n, k;
     float* out;
+    uint32_t ldo = 0;  // elements between output rows (0: n)
+};
+
+// Peer-memory outputs of a sharded decode GEMV. Every rank of a communicator owns a symmetric
+// region (same size, mapped into every other rank's process); it starts with this header. A GEMV
+// launched with peers stores each output at the same offset of every rank's region, and the
+// header words order the exchange (all written and read with system-scope release/acquire):
+//   entry[r]  the last call rank r has started (a rank stores into peers only after all entered:
+//             entering proves the peer's earlier stream work, which may still read the previous
+//             call's outputs, is done);
+//   data[r]   the last call whose outputs rank r has finished storing into this region;
+//   go        this rank's last call whose entry barrier completed (go_owner: the call whose
+//             barrier a warp has taken on: the first warp that needs it waits for the entries);
+//   epoch     this rank's last finished call (the next one is epoch + 1; kept on the device so that
+//             captured CUDA graphs replay correctly);
+//   done      CTAs of the running call that finished storing; err: sticky error bits.
+struct SymmHeader {
+    unsigned long long entry[8];
+    unsigned long long data[8];
+    unsigned long long go;
+    unsigned long long go_owner;
+    unsigned long long epoch;
+    unsigned int done;
+    unsigned int err;  // bit 0: entry barrier timed out; bit 1: data barrier timed out
+};
+constexpr size_t kSymmHeaderBytes = 4096;
+constexpr int kMaxRanks = 8;
+struct GemvPeers {
+    SymmHeader* hdr;             // this rank's header (device address)
+    long long delta[kMaxRanks];  // rank r's region minus this rank's, in bytes (0 for this rank)
+    int world, rank;
 };
 bool gemv_fast_path_ok(uint32_t m, uint32_t k, const uint8_t* qs, const uint8_t* sc);
 uint32_t gemv_max_group();
 size_t gemv_group_workspace_size(const GemvProblemHost* probs, uint32_t count, uint32_t m, int num_sms);
 cudaError_t launch_gemv_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
-                              void* workspace, int num_sms, cudaStream_t stream);
+                              void* workspace, int num_sms, cudaStream_t stream, const GemvPeers* peers = nullptr);
 size_t gemv_workspace_size(uint32_t m, uint32_t n, uint32_t k, int num_sms);
 cudaError_t launch_gemv(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
                         uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,

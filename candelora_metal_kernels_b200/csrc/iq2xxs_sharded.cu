@@ -8,6 +8,12 @@
 // ncclAllGather of that buffer (rank-major), then one kernel that scatters the gathered slices
 // into each projection's [m, N] output. A single projection at m = 1 is all-gathered straight
 // into its output (rank-major slices of one row are already the row).
+//
+// Fused exchange: when every output lies in the communicator's symmetric region (allocated by
+// iq2_comm_symmetric_alloc: one device allocation per rank, mapped into every other rank's process
+// with CUDA IPC) and m <= 16, the decode GEMV stores each output value straight into all ranks'
+// regions over NVLink (plain peer stores) and synchronises through flag words at the head of each
+// region: no NCCL call, no gather buffer, no scatter kernel, one launch per call.
 #include <nccl.h>
 
 #include <algorithm>
@@ -21,6 +27,9 @@
 struct iq2_comm_s {
     ncclComm_t nccl;
     int world, rank, device;
+    uint8_t* symm = nullptr;     // this rank's symmetric region (header + user area)
+    size_t symm_bytes = 0;       // user area bytes
+    void* peer[iq2::kMaxRanks] = {};  // the other ranks' regions mapped here (IPC); peer[rank] = symm
 };
 
 namespace iq2 {
@@ -89,6 +98,58 @@ std::vector<iq2_matmul_problem> local_problems(const iq2_matmul_problem* probs, 
 }
 
 }  // namespace
+
+// The fused-exchange path is taken when every output lies in the symmetric region and m <= 16.
+// Every input to this decision is the same on all ranks (the region is allocated collectively and
+// carved identically), so all ranks take the same path.
+bool use_peer_path(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t count, uint32_t m) {
+    if (comm->symm == nullptr || m > 16 || count > gemv_max_group()) return false;
+    const uint8_t* lo = comm->symm + kSymmHeaderBytes;
+    const uint8_t* hi = lo + comm->symm_bytes;
+    for (uint32_t i = 0; i < count; ++i) {
+        const uint8_t* o = reinterpret_cast<const uint8_t*>(probs[i].out);
+        if (o < lo || o + (size_t)m * probs[i].out_dim * sizeof(float) > hi) return false;
+    }
+    return true;
+}
+
+int sharded_peer(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t count, uint32_t m, int x_dtype,
+                 void* workspace, size_t workspace_bytes, iq2_stream_t stream) {
+    const char* op = "iq2_matmul_grouped_sharded";
+    std::vector<GemvProblemHost> loc(count);
+    for (uint32_t i = 0; i < count; ++i) {
+        const iq2_matmul_problem& p = probs[i];
+        const uint32_t n_loc = p.out_dim / (uint32_t)comm->world;
+        float* out = p.out + (size_t)comm->rank * n_loc;  // this rank's columns of the full [m, out_dim]
+        int rc = capi_validate_matmul(op, p.x, x_dtype, m, p.weight_bytes, p.weight_bytes_len, p.weight_scales,
+                                      p.weight_scales_len, n_loc, p.in_dim, out, IQ2_VARIANT_IQ2_XXS);
+        if (rc != IQ2_OK) return rc;
+        // no fallback here: the other ranks are already committed to the fused exchange (their
+        // bounded waits end in an error that iq2_comm_check reports)
+        if (!gemv_fast_path_ok(m, p.in_dim, p.weight_bytes, p.weight_scales))
+            return capi_fail(IQ2_ERR_UNSUPPORTED,
+                             "%s: problem %u: with outputs in the symmetric region the weight slices must be 16-byte "
+                             "(bytes) and 4-byte (scales) aligned",
+                             op, i);
+        loc[i] = GemvProblemHost{p.x, p.weight_bytes, p.weight_scales, n_loc, p.in_dim, out, p.out_dim};
+    }
+    const int sms = capi_num_sms();
+    const size_t need = gemv_group_workspace_size(loc.data(), count, m, sms);
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+        return capi_fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
+                         workspace ? workspace_bytes : (size_t)0);
+    GemvPeers pe;
+    pe.hdr = reinterpret_cast<SymmHeader*>(comm->symm);
+    pe.world = comm->world;
+    pe.rank = comm->rank;
+    for (int r = 0; r < kMaxRanks; ++r)
+        pe.delta[r] = r < comm->world ? (long long)(static_cast<uint8_t*>(comm->peer[r]) - comm->symm) : 0;
+    const cudaError_t e = launch_gemv_group(loc.data(), count, m, x_dtype, workspace, sms,
+                                            reinterpret_cast<cudaStream_t>(stream), &pe);
+    if (e != cudaSuccess) return capi_cuda_fail(op, e);
+    return capi_ok();
+}
+
 }  // namespace iq2
 
 using iq2::capi_fail;
@@ -122,11 +183,123 @@ int iq2_comm_init(const uint8_t* id, int world, int rank, iq2_comm_t* comm) {
     return iq2::capi_ok();
 }
 
+namespace {
+
+// Every rank reaches this point before any goes on (a one-element all-reduce), so that no rank
+// unmaps or frees a region a peer may still store into.
+ncclResult_t comm_barrier(iq2_comm_t comm, cudaStream_t s) {
+    float* one = nullptr;
+    if (cudaMalloc(&one, sizeof(float)) != cudaSuccess) return ncclUnhandledCudaError;
+    ncclResult_t r = ncclAllReduce(one, one, 1, ncclFloat, ncclSum, comm->nccl, s);
+    if (r == ncclSuccess && cudaStreamSynchronize(s) != cudaSuccess) r = ncclUnhandledCudaError;
+    cudaFree(one);
+    return r;
+}
+
+void release_symmetric(iq2_comm_t comm) {
+    for (int r = 0; r < comm->world && r < iq2::kMaxRanks; ++r)
+        if (r != comm->rank && comm->peer[r] != nullptr) cudaIpcCloseMemHandle(comm->peer[r]);
+    if (comm->symm != nullptr) cudaFree(comm->symm);
+    comm->symm = nullptr;
+    comm->symm_bytes = 0;
+    for (auto& p : comm->peer) p = nullptr;
+}
+
+}  // namespace
+
 int iq2_comm_destroy(iq2_comm_t comm) {
     if (comm == nullptr) return iq2::capi_ok();
-    const ncclResult_t r = ncclCommDestroy(comm->nccl);
+    ncclResult_t r = ncclSuccess;
+    if (comm->symm != nullptr) {
+        cudaStream_t s = nullptr;
+        cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        r = comm_barrier(comm, s);
+        cudaStreamDestroy(s);
+        release_symmetric(comm);
+    }
+    const ncclResult_t r2 = ncclCommDestroy(comm->nccl);
     delete comm;
+    if (r == ncclSuccess) r = r2;
     if (r != ncclSuccess) return capi_fail(IQ2_ERR_COMM, "iq2_comm_destroy: %s", ncclGetErrorString(r));
+    return iq2::capi_ok();
+}
+
+int iq2_comm_symmetric_alloc(iq2_comm_t comm, size_t bytes, void** ptr) {
+    const char* op = "iq2_comm_symmetric_alloc";
+    if (comm == nullptr || ptr == nullptr) return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL comm or ptr", op);
+    *ptr = nullptr;
+    if (bytes == 0) return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "%s: zero bytes", op);
+    if (comm->symm != nullptr) return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "%s: the communicator already has one", op);
+    if (comm->world > iq2::kMaxRanks)
+        return capi_fail(IQ2_ERR_UNSUPPORTED, "%s: at most %d ranks, got %d", op, iq2::kMaxRanks, comm->world);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device)
+        return capi_fail(IQ2_ERR_DEVICE, "%s: the current device is not the communicator's Cuda(%d)", op, comm->device);
+    const size_t total = iq2::kSymmHeaderBytes + (bytes + 255) / 256 * 256;
+    cudaStream_t s = nullptr;
+    cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return iq2::capi_cuda_fail(op, e);
+    // what every rank publishes: its IPC handle and its size (all sizes must agree, since a rank
+    // stores into the others' regions at its own offsets)
+    struct Entry {
+        cudaIpcMemHandle_t handle;
+        unsigned long long total;
+    };
+    uint8_t* base = nullptr;
+    uint8_t* entries = nullptr;  // world entries, gathered on the device
+    ncclResult_t nr = ncclSuccess;
+    std::vector<Entry> h(comm->world);
+    std::memset(h.data(), 0, sizeof(Entry) * h.size());
+    e = cudaMalloc(&entries, sizeof(Entry) * comm->world);
+    if (e != cudaSuccess) {
+        cudaStreamDestroy(s);
+        return iq2::capi_cuda_fail(op, e);
+    }
+    // a rank that fails here still takes part in the exchange (publishing size 0), so that all
+    // ranks see the failure instead of waiting for it
+    cudaError_t le = cudaMalloc(&base, total);
+    if (le == cudaSuccess) le = cudaMemset(base, 0, total);  // zero header: no call entered yet
+    if (le == cudaSuccess) le = cudaIpcGetMemHandle(&h[comm->rank].handle, base);
+    h[comm->rank].total = le == cudaSuccess ? total : 0ull;
+    e = cudaMemcpy(entries + sizeof(Entry) * comm->rank, &h[comm->rank], sizeof(Entry), cudaMemcpyHostToDevice);
+    nr = ncclAllGather(entries + sizeof(Entry) * comm->rank, entries, sizeof(Entry), ncclUint8, comm->nccl, s);
+    if (nr == ncclSuccess && e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess && nr == ncclSuccess)
+        e = cudaMemcpy(h.data(), entries, sizeof(Entry) * comm->world, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = le;
+    bool same_size = true;
+    for (int r = 0; r < comm->world; ++r) same_size = same_size && h[r].total == total;
+    comm->symm = base;
+    comm->peer[comm->rank] = base;
+    for (int r = 0; r < comm->world && same_size && e == cudaSuccess && nr == ncclSuccess; ++r)
+        if (r != comm->rank) e = cudaIpcOpenMemHandle(&comm->peer[r], h[r].handle, cudaIpcMemLazyEnablePeerAccess);
+    // every rank takes part in this barrier whatever happened above, so none is left waiting
+    const ncclResult_t br = comm_barrier(comm, s);  // every rank has mapped every region
+    if (nr == ncclSuccess) nr = br;
+    if (entries != nullptr) cudaFree(entries);
+    cudaStreamDestroy(s);
+    if (e != cudaSuccess || nr != ncclSuccess || !same_size) {
+        release_symmetric(comm);
+        if (e != cudaSuccess) return iq2::capi_cuda_fail(op, e);
+        if (nr != ncclSuccess) return capi_fail(IQ2_ERR_COMM, "%s: %s", op, ncclGetErrorString(nr));
+        return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "%s: the ranks asked for different sizes", op);
+    }
+    comm->symm_bytes = total - iq2::kSymmHeaderBytes;
+    *ptr = base + iq2::kSymmHeaderBytes;
+    return iq2::capi_ok();
+}
+
+int iq2_comm_check(iq2_comm_t comm) {
+    if (comm == nullptr) return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "iq2_comm_check: NULL comm");
+    if (comm->symm == nullptr) return iq2::capi_ok();
+    unsigned err = 0;
+    const cudaError_t e = cudaMemcpy(&err, &reinterpret_cast<iq2::SymmHeader*>(comm->symm)->err, sizeof(err),
+                                     cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return iq2::capi_cuda_fail("iq2_comm_check", e);
+    if (err != 0)
+        return capi_fail(IQ2_ERR_COMM, "iq2_comm_check: a peer exchange timed out (%s%s); outputs of that call are incomplete",
+                         (err & 1u) ? "a rank never entered the call" : "",
+                         (err & 2u) ? ((err & 1u) ? ", a rank never finished" : "a rank never finished") : "");
     return iq2::capi_ok();
 }
 
@@ -159,6 +332,8 @@ int iq2_matmul_grouped_sharded(iq2_comm_t comm, const iq2_matmul_problem* proble
                              op, i, problems[i].out_dim, comm->world);
         if (problems[i].out == nullptr) return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "%s: problem %u: NULL out", op, i);
     }
+    if (iq2::use_peer_path(comm, problems, count, m))
+        return iq2::sharded_peer(comm, problems, count, m, x_dtype, workspace, workspace_bytes, stream);
     const iq2::ShardPlan pl = iq2::plan_shards(problems, count, m, comm->world);
     const size_t need = iq2_matmul_grouped_sharded_workspace_size(problems, count, m, x_dtype, comm->world);
     if (workspace == nullptr || workspace_bytes < need)

@@ -55,17 +55,71 @@ class Iq2Comm:
         handle = ctypes.c_void_p()
         _lib.check(lib.iq2_comm_init(uid, self.world, self.rank, ctypes.byref(handle)))
         self._h = handle
+        self._symm = None  # (base address, bytes) of the symmetric region
+        self._symm_used = 0
+
+    def alloc_symmetric(self, nbytes: int):
+        """Collective: give this communicator a symmetric output region of `nbytes` (same on every
+        rank). Outputs carved from it with symmetric_empty let the sharded decode (m <= 16)
+        store straight into every rank's copy instead of going through an NCCL all-gather."""
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.load().iq2_comm_symmetric_alloc(self._h, int(nbytes), ctypes.byref(ptr)))
+        self._symm = (int(ptr.value), int(nbytes))
+        self._symm_used = 0
+
+    def symmetric_empty(self, *shape, dtype=torch.float32) -> torch.Tensor:
+        """A tensor in the symmetric region (bump allocation, 256-byte aligned). Every rank must
+        carve the same shapes in the same order, so that offsets agree."""
+        if self._symm is None:
+            _bail(_lib.IQ2_ERR_INVALID_ARGUMENT, "symmetric_empty: call alloc_symmetric first")
+        shape = tuple(int(d) for d in (shape[0] if len(shape) == 1 and isinstance(shape[0], (tuple, list)) else shape))
+        itemsize = torch.empty((), dtype=dtype).element_size()
+        nbytes = itemsize
+        for d in shape:
+            nbytes *= d
+        base, cap = self._symm
+        off = (self._symm_used + 255) // 256 * 256
+        if off + nbytes > cap:
+            _bail(_lib.IQ2_ERR_TOO_SMALL, f"symmetric_empty: region of {cap} bytes is full")
+        self._symm_used = off + nbytes
+        return _device_view(base + off, shape, dtype, self.device, owner=self)
+
+    def check(self):
+        """Raise if a fused exchange of this communicator timed out (synchronises the device)."""
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.load().iq2_comm_check(self._h))
 
     def close(self):
         if self._h:
             _lib.check(_lib.load().iq2_comm_destroy(self._h))
             self._h = ctypes.c_void_p()
+            self._symm = None
 
     def __del__(self):
         try:
             self.close()
         except Exception:
             pass
+
+
+class _CudaArray:
+    """Exposes raw device memory to torch through the CUDA array interface (no copy)."""
+
+    _TYPESTR = {torch.float32: "<f4", torch.float16: "<f2", torch.uint8: "|u1", torch.int32: "<i4"}
+
+    def __init__(self, ptr, shape, dtype, owner):
+        self.owner = owner  # keeps the communicator (and its region) alive
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": self._TYPESTR[dtype],
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+def _device_view(ptr, shape, dtype, device, owner):
+    if dtype not in _CudaArray._TYPESTR:
+        _bail(_lib.IQ2_ERR_DTYPE, f"symmetric_empty: unsupported dtype {dtype}")
+    t = torch.as_tensor(_CudaArray(ptr, shape, dtype, owner), device=device)
+    t._iq2_owner = owner
+    return t
 
 
 def _problems(op, comm: Iq2Comm, problems):

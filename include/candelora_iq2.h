@@ -199,15 +199,31 @@ int iq2_split_interleaved(const uint8_t* blocks, size_t blocks_len, uint64_t nbl
 typedef struct iq2_comm_s* iq2_comm_t;
 int iq2_comm_unique_id(uint8_t* id /* IQ2_COMM_ID_BYTES */);
 int iq2_comm_init(const uint8_t* id, int world, int rank, iq2_comm_t* comm);
-int iq2_comm_destroy(iq2_comm_t comm);
+int iq2_comm_destroy(iq2_comm_t comm);  /* collective when a symmetric region exists */
+
+/*
+ * Symmetric output region (no reference counterpart; it is the fused all-gather epilogue of the
+ * sharded decode). Collective: every rank asks for the same `bytes`; each gets a device buffer of
+ * that size whose storage every other rank of the communicator has mapped (CUDA IPC over NVLink).
+ * One region per communicator, freed by iq2_comm_destroy. When every `out` of an
+ * iq2_matmul_grouped_sharded call lies in the region (at the same offsets on all ranks) and
+ * m <= 16, the decode GEMV stores each output straight into every rank's region: no NCCL call, no
+ * gather buffer, one kernel launch. Its waits for the other ranks are bounded (about a second);
+ * a wait that runs out leaves that call's outputs incomplete and is reported by iq2_comm_check.
+ */
+int iq2_comm_symmetric_alloc(iq2_comm_t comm, size_t bytes, void** ptr);
+/* IQ2_OK, or IQ2_ERR_COMM if a fused exchange of this communicator timed out (synchronising). */
+int iq2_comm_check(iq2_comm_t comm);
 
 /* Workspace for iq2_matmul_grouped_sharded: the problems describe the rank's slices, with
  * out_dim the full N (a multiple of world) and out the full [m, N] output. */
 size_t iq2_matmul_grouped_sharded_workspace_size(const iq2_matmul_problem* problems, uint32_t count,
                                                  uint32_t m, int x_dtype, int world);
 /* Up to 256 projections: their slices through one grouped call, one ncclAllGather of all of them
- * on `stream`, one scatter kernel into the outputs. Stream-ordered, collective: every rank makes
- * the same call with the same shapes. */
+ * on `stream`, one scatter kernel into the outputs (or, with every output in the symmetric
+ * region and m <= 16, the fused exchange above; its weight slices must then be 16-byte (bytes)
+ * and 4-byte (scales) aligned on every rank). Stream-ordered, collective: every rank makes the
+ * same call with the same shapes. */
 int iq2_matmul_grouped_sharded(iq2_comm_t comm, const iq2_matmul_problem* problems, uint32_t count,
                                uint32_t m, int x_dtype, void* workspace, size_t workspace_bytes,
                                iq2_stream_t stream);

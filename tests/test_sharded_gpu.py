@@ -1,6 +1,8 @@
 """GPU parity of the column-sharded path (iq2_matmul_grouped_sharded: local slices, one NCCL
-all-gather, one scatter kernel) against the single-GPU iq2_matmul on the full weights. Needs two
-GPUs of one node; skipped otherwise."""
+all-gather, one scatter kernel; or, with outputs in the communicator's symmetric region, the
+decode GEMV storing into every rank's copy) against the single-GPU iq2_matmul on the full
+weights. Needs two GPUs of one node; skipped otherwise. A rank that skips a call makes the other
+rank's bounded waits run out: the status says so and no GPU is faulted."""
 import os
 import socket
 
@@ -60,6 +62,107 @@ def _rank(rank: int, port: int, q):
         q.put((rank, errs))
     except Exception as e:
         q.put((rank, repr(e)))
+
+
+def _rank_fused(rank: int, port: int, q):
+    try:
+        import numpy as np
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+        import candelora_metal_kernels_b200 as c
+        from candelora_metal_kernels_b200 import synth
+        from candelora_metal_kernels_b200 import _lib
+        from candelora_metal_kernels_b200.sharded import Iq2Comm, iq2_matmul_grouped_sharded, shard_rows
+        comm = Iq2Comm()
+        comm.alloc_symmetric(64 << 20)
+        dev = torch.device("cuda", rank)
+
+        def rel(a, b):
+            a, b = a.double().cpu().numpy(), b.double().cpu().numpy()
+            return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+        res = {}
+        shapes = [(4096, 4096), (1024, 14336), (14336, 4096), (96, 512)]
+        full = [tuple(t.to(dev) for t in synth.iq2xxs_weights(n, k, seed=i)) for i, (n, k) in enumerate(shapes)]
+        slices = [shard_rows(full[i][0], full[i][1], n, k, rank, WORLD) for i, (n, k) in enumerate(shapes)]
+        for m in (1, 3, 16):
+            xs = [synth.activations(m, k, seed=30 + i, device=dev) for i, (n, k) in enumerate(shapes)]
+            outs = [comm.symmetric_empty(m, n) for (n, k) in shapes]
+            probs = [(xs[i], *slices[i], n, k, outs[i]) for i, (n, k) in enumerate(shapes)]
+            ys = iq2_matmul_grouped_sharded(comm, probs)  # fused exchange
+            ref_nccl = iq2_matmul_grouped_sharded(comm, [p[:5] for p in probs])  # NCCL all-gather
+            for i, (n, k) in enumerate(shapes):
+                res[f"m={m} {n}x{k} vs single"] = rel(ys[i], c.iq2_xxs_matmul(xs[i], full[i][0], full[i][1], n, k))
+                res[f"m={m} {n}x{k} same as nccl"] = 0.0 if torch.equal(ys[i], ref_nccl[i]) else 1.0
+            # one projection per call, then a CUDA graph of three calls replayed with new x
+            y1 = iq2_matmul_grouped_sharded(comm, [probs[2]])[0]
+            res[f"m={m} single call"] = rel(y1, c.iq2_xxs_matmul(xs[2], full[2][0], full[2][1], *shapes[2]))
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                iq2_matmul_grouped_sharded(comm, probs[:3])
+            s.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(3):
+                    iq2_matmul_grouped_sharded(comm, probs[:3])
+            for rep in range(3):
+                for i, (n, k) in enumerate(shapes[:3]):
+                    xs[i].copy_(synth.activations(m, k, seed=100 * rep + i, device=dev))
+                with torch.cuda.stream(s):
+                    g.replay()
+                s.synchronize()
+                for i, (n, k) in enumerate(shapes[:3]):
+                    res[f"m={m} graph replay {rep} {n}x{k}"] = rel(
+                        outs[i], c.iq2_xxs_matmul(xs[i], full[i][0], full[i][1], n, k))
+            del g
+        torch.cuda.synchronize()
+        comm.check()
+        # failure detection: rank 1 skips one call, so rank 0's entry wait runs out (bounded)
+        x = synth.activations(1, 4096, seed=5, device=dev)
+        out = comm.symmetric_empty(1, 4096)
+        if rank == 0:
+            iq2_matmul_grouped_sharded(comm, [(x, *slices[0], 4096, 4096, out)])
+            torch.cuda.synchronize()
+            try:
+                comm.check()
+                res["timeout reported"] = 1.0
+            except c.Iq2Error as e:
+                res["timeout reported"] = 0.0 if e.code == _lib.IQ2_ERR_COMM else 1.0
+        dist.barrier()
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception as e:
+        import traceback
+        q.put((rank, repr(e) + traceback.format_exc()))
+
+
+def _spawn(target):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=target, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    try:
+        return [q.get(timeout=300) for _ in range(WORLD)]
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
+def test_fused_exchange_matches_single_gpu_and_nccl():
+    for rank, res in _spawn(_rank_fused):
+        assert isinstance(res, dict), (rank, res)
+        for name, e in res.items():
+            assert e <= TOL, (rank, name, e)
+        if rank == 0:
+            assert "timeout reported" in res
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
