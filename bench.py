@@ -20,9 +20,11 @@ from L2). Synthetic data.
 
 --gpus N > 1 (launched by torchrun, one rank per GPU): every projection is column-sharded over the
 N ranks (rank r holds weight rows [r*N/g, (r+1)*N/g), a contiguous slice), and every rank ends
-with the full outputs through NCCL all-gathers over NVLink (one per step in the batched call, one
-per projection in the per-call path) -- strong scaling of the same workload; value = whole-job
-weight bytes/s, the max over ranks of the device time.
+with the full outputs: by default (--exchange fused) the decode GEMV stores each output into
+every rank's copy over NVLink (outputs in the communicator's symmetric region; one kernel per
+call), or (--exchange nccl) through NCCL all-gathers (one per step in the batched call, one per
+projection in the per-call path) -- strong scaling of the same workload; value = whole-job weight
+bytes/s, the max over ranks of the device time.
 
 --impl reference: the reference's own kernels on the host cores (see above), same metric.
 """
@@ -116,8 +118,10 @@ class Workload:
                 x_elems += m * k
                 out_elems += m * n  # every rank ends with the full outputs
                 self.weight_bytes += synth.packed_bytes(n, k)
+        self.fused = comm is not None and comm.has_symmetric and m <= 16
         self.x_dev = torch.empty(x_elems, dtype=torch.float32, device=device)
-        self.out_dev = torch.empty(out_elems, dtype=torch.float32, device=device)
+        self.out_dev = (comm.symmetric_empty(out_elems) if comm is not None and comm.has_symmetric
+                        else torch.empty(out_elems, dtype=torch.float32, device=device))
         self.x_host = torch.empty(x_elems, dtype=torch.float32, pin_memory=True)
         self.out_host = torch.empty(out_elems, dtype=torch.float32, pin_memory=True)
         ws_cache = {}
@@ -161,14 +165,16 @@ class Workload:
     def launches_per_step(self, grouped: bool = False) -> int:
         """This library's kernels per step (NCCL's all-gather kernels not counted): a GEMV launch,
         plus the x-limb prep when the call has a workspace for it (per 256 projections when
-        grouped), plus on N > 1 GPUs the scatter kernel (not needed for one projection at m = 1)."""
+        grouped), plus with the NCCL exchange on N > 1 GPUs the scatter kernel (not needed for one
+        projection at m = 1). The fused exchange adds no launch."""
         from candelora_metal_kernels_b200 import workspace_bytes
+        scatter = self.world > 1 and not self.fused
         if grouped:
-            return 2 * ((len(self.calls) + 255) // 256) + (1 if self.world > 1 else 0)
+            return 2 * ((len(self.calls) + 255) // 256) + (1 if scatter else 0)
         total = 0
         for (_, _, _, n, k, _, _, _) in self.calls:
             total += 1 if workspace_bytes(self.m, n // self.world, k, torch.float32) == 0 else 2
-            if self.world > 1 and self.m > 1:
+            if scatter and self.m > 1:
                 total += 1
         return total
 
@@ -196,6 +202,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if dist:
         from candelora_metal_kernels_b200.sharded import Iq2Comm
         comm = Iq2Comm()  # the library's NCCL communicator; the NCCL process group carries its id
+        if args.exchange == "fused":  # outputs here: the GEMV stores them into every rank
+            step_out = args.m * args.layers * sum(n for (_, _, n) in synth.LLAMA3_8B_PROJECTIONS) * 4
+            comm.alloc_symmetric(step_out + (32 << 20))  # + the configuration 3/4 decode outputs
     wl = Workload(args.m, args.layers, rank, world, device, comm)
     stream = torch.cuda.Stream(device)
     torch.cuda.synchronize()
@@ -259,7 +268,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     per_call = {"value": round(wl.weight_bytes / (pms / args.steps * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(pms / args.steps, 4),
                 "path": ("224 iq2_xxs_matmul calls per step" if not dist else
-                         "224 column-sharded calls per step, one all-gather each"),
+                         "224 column-sharded calls per step, " + _exchange_words(wl, "each")),
                 "gpu_launches": wl.launches_per_step(False) * args.steps}
 
     # ---- end to end: host x -> device, the step through the public API, outputs -> host
@@ -330,17 +339,18 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "config": {"workload": "config1: Llama-3-8B projections q,k,v,o,gate,up,down x 32 layers, M=1",
                        "m": args.m, "layers": args.layers,
                        "weight_bytes_per_step": wl.weight_bytes,
-                       "parallelism": f"column-shard over {world} GPUs + NCCL all-gather" if world > 1 else "1 GPU",
+                       "parallelism": (f"column-shard over {world} GPUs, " + _exchange_words(wl, "per call"))
+                                      if world > 1 else "1 GPU",
                        "l2": "no flush needed: 1.80 GB of distinct weights per step vs 126 MB L2",
                        "step": ("the 224 projections in one iq2_matmul_grouped call" if world == 1 else
-                                "the 224 projections column-sharded in one iq2_matmul_grouped_sharded call "
-                                "(one NCCL all-gather per step)"),
+                                "the 224 projections column-sharded in one iq2_matmul_grouped_sharded call ("
+                                + _exchange_words(wl, "per step") + ")"),
                        "timing": "CUDA events around K replays of a CUDA graph of one step"},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": wl.x_host.numel() * 4,
                     "d2h_bytes_per_step": wl.out_host.numel() * 4,
                     "path": ("pinned host x -> device, 224 reference-shaped iq2_matmul calls"
-                             + (" (column-sharded, one all-gather each)" if dist else "")
+                             + (" (column-sharded, " + _exchange_words(wl, "each") + ")" if dist else "")
                              + ", outputs -> pinned host")},
             "gpu_launches": wl.launches_per_step(True) * args.steps,
             "per_call": per_call,
@@ -369,6 +379,11 @@ def _ncu_traffic(bytes_per_launch: int):
     return None
 
 
+def _exchange_words(wl, per: str) -> str:
+    return ("fused peer-memory all-gather in the GEMV epilogue, no NCCL call" if wl.fused
+            else f"one NCCL all-gather {per}")
+
+
 # ---------------------------------------------------------------------------------------- models
 def forward_bench(args, wl, device, stream, comm, dist):
     """Benchmark configuration 4: the 32-layer Llama-3-8B linear stack as one forward pass, with
@@ -383,7 +398,9 @@ def forward_bench(args, wl, device, stream, comm, dist):
     res = {}
     for m in (1, 32):
         x0 = synth.activations(m, 4096, seed=4242, device=device, rms_normalize=True)
-        outs = {name: torch.empty(m, n, device=device) for (_, _, _, n, _, _, _, name) in layers[0]}
+        sym = dist and comm.has_symmetric  # the sharded decode stores into every rank's copy
+        outs = {name: (comm.symmetric_empty(m, n) if sym else torch.empty(m, n, device=device))
+                for (_, _, _, n, _, _, _, name) in layers[0]}
 
         def matmuls(probs):
             if dist:
@@ -451,7 +468,8 @@ def ffn70b_bench(args, device, stream, comm, rank, world, peaks):
         probs = []
         for i, (qs, sc, n, k) in enumerate(ws):
             x = synth.activations(m, k, seed=800 + i, dtype=dtype, device=device)
-            probs.append((x, qs, sc, n, k, torch.empty(m, n, device=device)))
+            sym = dist and m <= 16 and comm.has_symmetric
+            probs.append((x, qs, sc, n, k, comm.symmetric_empty(m, n) if sym else torch.empty(m, n, device=device)))
 
         def run():
             if dist:
@@ -487,7 +505,9 @@ def ffn70b_bench(args, device, stream, comm, rank, world, peaks):
             res["m2048"] = {"ms": round(ms, 3), "tflops": round(tf, 1),
                             "frac_bf16_per_gpu": round(tf / world / peaks["bf16_tflops"], 4)}
     return {"workload": "config3: Llama-3-70B FFN gate/up 8192x28672, down 28672x8192, one grouped call"
-                        + (f", column-sharded over {world} GPUs + NCCL all-gather" if dist else ""), **res}
+                        + (f", column-sharded over {world} GPUs (M=1: "
+                           + ("fused peer-memory all-gather" if comm.has_symmetric else "NCCL all-gather")
+                           + "; M=2048: NCCL all-gather)" if dist else ""), **res}
 
 
 # ---------------------------------------------------------------------------------------- GEMM
@@ -634,6 +654,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--no-models", action="store_true", help="skip the configuration 3 and 4 measurements")
+    ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: how the sharded decode's output slices reach every rank")
     ap.add_argument("--gemm-reps", type=int, default=5)
     ap.add_argument("--case", choices=["gemv", "gemm"], default=None,
                     help="run only the dominant kernel's shape (the profiler's small case) and exit")

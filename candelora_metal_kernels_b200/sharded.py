@@ -85,6 +85,10 @@ class Iq2Comm:
         self._symm_used = off + nbytes
         return _device_view(base + off, shape, dtype, self.device, owner=self)
 
+    @property
+    def has_symmetric(self) -> bool:
+        return self._symm is not None
+
     def check(self):
         """Raise if a fused exchange of this communicator timed out (synchronises the device)."""
         with torch.cuda.device(self.device):
