@@ -47,6 +47,8 @@ import torch  # noqa: E402
 
 METRIC = "IQ2_XXS matmul: weight GB/s at M=1, TFLOPS at M=2048, % of roofline"
 LAYERS = 32
+# packed weight bytes of the launch captured in profiles/gemv_kernel_grouped_m1.md (8 layers)
+GROUPED_PROFILE_BYTES = 8 * 56_229_888
 
 
 def _peaks():
@@ -314,11 +316,21 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         per_launch_ms = ms_big / (reps * len(big))
         bytes_per_launch = synth.packed_bytes(n_loc, k)
         achieved = bytes_per_launch / (per_launch_ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": f"gemv_kernel<1,1,0> (x limbs in-kernel), 4096x{n_loc} m=1, one launch per call",
-                "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peak_src,
-                "us_per_launch": round(per_launch_ms * 1e3, 3), "algorithmic_bytes": bytes_per_launch,
-                "traffic": _ncu_traffic(bytes_per_launch)}
+        single = {"kernel": f"gemv_kernel<1,1,0> (x limbs in-kernel), 4096x{n_loc} m=1, one launch per call",
+                  "achieved": round(achieved, 1), "frac": round(achieved / peaks["hbm_gbs"], 4),
+                  "us_per_launch": round(per_launch_ms * 1e3, 3), "algorithmic_bytes": bytes_per_launch,
+                  "traffic": _ncu_traffic("gemv_kernel_4096x14336_m1.md", bytes_per_launch, bytes_per_launch)}
+        # the kernel that dominates the timed region: the step's one grouped GEMV launch (this
+        # rank's rows of all 224 projections); its duration is bounded by the step time, which
+        # also holds the x-limb prep kernel (a few us)
+        step_bytes = sum(synth.packed_bytes(n // world, k) for (_, _, _, n, k, _, _, _) in wl.calls)
+        g_achieved = step_bytes / (ms_per_step * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "gemv_kernel<1,256,-1>: the step's projections in one launch (grouped)",
+                "achieved": round(g_achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(g_achieved / peaks["hbm_gbs"], 4), "peak_source": peak_src,
+                "us_per_launch": round(ms_per_step * 1e3, 2), "algorithmic_bytes": step_bytes,
+                "traffic": _ncu_traffic("gemv_kernel_grouped_m1.md", step_bytes, GROUPED_PROFILE_BYTES),
+                "single_call": single}
         del g2
 
     del graph, ggraph
@@ -367,13 +379,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     return line
 
 
-def _ncu_traffic(bytes_per_launch: int):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "gemv_kernel_4096x14336_m1.md"
+def _ncu_traffic(summary: str, bytes_per_launch: int, profiled_bytes: int):
+    """DRAM bytes per launch from a committed ncu summary (profiles/<summary>), scaled from the
+    captured launch (`profiled_bytes` of packed weights) to this one by the weight bytes each
+    processes (the traffic is the weights streamed once, so it grows in proportion)."""
+    p = ROOT / "profiles" / summary
     try:
         for line in p.read_text().splitlines():
             if line.startswith("dram_bytes_per_launch:"):
-                return int(line.split(":")[1])
+                return int(int(line.split(":")[1]) * bytes_per_launch / profiled_bytes)
     except Exception:
         pass
     return None
@@ -618,10 +632,26 @@ def run_reference(args, rank: int, world: int):
 def run_case(args):
     """Only the dominant kernel on its roofline shape, `--steps` times after two warm calls: the
     command the profiler captures. gemv: 4096x14336 (K x N) at M=1, f32 x, two weight copies
-    (30 MB) in turn; gemm: M=2048 on the same projection, bf16 x."""
+    (30 MB) in turn; gemm: M=2048 on the same projection, bf16 x; grouped: the benchmark step
+    (every projection of `--layers` layers in one iq2_matmul_grouped call, M=1)."""
     import candelora_metal_kernels_b200 as c
     from candelora_metal_kernels_b200 import synth
     torch.cuda.set_device(0)
+    if args.case == "grouped":
+        wl = Workload(1, args.layers, 0, 1, torch.device("cuda", 0))
+        for _ in range(2):
+            wl.step(grouped=True)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            wl.step(grouped=True)
+        e1.record()
+        e1.synchronize()
+        print(json.dumps({"case": "grouped", "m": 1, "layers": args.layers, "weight_bytes": wl.weight_bytes,
+                          "calls": args.steps, "us_per_call": round(e0.elapsed_time(e1) * 1e3 / args.steps, 2)}),
+              flush=True)
+        return
     n, k = 14336, 4096
     m = 1 if args.case == "gemv" else 2048
     dtype = torch.float32 if args.case == "gemv" else torch.bfloat16
@@ -657,7 +687,7 @@ def main():
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
                     help="N > 1: how the sharded decode's output slices reach every rank")
     ap.add_argument("--gemm-reps", type=int, default=5)
-    ap.add_argument("--case", choices=["gemv", "gemm"], default=None,
+    ap.add_argument("--case", choices=["gemv", "gemm", "grouped"], default=None,
                     help="run only the dominant kernel's shape (the profiler's small case) and exit")
     args = ap.parse_args()
     if args.case:

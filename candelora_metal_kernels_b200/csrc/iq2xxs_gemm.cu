@@ -11,7 +11,9 @@
 //     pairs by grid code (IQ2XXS_BF16_SEL), an XOR applies the signs (the 7 stored sign bits and
 //     their parity spread to the bf16 sign bits by one multiply per pair). This is bit-identical to
 //     rounding every weight's exact f32 value (the dequant kernel's bf16). The table is kept small
-//     (2 KB) because the tensor core reads its operands through the same shared memory.
+//     (2 KB, held in 16 interleaved copies so that the 16 lanes of a half-warp, each reading its
+//     own copy, never share a bank) because the tensor core reads its operands through the same
+//     shared memory.
 //   * D: two 128 x BN f32 accumulators in TMEM (512 columns allocated): one CTA computes a tile of
 //     256 tokens x BN weight rows (BN = 256, or 224 when that leaves fewer SMs idle in the last
 //     wave, e.g. 512 tiles instead of 448 on 148 SMs for N = 14336), issuing per 64-k stage
@@ -45,7 +47,8 @@ constexpr int G_A_HALF = 128 * G_BK * 2;        // 16 KB: one 128-token box
 constexpr int G_A_BYTES = 2 * G_A_HALF;         // 32 KB
 constexpr int G_B_BYTES = G_BN * G_BK * 2;      // 32 KB
 constexpr int G_STAGE_BYTES = G_A_BYTES + G_B_BYTES;
-constexpr int G_SEL_BYTES = 256 * 8;            // decode table: selector pairs per grid code
+constexpr int G_SEL_COPIES = 16;                 // the decode table, once per lane of a half-warp
+constexpr int G_SEL_BYTES = 256 * G_SEL_COPIES * 8;  // selector pairs per grid code, interleaved copies
 constexpr int G_SMEM = 1024 /*align*/ + G_STAGES * G_STAGE_BYTES + G_SEL_BYTES + 256 /*barriers*/;
 constexpr uint32_t G_TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: only a broken pipeline waits that long
@@ -177,10 +180,11 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
 // 16-byte chunks at dst ^ (t << 4) (dst: the row's first chunk of the sub-block in the SW128 tile,
 // its low 7 bits the swizzled chunk; t < 4 only flips bits 4-5). Each weight is
 // bf16(d*(2s+1)/8 * g) with g in {8, 25, 43}: the three products are rounded once and a `prmt`
-// picks the bf16 pairs by grid code (sel_s: IQ2XXS_BF16_SEL packed as two words per entry); an
-// XOR applies the signs. TAIL: zero the weights at k >= K (k_lo = the sub-block's first k).
+// picks the bf16 pairs by grid code (sel_l: this lane's copy of IQ2XXS_BF16_SEL, two words per
+// entry, entries 128 bytes apart); an XOR applies the signs. TAIL: zero the weights at k >= K
+// (k_lo = the sub-block's first k).
 template <bool TAIL>
-__device__ __forceinline__ void decode_sub(uint2 q, float d, uint32_t sel_s, uint32_t dst, uint32_t k_lo,
+__device__ __forceinline__ void decode_sub(uint2 q, float d, uint32_t sel_l, uint32_t dst, uint32_t k_lo,
                                            uint32_t K) {
     const uint32_t aux_g = q.x, aux_s = q.y;
     const float dl = d * (float)((aux_s >> 27) | 1u) * 0.125f;  // d*(2s+1)/8, exact
@@ -189,7 +193,7 @@ __device__ __forceinline__ void decode_sub(uint2 q, float d, uint32_t sel_s, uin
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
         const uint32_t gi = (aux_g >> (8 * t)) & 0xFFu, si = (aux_s >> (7 * t)) & 0x7Fu;
-        const uint2 sel = ld_shared_v2_const(sel_s + gi * 8);
+        const uint2 sel = ld_shared_v2_const(sel_l + gi * (G_SEL_COPIES * 8));
         // the 8 sign bits (bit j: weight j negative): 7 stored, the 8th makes their parity even
         const uint32_t S = si | ((__popc(si) & 1u) << 7);
         // (S * K_i) & 0x80008000 puts sign bits 2i and 2i+1 at bits 15 and 31 (the two bf16 sign
@@ -243,10 +247,10 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
     const bool upper = m0 + 128 < p.M;  // the tile's second 128-token half holds tokens
 
     // decode table -> shared memory: per grid entry the four 16-bit prmt selectors packed in two
-    // words
-    for (int i = threadIdx.x; i < 256 * 2; i += blockDim.x) {
-        const uint32_t* e = IQ2XXS_BF16_SEL[i >> 1];
-        reinterpret_cast<uint32_t*>(base + (sel_s - base_s))[i] = (i & 1) ? (e[2] | (e[3] << 16)) : (e[0] | (e[1] << 16));
+    // words, G_SEL_COPIES times (copy c of entry e at (e * G_SEL_COPIES + c) * 8)
+    for (int i = threadIdx.x; i < 256 * G_SEL_COPIES; i += blockDim.x) {
+        const uint32_t* e = IQ2XXS_BF16_SEL[i / G_SEL_COPIES];
+        reinterpret_cast<uint2*>(base + (sel_s - base_s))[i] = make_uint2(e[0] | (e[1] << 16), e[2] | (e[3] << 16));
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < G_STAGES; ++s) {
@@ -326,6 +330,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
         const uint32_t brow = base_s + G_A_BYTES + (r >> 3) * 1024u + (r & 7u) * 128u +
                               ((((hh * 4u) ^ (r & 7u))) << 4);
         const uint32_t kt_full = p.K / G_BK;  // stages below this one have no K tail
+        const uint32_t sel_l = sel_s + (lane & (G_SEL_COPIES - 1)) * 8u;  // this lane's table copy
         // loads run ahead of the decode: the sub-block two stages on, the block scale one block on
         const uint32_t kt_end = kt0 + NKT;
         auto ld_q = [&](uint32_t kt, const uint8_t* ptr) {
@@ -357,8 +362,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
             if (rok) {
                 const float d = half_bits_to_float(dbits);
                 const uint32_t dst = brow + s * G_STAGE_BYTES;
-                if (kt < kt_full) decode_sub<false>(q, d, sel_s, dst, 0, p.K);
-                else decode_sub<true>(q, d, sel_s, dst, kt * G_BK + hh * 32, p.K);
+                if (kt < kt_full) decode_sub<false>(q, d, sel_l, dst, 0, p.K);
+                else decode_sub<true>(q, d, sel_l, dst, kt * G_BK + hh * 32, p.K);
             }
             fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
             __syncwarp();
