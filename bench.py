@@ -11,10 +11,13 @@ from L2). Synthetic data.
              projections in one batched call (iq2_matmul_grouped; CUDA events on the launch
              stream around K back-to-back replays of a CUDA graph holding one step; inputs resident)
   per_call = the same step as 224 reference-shaped iq2_xxs_matmul calls
-  e2e      = the per-call step through the public API with every projection's x copied host->device
-             from pinned memory and every output device->host inside the timed region
-  roofline: the dominant kernel (the decode GEMV of a 4096x14336 gate/up projection, one call)
-            timed alone with CUDA events (64 distinct matrices in rotation, > L2), against measured HBM.
+  e2e      = the same step through the public API (the one grouped call) with every projection's x
+             copied host->device from pinned memory and every output device->host inside the timed
+             region; e2e.per_call: the same with the 224 reference-shaped calls
+  roofline: the dominant kernel of the timed region (the step's one grouped GEMV launch; its
+            duration bounded by the step time) against measured HBM, with ncu DRAM traffic;
+            roofline.single_call: the decode GEMV of one 4096x14336 gate/up projection timed alone
+            with CUDA events (64 distinct matrices in rotation, > L2).
   cpu_baseline: the reference's own kernels (compiled from source for the host, all threads) on
             a bounded sample of the same workload.
 
@@ -273,27 +276,37 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                          "224 column-sharded calls per step, " + _exchange_words(wl, "each")),
                 "gpu_launches": wl.launches_per_step(False) * args.steps}
 
-    # ---- end to end: host x -> device, the step through the public API, outputs -> host
-    def e2e_step():
-        wl.x_dev.copy_(wl.x_host, non_blocking=True)
-        graph.replay()
-        wl.out_host.copy_(wl.out_dev, non_blocking=True)
+    # ---- end to end: host x -> device, the step through the public API, outputs -> host; the
+    # ---- same step as `value` (one grouped call) and, beside it, as 224 reference-shaped calls
+    def e2e_run(g) -> float:
+        def e2e_step():
+            wl.x_dev.copy_(wl.x_host, non_blocking=True)
+            g.replay()
+            wl.out_host.copy_(wl.out_dev, non_blocking=True)
 
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            e2e_step()
-    stream.synchronize()
-    if dist:
-        torch.distributed.barrier()
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        s0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
-        s1.record(stream)
-    s1.synchronize()
-    e2e_ms = max_over_ranks(s0.elapsed_time(s1))
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                e2e_step()
+        stream.synchronize()
+        if dist:
+            torch.distributed.barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            s0.record(stream)
+            for _ in range(args.steps):
+                e2e_step()
+            s1.record(stream)
+        s1.synchronize()
+        return max_over_ranks(s0.elapsed_time(s1))
+
+    e2e_ms = e2e_run(ggraph)
     e2e_value = wl.weight_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
+    e2e_pc_ms = e2e_run(graph)
+    e2e_per_call = {"value": round(wl.weight_bytes / (e2e_pc_ms / args.steps * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(e2e_pc_ms / args.steps, 4),
+                    "path": ("pinned host x -> device, 224 reference-shaped iq2_matmul calls"
+                             + (" (column-sharded, " + _exchange_words(wl, "each") + ")" if dist else "")
+                             + ", outputs -> pinned host")}
 
     # ---- roofline of the dominant kernel: 4096x14336 decode GEMV alone, 64 matrices in rotation
     peaks, peak_src = _peaks()
@@ -361,9 +374,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": wl.x_host.numel() * 4,
                     "d2h_bytes_per_step": wl.out_host.numel() * 4,
-                    "path": ("pinned host x -> device, 224 reference-shaped iq2_matmul calls"
-                             + (" (column-sharded, " + _exchange_words(wl, "each") + ")" if dist else "")
-                             + ", outputs -> pinned host")},
+                    "ms_per_step": round(e2e_ms / args.steps, 4),
+                    "path": ("pinned host x -> device, the step's 224 projections through one "
+                             + ("iq2_matmul_grouped call" if not dist else
+                                "iq2_matmul_grouped_sharded call (" + _exchange_words(wl, "per step") + ")")
+                             + ", outputs -> pinned host"),
+                    "per_call": e2e_per_call},
             "gpu_launches": wl.launches_per_step(True) * args.steps,
             "per_call": per_call,
             "clocks": clocks.summary(),
