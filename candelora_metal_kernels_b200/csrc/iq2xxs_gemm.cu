@@ -318,48 +318,54 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
         }
     } else {
         // ---------------- weight decode (warps 0..15), then epilogue ----------------
-        // thread = (tile row r, sub-block hh of the stage's two). Rows past BN or N are never
-        // stored, so they are left undecoded (whatever the stage holds there only reaches
-        // accumulator columns the epilogue skips).
+        // thread = (tile row r, sub-block hh of the stage's two). Warps whose 32 rows all lie past
+        // BN skip the decode (the MMA never reads those rows); a row past N decodes row N - 1
+        // instead (it only reaches accumulator columns the epilogue skips), so the loop carries no
+        // per-thread condition.
         const uint32_t r = threadIdx.x & 255u, hh = threadIdx.x >> 8;
-        const uint32_t row = n0 + r;
-        const bool rok = r < (uint32_t)BN && row < p.N;
-        const uint8_t* qp = p.qs + (size_t)(rok ? row : 0) * p.nb * QS_BYTES + (size_t)kt0 * 16 + hh * 8;
-        const uint8_t* srow = p.sc + (size_t)(rok ? row : 0) * p.nb * SC_BYTES;
+        const bool live = (r & ~31u) < (uint32_t)BN;  // warp-uniform: BN is a multiple of 32
+        const uint32_t row = min(n0 + r, p.N - 1u);
+        const uint8_t* qrow = p.qs + (size_t)row * p.nb * QS_BYTES + hh * 8;
+        const uint8_t* srow = p.sc + (size_t)row * p.nb * SC_BYTES;
         // this thread's 16-byte chunks of a stage: row r of the SW128 tile, chunk (hh*4 + t) ^ (r%8)
         const uint32_t brow = base_s + G_A_BYTES + (r >> 3) * 1024u + (r & 7u) * 128u +
                               ((((hh * 4u) ^ (r & 7u))) << 4);
         const uint32_t kt_full = p.K / G_BK;  // stages below this one have no K tail
         const uint32_t sel_l = sel_s + (lane & (G_SEL_COPIES - 1)) * 8u;  // this lane's table copy
-        // loads run ahead of the decode: the sub-block two stages on, the block scale one block on
-        const uint32_t kt_end = kt0 + NKT;
-        auto ld_q = [&](uint32_t kt, const uint8_t* ptr) {
-            return rok && kt < kt_end ? __ldg(reinterpret_cast<const uint2*>(ptr)) : make_uint2(0, 0);
+        // loads run ahead of the decode (the sub-block two stages on, the block scale one block
+        // on), clamped to this CTA's last stage and block
+        const uint32_t kt_last = kt0 + NKT - 1u, b_last = b1 - 1u;
+        auto ld_q = [&](uint32_t kt) {
+            return __ldg(reinterpret_cast<const uint2*>(qrow + (size_t)min(kt, kt_last) * 16));
         };
         auto ld_d = [&](uint32_t blk) {
-            return rok && blk < b1 ? (uint32_t)srow[blk * 2] | ((uint32_t)srow[blk * 2 + 1] << 8) : 0u;
+            const uint8_t* e = srow + (size_t)min(blk, b_last) * 2;
+            return (uint32_t)e[0] | ((uint32_t)e[1] << 8);
         };
-        uint2 q1 = ld_q(kt0, qp), q2 = ld_q(kt0 + 1, qp + 16);
+        uint2 q1 = ld_q(kt0), q2 = ld_q(kt0 + 1);
         uint32_t dbits = ld_d(b0), dnext = ld_d(b0 + 1);
         uint32_t s = 0, ph = 0;  // stage slot and the parity of its current use
         for (uint32_t i = 0; i < NKT; ++i) {
             const uint32_t kt = kt0 + i;
             const uint2 q = q1;
             q1 = q2;
-            q2 = ld_q(kt + 2, qp + 32);
-            qp += 16;
+            q2 = ld_q(kt + 2);
             if ((kt & 3) == 0 && i > 0) {
                 dbits = dnext;
                 dnext = ld_d((kt >> 2) + 1);
             }
-            bool go = true;
-            if (lane == 0) go = (i < G_STAGES || mbar_wait(empty(s), ph ^ 1u, p.err, 8u)) && !*abort_flag;
-            go = __shfl_sync(0xFFFFFFFFu, go ? 1 : 0, 0) != 0;  // one decision for the whole warp
-            if (!go) {
-                *abort_flag = 1u;
-                break;
+            if (i >= G_STAGES) {
+                // a wait that runs out (only a broken pipeline) stops this warp; the MMA thread
+                // then runs out of its own waits and stops too
+                bool go = true;
+                if (lane == 0) go = mbar_wait(empty(s), ph ^ 1u, p.err, 8u);
+                go = __shfl_sync(0xFFFFFFFFu, go ? 1 : 0, 0) != 0;  // one decision for the whole warp
+                if (!go) {
+                    *abort_flag = 1u;
+                    break;
+                }
             }
-            if (rok) {
+            if (live) {
                 const float d = half_bits_to_float(dbits);
                 const uint32_t dst = brow + s * G_STAGE_BYTES;
                 if (kt < kt_full) decode_sub<false>(q, d, sel_l, dst, 0, p.K);
