@@ -392,25 +392,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     const uint32_t tb0 = a >> 3, tb1 = (b + 7) >> 3;
     const uint32_t p0 = L.cl_p[cl];
 
-    // ---- the decode table, built from the 1.5 KB compact copy: row e = 32 copies (one per lane)
-    // ---- of the grid selector of code e, then (e < 128) 32 copies of the sign selector of index e
-    {
-        constexpr int PER_THREAD = LUT_BYTES / 16 / (GEMV_WARPS * 32);
-        uint32_t v[PER_THREAD];  // all loads first: one latency, not one per store
-#pragma unroll
-        for (int i = 0; i < PER_THREAD; ++i) {
-            const int c = threadIdx.x + i * GEMV_WARPS * 32;
-            const int row = c >> 4, half = (c >> 3) & 1;
-            v[i] = half == 0 ? __ldg(IQ2XXS_SEL_COMPACT + row)
-                             : (row < 128 ? __ldg(IQ2XXS_SEL_COMPACT + 256 + row) : 0u);
-        }
-#pragma unroll
-        for (int i = 0; i < PER_THREAD; ++i) {
-            const int c = threadIdx.x + i * GEMV_WARPS * 32;
-            *reinterpret_cast<uint4*>(smem + gap + c * 16) = make_uint4(v[i], v[i], v[i], v[i]);
-        }
-    }
-
     // ---- issue side: cp.async stages of one tile-block each, NSTAGES ahead ----
     TbCursor ic;
     if (a < b) cursor_seek(L, p0, tb0, ic);
@@ -470,20 +451,32 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         islot = (islot + 1 == NSTAGES) ? 0 : islot + 1;
     };
 
-    // Until the kernels before this one have finished, the weights may still be being written:
-    // only warm L2 with the first stage (a prefetch brings nothing into the SM, and L2 is
-    // coherent with every writer), then wait, then copy the stages for real.
-    if (a < b) {
-        const GemvProblem& P = L.prob[ic.p];
-        const uint32_t row = ic.rg * ROWS + lane;
-        if (lane < ROWS && row < P.N) {
-            const size_t blk_idx = (size_t)row * P.nb + ic.blk;
-            const uint8_t* q = P.qs + blk_idx * QS_BYTES;
-            prefetch_l2(q);
-            prefetch_l2(q + 32);
-            prefetch_l2(P.sc + blk_idx * SC_BYTES);
+    // The weights are only ever written by kernels that do not release their dependents early
+    // (only this library's GEMV and prep kernels do, and they never write weights), so the first
+    // stages can be copied before the wait: their DRAM latency overlaps the table build and the
+    // previous kernel's tail.
+#pragma unroll
+    for (int i = 0; i < NSTAGES; ++i) issue();
+
+    // ---- the decode table, built from the 1.5 KB compact copy: row e = 32 copies (one per lane)
+    // ---- of the grid selector of code e, then (e < 128) 32 copies of the sign selector of index e
+    {
+        constexpr int PER_THREAD = LUT_BYTES / 16 / (GEMV_WARPS * 32);
+        uint32_t v[PER_THREAD];  // all loads first: one latency, not one per store
+#pragma unroll
+        for (int i = 0; i < PER_THREAD; ++i) {
+            const int c = threadIdx.x + i * GEMV_WARPS * 32;
+            const int row = c >> 4, half = (c >> 3) & 1;
+            v[i] = half == 0 ? __ldg(IQ2XXS_SEL_COMPACT + row)
+                             : (row < 128 ? __ldg(IQ2XXS_SEL_COMPACT + 256 + row) : 0u);
+        }
+#pragma unroll
+        for (int i = 0; i < PER_THREAD; ++i) {
+            const int c = threadIdx.x + i * GEMV_WARPS * 32;
+            *reinterpret_cast<uint4*>(smem + gap + c * 16) = make_uint4(v[i], v[i], v[i], v[i]);
         }
     }
+
     if constexpr (FUSED) {
         constexpr uint32_t XB = XDT == 0 ? 4u : 2u;
         const uint8_t* xp = static_cast<const uint8_t*>(L.x);
@@ -550,8 +543,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         }
         *o = v;
     };
-#pragma unroll
-    for (int i = 0; i < NSTAGES; ++i) issue();
     if constexpr (FUSED) {
         using XT = typename std::conditional<XDT == 0, float, typename std::conditional<XDT == 1, __half, __nv_bfloat16>::type>::type;
         for (uint32_t job = warp; job < TOK * nbx; job += GEMV_WARPS)
