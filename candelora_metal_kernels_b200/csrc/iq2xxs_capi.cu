@@ -126,7 +126,7 @@ int current_device(const char* op, int* dev) {
 
 size_t workspace_for(uint32_t m, uint32_t out_dim, uint32_t in_dim, int x_dtype, int num_sms) {
     if (m == 0 || out_dim == 0 || in_dim == 0) return 0;
-    if (m <= 16) return iq2::gemv_workspace_size(m, out_dim, in_dim, num_sms);
+    if (m <= iq2::kGemvMaxM) return iq2::gemv_workspace_size(m, out_dim, in_dim, num_sms);
     return iq2::gemm_workspace_size(m, out_dim, in_dim, x_dtype, num_sms);
 }
 
@@ -155,7 +155,7 @@ int matmul_impl(const char* op, const void* x, int x_dtype, uint32_t m, const ui
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (variant != IQ2_VARIANT_IQ2_XXS) {  // the other formats: one generic kernel, no workspace
         e = iq2::launch_variant_matmul(variant, x, x_dtype, m, weight_bytes, weight_scales, out_dim, in_dim, out, sms, s);
-    } else if (m <= 16) {
+    } else if (m <= iq2::kGemvMaxM) {
         if (iq2::gemv_fast_path_ok(m, in_dim, weight_bytes, weight_scales)) {
             const size_t need = iq2::gemv_workspace_size(m, out_dim, in_dim, sms);
             if (need > 0 && (workspace == nullptr || workspace_bytes < need))
@@ -183,7 +183,7 @@ int matmul_impl(const char* op, const void* x, int x_dtype, uint32_t m, const ui
 }
 
 // Splits a grouped call into launches: fast-path problems in chunks of gemv_max_group() when
-// m <= 16; everything else one by one. With `ws` NULL only sizes the workspace.
+// m <= kGemvMaxM; everything else one by one. With `ws` NULL only sizes the workspace.
 int grouped_impl(const iq2_matmul_problem* probs, uint32_t count, uint32_t m, int x_dtype, void* ws,
                  size_t ws_bytes, iq2_stream_t stream, size_t* need_out) {
     const char* op = "iq2_matmul_grouped";
@@ -193,7 +193,7 @@ int grouped_impl(const iq2_matmul_problem* probs, uint32_t count, uint32_t m, in
     std::vector<uint32_t> slow;
     for (uint32_t i = 0; i < count; ++i) {
         const iq2_matmul_problem& p = probs[i];
-        if (m <= 16 && iq2::gemv_fast_path_ok(m, p.in_dim, p.weight_bytes, p.weight_scales)) {
+        if (iq2::gemv_fast_path_ok(m, p.in_dim, p.weight_bytes, p.weight_scales)) {
             fast.push_back({p.x, p.weight_bytes, p.weight_scales, p.out_dim, p.in_dim, p.out});
         } else {
             slow.push_back(i);

@@ -1,4 +1,4 @@
-// IQ2_XXS prefill GEMM (m > 16) on the sm_100a tensor cores: tcgen05.mma with TMEM accumulators.
+// IQ2_XXS prefill GEMM (m > 32) on the sm_100a tensor cores: tcgen05.mma with TMEM accumulators.
 //
 // out[m, n] = sum_k x[m, k] * W[n, k] (reference: iq2_xxs_matmul_kernel,
 // src/metal_src/iq2_matmul.metal:188-240, which recomputes the weights per output element) as a

@@ -1,4 +1,4 @@
-// IQ2_XXS decode GEMV for small m (m <= 16) on sm_100a, single or grouped projections.
+// IQ2_XXS decode GEMV for small m (m <= 32) on sm_100a, single or grouped projections.
 //
 // Computes out[m, n] = sum_k x[m, k] * W[n, k] with W the IQ2_XXS weights in the reference's
 // split layout (reference: iq2_xxs_matmul_kernel, src/metal_src/iq2_matmul.metal:188-240;
@@ -15,7 +15,8 @@
 //     tables that each CTA builds, so a warp's random lookups never share a bank) into four
 //     signed int8 weights.
 //   * x is split per (token, 256-block) into four 7-bit signed limbs of a 28-bit fixed-point
-//     value: x @ W^T becomes mma.m16n8k32 s8 x s8 -> s32 per 32-weight sub-block, scaled by the
+//     value (two limbs, 14 bits, for 16 < m <= 32, where the tolerance is the tensor-core
+//     path's): x @ W^T becomes mma.m16n8k32 s8 x s8 -> s32 per 32-weight sub-block, scaled by the
 //     odd integer 2s+1 in s32 (exact, |sum| < 2^31) and turned into f32 once per 256-block with d
 //     and the limb scale. The only rounding is the 2^-28-relative quantisation of x and f32
 //     rounding of per-block partial sums (rel. error ~1e-6).
@@ -53,14 +54,17 @@ constexpr int MAX_PROBLEMS = 256;         // per grouped launch
 constexpr int MAX_CLUSTERS = 96;          // >= SMs / 2 of the device (74 on B200)
 constexpr int SMEM_LIMIT = 227 * 1024;
 
-template <int NT>
+// LB: x limbs per token (4: the 28-bit decode path, m <= 16; 2: 14 bits for 16 < m <= 32, where
+// the eight columns of an n8 tile carry four tokens instead of two).
+template <int NT, int LB = 4>
 struct GemvShape {
     static constexpr int T = NT <= 2 ? 2 : 1;          // 16-row mma tiles per warp
     static constexpr int ROWS = 16 * T;                // rows of a tile
-    static constexpr int TOK = 2 * NT;                 // tokens incl. the zero padding of the last n8 tile
+    static constexpr int TPN = 8 / LB;                 // tokens per n8 tile
+    static constexpr int TOK = TPN * NT;               // tokens incl. the zero padding of the last n8 tile
     static constexpr int STAGE_QS = ROWS * 64;         // one block of qs per row
     static constexpr int STAGE_BYTES = STAGE_QS + ROWS * 4;  // + the aligned scale word per row
-    static constexpr int NSTAGES = T == 2 ? 3 : 6;
+    static constexpr int NSTAGES = T == 2 ? 3 : (LB == 4 ? 6 : 4);  // (LB 2: the partials are twice as large)
     static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;  // per warp
     static constexpr int PART_BYTES = GEMV_WARPS * 2 * TOK * ROWS * 4;  // [warp][first|last][token][row]
     // The table sits at the first 64 KB-aligned shared address of the block's window and the
@@ -70,6 +74,7 @@ struct GemvShape {
 
 int nt_for(uint32_t m) { return m <= 2 ? 1 : (m <= 4 ? 2 : (m <= 8 ? 4 : 8)); }
 int rows_for(uint32_t m) { return nt_for(m) <= 2 ? 32 : 16; }
+int limbs_for(uint32_t m) { return m <= 16 ? 4 : 2; }
 
 // x limbs of one block (256 k) of one x, for the kernel-side layout
 __host__ __device__ inline size_t xs_bytes(uint32_t nb, int nt) { return (size_t)nb * 8 * nt * 256; }
@@ -77,15 +82,15 @@ __host__ __device__ inline size_t cs_bytes(uint32_t nb, int nt) { return (size_t
 
 // ---------------------------------------------------------------------------------------------
 // x -> int8 limb fragments of one (token m, block b). Lane = (sub-block sbi, group t) owns the 8
-// activations k = b*256 + sbi*32 + t*8 + [0, 8). With amax = max |x| over the block and
-// amax = f * 2^E (f in [0.5, 1)):
-//   q = rint(x * 2^(27-E)) (|q| <= 2^27), |q| = L3*2^21 + L2*2^14 + L1*2^7 + L0 (7-bit limbs),
-//   each limb carrying the sign of q; column scale of limb l = 2^(E - 27 + 7l) / 8 (the /8 is
-//   the weight scale's (2s+1)/8). Non-finite blocks get NaN scales, so the output is NaN.
+// activations k = b*256 + sbi*32 + t*8 + [0, 8). With amax = max |x| over the block,
+// amax = f * 2^E (f in [0.5, 1)) and B = 7*LB - 1 bits (27 for four limbs, 13 for two):
+//   q = rint(x * 2^(B-E)) (|q| <= 2^B), |q| = sum of 7-bit limbs L_l * 2^(7l) (the last one at
+//   most 2^6), each limb carrying the sign of q; column scale of limb l = 2^(E - B + 7l) / 8 (the
+//   /8 is the weight scale's (2s+1)/8). Non-finite blocks get NaN scales, so the output is NaN.
 //   Tokens m >= M (the padding of the last n8 tile) get zero limbs and scales.
-// Fragment layout (mma B operand, m16n8k32 "col"), sub-block sb, n8 tile nt:
-//   xb[((sb*NT + nt)*32 + col*4 + t)*8 + i] = limb of group t, element i; col = (m%2)*4 + l.
-template <typename XT, int NT>
+// Fragment layout (mma B operand, m16n8k32 "col"), sub-block sb, n8 tile nt = m / (8/LB):
+//   xb[((sb*NT + nt)*32 + col*4 + t)*8 + i] = limb of group t, element i; col = (m % (8/LB))*LB + l.
+template <typename XT, int NT, int LB = 4>
 __device__ __forceinline__ void limb_job(const XT* __restrict__ x, uint32_t M, uint32_t K, uint32_t m,
                                          uint32_t b, uint8_t* xb, float* colscale, int lane) {
     const int sbi = lane >> 2, t = lane & 3;
@@ -108,37 +113,41 @@ __device__ __forceinline__ void limb_job(const XT* __restrict__ x, uint32_t M, u
     // E from the exponent field (amax normal); 2^(27-E) is then a normal float for E >= -100,
     // and x * 2^(27-E) is exact. Tiny or subnormal blocks take the library path.
     const uint32_t abits = __float_as_uint(amax);
+    constexpr int B = 7 * LB - 1;
     const bool fast = (abits >> 23) >= 27u;  // amax >= 2^-100
     int E = (int)(abits >> 23) - 126;
     if (!fast && !bad && amax > 0.0f) frexpf(amax, &E);
-    const float sc = __uint_as_float((uint32_t)(154 - E) << 23);
-    uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+    const float sc = __uint_as_float((uint32_t)(127 + B - E) << 23);
+    uint32_t lo[LB], hi[LB];
+#pragma unroll
+    for (int l = 0; l < LB; ++l) lo[l] = hi[l] = 0u;
     if (!bad && amax > 0.0f) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int q = (int)rintf(fast ? v[i] * sc : ldexpf(v[i], 27 - E));
+            const int q = (int)rintf(fast ? v[i] * sc : ldexpf(v[i], B - E));
             const uint32_t mag = (uint32_t)(q < 0 ? -q : q);
 #pragma unroll
-            for (int l = 0; l < 4; ++l) {
-                const int limb = (l < 3) ? (int)((mag >> (7 * l)) & 127u) : (int)(mag >> 21);
+            for (int l = 0; l < LB; ++l) {
+                const int limb = (l < LB - 1) ? (int)((mag >> (7 * l)) & 127u) : (int)(mag >> (7 * (LB - 1)));
                 const uint32_t byte = (uint32_t)(uint8_t)(int8_t)(q < 0 ? -limb : limb);
                 if (i < 4) lo[l] |= byte << (8 * i);
                 else hi[l] |= byte << (8 * (i - 4));
             }
         }
     }
-    const uint32_t nt = m >> 1, colbase = (m & 1u) * 4u;
+    constexpr uint32_t TPN = 8 / LB;
+    const uint32_t nt = m / TPN, colbase = (m % TPN) * LB;
     const size_t sb = (size_t)b * 8 + sbi;
 #pragma unroll
-    for (int l = 0; l < 4; ++l) {
+    for (int l = 0; l < LB; ++l) {
         uint2* dst = reinterpret_cast<uint2*>(xb + ((sb * NT + nt) * 32 + (colbase + l) * 4 + t) * 8);
         *dst = make_uint2(lo[l], hi[l]);
     }
-    if (lane < 4) {
+    if (lane < LB) {
         float s;
         if (bad) s = __int_as_float(0x7FC00000);
         else if (amax == 0.0f) s = 0.0f;
-        else s = ldexpf(1.0f, E - 30 + 7 * lane);
+        else s = ldexpf(1.0f, E - B - 3 + 7 * lane);
         colscale[(size_t)b * (NT * 8) + nt * 8 + colbase + lane] = s;
     }
 }
@@ -156,12 +165,12 @@ struct PrepLaunch {
     uint32_t count, M;
 };
 
-// One warp per (x item, token m < 2*NT, block b).
-template <typename XT, int NT, int CAP>
+// One warp per (x item, token m < TOK, block b).
+template <typename XT, int NT, int CAP, int LB = 4>
 __global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ PrepLaunch<CAP> L) {
-    // The GEMV may be scheduled at once: before its own wait it only builds its constant
-    // table and warms L2. x may be written by the previous kernel and the workspace may still
-    // be read by the previous GEMV, so wait for both before touching memory.
+    // The GEMV may be scheduled at once: before its own wait it only copies weights and builds
+    // its constant table. x may be written by the previous kernel and the workspace may still be
+    // read by the previous GEMV, so wait for both before touching memory.
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -170,9 +179,9 @@ __global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ 
     while (it + 1 < L.count && L.item[it + 1].warp_begin <= wid) ++it;
     const PrepItem& P = L.item[it];
     const uint32_t local = wid - P.warp_begin;
-    if (local >= 2u * NT * P.nb) return;
-    limb_job<XT, NT>(static_cast<const XT*>(P.x), L.M, P.K, local / P.nb, local % P.nb, P.xb, P.colscale,
-                     lane);
+    if (local >= (uint32_t)GemvShape<NT, LB>::TOK * P.nb) return;
+    limb_job<XT, NT, LB>(static_cast<const XT*>(P.x), L.M, P.K, local / P.nb, local % P.nb, P.xb, P.colscale,
+                         lane);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -348,9 +357,9 @@ __device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, 
 // whose f32/f16/bf16 x this kernel turns into limbs itself (kernel-side layout in shared memory).
 // P2P: every output is stored at the same offset of every rank's symmetric region (the
 // column-sharded call's all-gather done by the epilogue), ordered by the header words.
-template <int NT, int CAP, int XDT, bool P2P = false>
+template <int NT, int CAP, int XDT, bool P2P = false, int LB = 4>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvLaunch<CAP> L) {
-    using S_ = GemvShape<NT>;
+    using S_ = GemvShape<NT, LB>;
     constexpr bool FUSED = XDT >= 0;
     constexpr int T = S_::T, ROWS = S_::ROWS, TOK = S_::TOK, STAGE_QS = S_::STAGE_QS;
     constexpr int STAGE_BYTES = S_::STAGE_BYTES, NSTAGES = S_::NSTAGES, RING_BYTES = S_::RING_BYTES;
@@ -546,7 +555,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     if constexpr (FUSED) {
         using XT = typename std::conditional<XDT == 0, float, typename std::conditional<XDT == 1, __half, __nv_bfloat16>::type>::type;
         for (uint32_t job = warp; job < TOK * nbx; job += GEMV_WARPS)
-            limb_job<XT, NT>(static_cast<const XT*>(L.x), L.M, L.K, job / nbx, job % nbx, smem + xs_off,
+            limb_job<XT, NT, LB>(static_cast<const XT*>(L.x), L.M, L.K, job / nbx, job % nbx, smem + xs_off,
                              reinterpret_cast<float*>(smem + cs_off), lane);
     }
     __syncthreads();  // the table (and the fused limbs) are complete
@@ -636,13 +645,17 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         for (int tt = 0; tt < T; ++tt) {
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
+                // this lane's columns 2t, 2t+1: with four limbs half of a token's (the other
+                // half in lane t^1), with two limbs all of token nt*4 + t
                 float v0 = F[tt][nt][0] + F[tt][nt][1];
                 float v1 = F[tt][nt][2] + F[tt][nt][3];
-                v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 1);
-                v1 += __shfl_xor_sync(0xFFFFFFFFu, v1, 1);
-                const uint32_t m = nt * 2 + (t >> 1);
+                if (LB == 4) {
+                    v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 1);
+                    v1 += __shfl_xor_sync(0xFFFFFFFFu, v1, 1);
+                }
+                const uint32_t m = LB == 4 ? nt * 2 + (t >> 1) : nt * 4 + t;
                 const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
-                if ((t & 1) == 0) {
+                if (LB == 2 || (t & 1) == 0) {
                     if (complete) {
                         if (m < L.M) {
                             float* o = P.out + (size_t)m * P.ldo;
@@ -784,7 +797,7 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const XT* __restrict_
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct GroupPlan {
-    int nt, rows;
+    int nt, rows, limbs;
     bool fused;
     uint32_t clusters;
     std::vector<uint32_t> cl_tb;      // clusters + 1 tile-block boundaries (whole tiles)
@@ -798,17 +811,17 @@ struct GroupPlan {
     size_t smem;
 };
 
-template <int NT>
+template <int NT, int LB = 4>
 size_t smem_for(bool fused, uint32_t nb) {
-    return GemvShape<NT>::SMEM + (fused ? xs_bytes(nb, NT) + cs_bytes(nb, NT) : 0);
+    return GemvShape<NT, LB>::SMEM + (fused ? xs_bytes(nb, NT) + cs_bytes(nb, NT) : 0);
 }
 
-size_t smem_for_nt(int nt, bool fused, uint32_t nb) {
+size_t smem_for_nt(int nt, int limbs, bool fused, uint32_t nb) {
     switch (nt) {
         case 1: return smem_for<1>(fused, nb);
         case 2: return smem_for<2>(fused, nb);
         case 4: return smem_for<4>(fused, nb);
-        default: return smem_for<8>(fused, nb);
+        default: return limbs == 2 ? smem_for<8, 2>(fused, nb) : smem_for<8>(fused, nb);
     }
 }
 
@@ -847,6 +860,7 @@ GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, i
     GroupPlan pl;
     pl.nt = nt_for(m);
     pl.rows = rows_for(m);
+    pl.limbs = limbs_for(m);
     uint64_t tbs = 0, total_tiles = 0;
     for (uint32_t i = 0; i < count; ++i) {
         const uint32_t nb = (probs[i].k + QK - 1) / QK;
@@ -865,8 +879,8 @@ GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, i
         pl.x_of.push_back(xi);
     }
     // one projection whose limbs fit in shared memory: the GEMV makes them itself
-    pl.fused = count == 1 && pl.nt <= 2 && smem_for_nt(pl.nt, true, pl.nb[0]) <= (size_t)SMEM_LIMIT;
-    pl.smem = smem_for_nt(pl.nt, pl.fused, count ? pl.nb[0] : 0);
+    pl.fused = count == 1 && pl.nt <= 2 && smem_for_nt(pl.nt, pl.limbs, true, pl.nb[0]) <= (size_t)SMEM_LIMIT;
+    pl.smem = smem_for_nt(pl.nt, pl.limbs, pl.fused, count ? pl.nb[0] : 0);
     // clusters: whole tiles, about equal numbers of tile-blocks each
     uint64_t cl = (uint64_t)(max_cl > 0 ? max_cl : 1);
     if (cl > MAX_CLUSTERS) cl = MAX_CLUSTERS;
@@ -909,14 +923,14 @@ GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, i
     return pl;
 }
 
-template <int NT, int CAP, int XDT, bool P2P>
+template <int NT, int CAP, int XDT, bool P2P, int LB>
 cudaError_t launch_gemv_kernel(const GemvLaunch<CAP>& L, const GroupPlan& pl, cudaStream_t stream) {
     static bool attr_set[64] = {};  // per device; an idempotent attribute, so a race is benign
     int dev = 0;
     cudaGetDevice(&dev);
     cudaError_t e;
     if (dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemv_kernel<NT, CAP, XDT, P2P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(gemv_kernel<NT, CAP, XDT, P2P, LB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  SMEM_LIMIT);
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set[dev] = true;
@@ -935,15 +949,16 @@ cudaError_t launch_gemv_kernel(const GemvLaunch<CAP>& L, const GroupPlan& pl, cu
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<NT, CAP, XDT, P2P>, L);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<NT, CAP, XDT, P2P, LB>, L);
 }
 
-template <int NT, int CAP, int XDT>
+template <int NT, int CAP, int XDT, int LB = 4>
 cudaError_t launch_gemv_kernel_p(const GemvLaunch<CAP>& L, const GroupPlan& pl, bool p2p, cudaStream_t stream) {
-    return p2p ? launch_gemv_kernel<NT, CAP, XDT, true>(L, pl, stream) : launch_gemv_kernel<NT, CAP, XDT, false>(L, pl, stream);
+    return p2p ? launch_gemv_kernel<NT, CAP, XDT, true, LB>(L, pl, stream)
+               : launch_gemv_kernel<NT, CAP, XDT, false, LB>(L, pl, stream);
 }
 
-template <int NT, int CAP>
+template <int NT, int CAP, int LB = 4>
 cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
                              uint8_t* ws, const GroupPlan& pl, cudaStream_t stream, const GemvPeers* peers) {
     cudaError_t e;
@@ -962,7 +977,7 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
             it.nb = (pl.xk[xi] + QK - 1) / QK;
             it.warp_begin = warps;
             it.pad = 0;
-            warps += 2u * NT * it.nb;
+            warps += (uint32_t)GemvShape<NT, LB>::TOK * it.nb;
         }
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -975,9 +990,9 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         switch (x_dtype) {
-            case 0: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<float, NT, CAP>, pre); break;
-            case 1: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__half, NT, CAP>, pre); break;
-            default: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__nv_bfloat16, NT, CAP>, pre); break;
+            case 0: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<float, NT, CAP, LB>, pre); break;
+            case 1: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__half, NT, CAP, LB>, pre); break;
+            default: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__nv_bfloat16, NT, CAP, LB>, pre); break;
         }
         if (e != cudaSuccess) return e;
     }
@@ -1007,8 +1022,8 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
     }
     const bool p2p = peers != nullptr;
     if (p2p) L.peers = *peers;
-    if (!pl.fused) e = launch_gemv_kernel_p<NT, CAP, -1>(L, pl, p2p, stream);
-    else if constexpr (NT <= 2 && CAP == 1) {
+    if (!pl.fused) e = launch_gemv_kernel_p<NT, CAP, -1, LB>(L, pl, p2p, stream);
+    else if constexpr (NT <= 2 && CAP == 1 && LB == 4) {
         switch (x_dtype) {
             case 0: e = launch_gemv_kernel_p<NT, CAP, 0>(L, pl, p2p, stream); break;
             case 1: e = launch_gemv_kernel_p<NT, CAP, 1>(L, pl, p2p, stream); break;
@@ -1025,6 +1040,13 @@ template <int NT>
 cudaError_t launch_group_nt(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
                             uint8_t* ws, const GroupPlan& pl, cudaStream_t stream, const GemvPeers* peers) {
     // parameter capacity: a single projection ships ~1 KB of launch parameters, not 16 KB
+    if constexpr (NT == 8) {
+        if (pl.limbs == 2) {  // 16 < m <= 32
+            if (count <= 1) return launch_group_cap<8, 1, 2>(probs, count, m, x_dtype, ws, pl, stream, peers);
+            if (count <= 16) return launch_group_cap<8, 16, 2>(probs, count, m, x_dtype, ws, pl, stream, peers);
+            return launch_group_cap<8, MAX_PROBLEMS, 2>(probs, count, m, x_dtype, ws, pl, stream, peers);
+        }
+    }
     if (count <= 1) return launch_group_cap<NT, 1>(probs, count, m, x_dtype, ws, pl, stream, peers);
     if (count <= 16) return launch_group_cap<NT, 16>(probs, count, m, x_dtype, ws, pl, stream, peers);
     return launch_group_cap<NT, MAX_PROBLEMS>(probs, count, m, x_dtype, ws, pl, stream, peers);
@@ -1033,7 +1055,7 @@ cudaError_t launch_group_nt(const GemvProblemHost* probs, uint32_t count, uint32
 }  // namespace
 
 bool gemv_fast_path_ok(uint32_t m, uint32_t k, const uint8_t* qs, const uint8_t* sc) {
-    return m >= 1 && m <= 16 && k >= 1 && (reinterpret_cast<uintptr_t>(qs) % 16) == 0 &&
+    return m >= 1 && m <= kGemvMaxM && k >= 1 && (reinterpret_cast<uintptr_t>(qs) % 16) == 0 &&
            (reinterpret_cast<uintptr_t>(sc) % 4) == 0;
 }
 

@@ -9,8 +9,10 @@ namespace iq2 {
 
 constexpr int kDtypeBf16 = 2;  // IQ2_DTYPE_BF16 of the C ABI
 
-// Decode GEMV (iq2xxs_gemv.cu), m <= 16. A group is up to gemv_max_group() projections with
-// the same m and x dtype, computed by one prep launch and one GEMV launch.
+// Decode GEMV (iq2xxs_gemv.cu), m <= kGemvMaxM (x in four 7-bit limbs for m <= 16, two for
+// 16 < m <= 32). A group is up to gemv_max_group() projections with the same m and x dtype,
+// computed by one prep launch and one GEMV launch.
+constexpr uint32_t kGemvMaxM = 32;
 struct GemvProblemHost {
     const void* x;
     const uint8_t* qs;

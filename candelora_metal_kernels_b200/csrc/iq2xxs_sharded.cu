@@ -11,7 +11,7 @@
 //
 // Fused exchange: when every output lies in the communicator's symmetric region (allocated by
 // iq2_comm_symmetric_alloc: one device allocation per rank, mapped into every other rank's process
-// with CUDA IPC) and m <= 16, the decode GEMV stores each output value straight into all ranks'
+// with CUDA IPC) and m <= 32, the decode GEMV stores each output value straight into all ranks'
 // regions over NVLink (plain peer stores) and synchronises through flag words at the head of each
 // region: no NCCL call, no gather buffer, no scatter kernel, one launch per call.
 #include <nccl.h>
@@ -99,11 +99,11 @@ std::vector<iq2_matmul_problem> local_problems(const iq2_matmul_problem* probs, 
 
 }  // namespace
 
-// The fused-exchange path is taken when every output lies in the symmetric region and m <= 16.
+// The fused-exchange path is taken when every output lies in the symmetric region and m <= 32.
 // Every input to this decision is the same on all ranks (the region is allocated collectively and
 // carved identically), so all ranks take the same path.
 bool use_peer_path(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t count, uint32_t m) {
-    if (comm->symm == nullptr || m > 16 || count > gemv_max_group()) return false;
+    if (comm->symm == nullptr || m > kGemvMaxM || count > gemv_max_group()) return false;
     const uint8_t* lo = comm->symm + kSymmHeaderBytes;
     const uint8_t* hi = lo + comm->symm_bytes;
     for (uint32_t i = 0; i < count; ++i) {

@@ -85,7 +85,8 @@ size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, 
  * m == 0 is valid and launches nothing (the reference returns an empty [0, out_dim] tensor).
  * weight_*_len are the element counts of the caller's buffers (checked like :246-259).
  * Routing (not part of the contract): IQ2_XXS with m <= 16 runs the decode GEMV (int8 tensor-core
- * decode, f32-accurate), larger m the tcgen05 GEMM (bf16 operands, f32 accumulate); IQ2_XS, IQ2_S
+ * decode, f32-accurate), 16 < m <= 32 the same GEMV with x in 14-bit fixed point (rel. error
+ * ~1e-4), larger m the tcgen05 GEMM (bf16 operands, f32 accumulate); IQ2_XS, IQ2_S
  * and IQ3_S run a generic f32 kernel (src/iq2_matmul.rs:884-1016 numerics, FMA accumulate).
  */
 int iq2_matmul(const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
@@ -129,7 +130,7 @@ size_t iq2_matmul_grouped_workspace_size(const iq2_matmul_problem* problems, uin
 /*
  * `count` independent IQ2_XXS projections with the same m and x dtype, e.g. the q/k/v or
  * gate/up projections of a layer, in as few launches as possible (one x-prep and one GEMV
- * launch per 256 projections when m <= 16; projections that share an x pointer share its
+ * launch per 256 projections when m <= 32; projections that share an x pointer share its
  * preparation). Each problem's result equals iq2_matmul on it. No reference counterpart: the
  * reference issues one dispatch per projection (src/iq2_matmul.rs:316-357); this is the batched
  * form of that call.
@@ -207,7 +208,7 @@ int iq2_comm_destroy(iq2_comm_t comm);  /* collective when a symmetric region ex
  * that size whose storage every other rank of the communicator has mapped (CUDA IPC over NVLink).
  * One region per communicator, freed by iq2_comm_destroy. When every `out` of an
  * iq2_matmul_grouped_sharded call lies in the region (at the same offsets on all ranks) and
- * m <= 16, the decode GEMV stores each output straight into every rank's region: no NCCL call, no
+ * m <= 32, the decode GEMV stores each output straight into every rank's region: no NCCL call, no
  * gather buffer, one kernel launch. Its waits for the other ranks are bounded (about a second);
  * a wait that runs out leaves that call's outputs incomplete and is reported by iq2_comm_check.
  */
@@ -221,7 +222,7 @@ size_t iq2_matmul_grouped_sharded_workspace_size(const iq2_matmul_problem* probl
                                                  uint32_t m, int x_dtype, int world);
 /* Up to 256 projections: their slices through one grouped call, one ncclAllGather of all of them
  * on `stream`, one scatter kernel into the outputs (or, with every output in the symmetric
- * region and m <= 16, the fused exchange above; its weight slices must then be 16-byte (bytes)
+ * region and m <= 32, the fused exchange above; its weight slices must then be 16-byte (bytes)
  * and 4-byte (scales) aligned on every rank). Stream-ordered, collective: every rank makes the
  * same call with the same shapes. */
 int iq2_matmul_grouped_sharded(iq2_comm_t comm, const iq2_matmul_problem* problems, uint32_t count,

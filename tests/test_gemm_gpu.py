@@ -1,4 +1,4 @@
-"""GPU parity of the tensor-core GEMM path (m > 16): tcgen05 MMA over bf16 x and bf16-rounded
+"""GPU parity of the tensor-core GEMM path (m > 32): tcgen05 MMA over bf16 x and bf16-rounded
 weights with f32 accumulation.
 
 Two references:
@@ -29,11 +29,11 @@ def _torch_ref(x: torch.Tensor, qs, sc, n, k):
 
 
 CASES = [  # m, n, k: tails in every dimension, the smallest GEMM m, benchmark shapes
-    (17, 33, 4096), (32, 4096, 4096), (64, 256, 512), (100, 300, 200), (256, 512, 1024),
+    (33, 33, 4096), (48, 4096, 4096), (64, 256, 512), (100, 300, 200), (256, 512, 1024),
     (300, 1000, 2048), (512, 14336, 4096), (2048, 4096, 14336),
     # K split into ranges of 256-blocks when the tiles do not fill the SMs: a K tail inside the
     # last range; one 128-token half (m = 128) and a second half holding one token (m = 129)
-    (40, 512, 4104), (128, 256, 2048), (129, 256, 2048), (32, 4096, 14336),
+    (40, 512, 4104), (128, 256, 2048), (129, 256, 2048), (33, 4096, 14336),
 ]
 
 
@@ -53,7 +53,7 @@ def test_gemm_matches_torch_fp32_of_same_operands(m, n, k, dtype):
     assert rel_l2(y.double().cpu().numpy(), ref.double().cpu().numpy()) <= 1e-4
 
 
-@pytest.mark.parametrize("m,n,k", [(64, 256, 512), (100, 300, 200), (32, 4096, 14336), (40, 512, 4104),
+@pytest.mark.parametrize("m,n,k", [(64, 256, 512), (100, 300, 200), (33, 4096, 14336), (40, 512, 4104),
                                    (512, 14336, 4096), (2048, 4096, 14336)])
 def test_gemm_matches_oracle(oracle, m, n, k):
     qs, sc = synth.iq2xxs_weights(n, k, seed=7 + n)

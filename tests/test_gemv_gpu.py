@@ -1,7 +1,9 @@
 """GPU parity of the matmul path (C ABI via the host binding) against the CPU oracle and the
 reference's golden vectors. Tolerances (from the benchmark specification): f32/f16/bf16-activation
 decode path (m <= 16) relative L2 <= 1e-4; plus the reference test's own criterion, every
-|diff| <= 2e-3 on its fixture (src/iq2_matmul.rs:1107-1125)."""
+|diff| <= 2e-3 on its fixture (src/iq2_matmul.rs:1107-1125). For 16 < m <= 32 the same GEMV runs
+with x in two 7-bit limbs (14-bit fixed point per 256-block); the specification's bound there is the
+tensor-core path's 2e-2, and the tests hold it to 2e-3 (the error is ~1e-4)."""
 import numpy as np
 import pytest
 import torch
@@ -13,6 +15,7 @@ from conftest import rel_l2
 pytestmark = pytest.mark.gpu
 
 GEMV_TOL = 1e-4
+WIDE_TOL = 2e-3  # 16 < m <= 32 (two limbs)
 
 
 def _dev(a: np.ndarray) -> torch.Tensor:
@@ -67,6 +70,41 @@ def test_gemv_matches_oracle(oracle, m, n, k, dtype):
     ref = oracle.matmul(xo, qs.numpy(), sc.numpy(), n, k, cols=cols,
                         x_dtype="f32" if dtype == torch.float32 else "bf16")
     assert rel_l2(y[:, cols], ref) <= GEMV_TOL
+
+
+WIDE_CASES = [(17, 33, 4096), (20, 100, 1000), (24, 4096, 4096), (31, 7, 300), (32, 14336, 4096),
+              (32, 4096, 14336)]
+
+
+@pytest.mark.parametrize("m,n,k", WIDE_CASES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gemv_two_limbs_matches_oracle(oracle, m, n, k, dtype):
+    qs, sc = synth.iq2xxs_weights(n, k, seed=n * 17 + k)
+    x = synth.activations(m, k, seed=m * 3 + n, dtype=dtype)
+    y = c.iq2_xxs_matmul(x.cuda(), qs.cuda(), sc.cuda(), n, k).cpu().numpy()
+    cols = np.unique(np.concatenate([np.arange(min(n, 16)), np.random.default_rng(n).integers(0, n, 24),
+                                     [n - 1]]))
+    xo = x.float().numpy() if dtype == torch.float32 else x.view(torch.int16).numpy().view(np.uint16)
+    ref = oracle.matmul(xo, qs.numpy(), sc.numpy(), n, k, cols=cols,
+                        x_dtype="f32" if dtype == torch.float32 else "bf16")
+    assert rel_l2(y[:, cols], ref) <= WIDE_TOL
+
+
+def test_gemv_two_limbs_grouped_and_full_output():
+    """m = 32 through one grouped launch (four projections sharing x, the prep kernel writing two
+    limbs per token) equals the single calls, and the whole output is within the bound of the
+    exact product (f32 dequant x f64)."""
+    m, k = 32, 4096
+    shapes = [4096, 1024, 14336, 96]
+    W = [tuple(t.cuda() for t in synth.iq2xxs_weights(n, k, seed=50 + i)) for i, n in enumerate(shapes)]
+    x = synth.activations(m, k, seed=51, device="cuda")
+    ys = c.iq2_matmul_grouped([(x, W[i][0], W[i][1], n, k) for i, n in enumerate(shapes)])
+    for i, n in enumerate(shapes):
+        single = c.iq2_xxs_matmul(x, W[i][0], W[i][1], n, k)
+        assert rel_l2(ys[i].double().cpu().numpy(), single.double().cpu().numpy()) <= 1e-6
+        w = c.iq2_dequantize(W[i][0], W[i][1], n, k, dtype=torch.float32)
+        exact = x.double() @ w.double().T
+        assert rel_l2(ys[i].double().cpu().numpy(), exact.cpu().numpy()) <= WIDE_TOL
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 14336, 4096), (4, 4096, 14336), (16, 1024, 4096)])

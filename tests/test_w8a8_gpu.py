@@ -4,7 +4,8 @@ reference's W8A8 kernels do (src/metal_src/iq2_matmul.metal:85-102, :437-499), t
 
 Against the reference's own W8A8 kernel outputs (golden vectors, its parity fixture: the
 reference test's 3e-3 absolute bound and our rel. L2 bound) and against the oracle restatement at
-larger sizes: rel. L2 <= 1e-4 on the decode path (m <= 16), <= 2e-2 on the bf16 tensor-core path."""
+larger sizes: rel. L2 <= 1e-4 on the decode path (m <= 16), <= 2e-2 above it (two-limb GEMV for m <= 32,
+the bf16 tensor-core path beyond)."""
 import numpy as np
 import pytest
 import torch
@@ -41,7 +42,7 @@ def test_w8a8_benchmark_distribution_golden(golden):
 
 
 @pytest.mark.parametrize("m,n,k,tol", [(1, 4096, 4096, 1e-4), (5, 1000, 2304, 1e-4), (16, 333, 700, 1e-4),
-                                       (64, 512, 1024, 2e-2), (300, 1024, 4096, 2e-2)])
+                                       (32, 700, 1024, 2e-2), (64, 512, 1024, 2e-2), (300, 1024, 4096, 2e-2)])
 def test_w8a8_matches_oracle(oracle, m, n, k, tol):
     qs, sc = synth.iq2xxs_weights(n, k, seed=n + m)
     x = synth.activations(m, k, seed=m)
