@@ -60,7 +60,7 @@ class Iq2Comm:
 
     def alloc_symmetric(self, nbytes: int):
         """Collective: give this communicator a symmetric output region of `nbytes` (same on every
-        rank). Outputs carved from it with symmetric_empty let the sharded decode (m <= 16)
+        rank). Outputs carved from it with symmetric_empty let the sharded decode (m <= 32)
         store straight into every rank's copy instead of going through an NCCL all-gather."""
         ptr = ctypes.c_void_p()
         with torch.cuda.device(self.device):
