@@ -117,9 +117,6 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
 
 // Global-memory flag words with system-scope ordering (peer GPUs' memory mapped into this
 // process is global memory too) and the wall clock that bounds every wait on them.
-__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
 __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");

@@ -104,11 +104,11 @@ std::vector<iq2_matmul_problem> local_problems(const iq2_matmul_problem* probs, 
 // carved identically), so all ranks take the same path.
 bool use_peer_path(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t count, uint32_t m) {
     if (comm->symm == nullptr || m > kGemvMaxM || count > gemv_max_group()) return false;
-    const uint8_t* lo = comm->symm + kSymmHeaderBytes;
-    const uint8_t* hi = lo + comm->symm_bytes;
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(comm->symm) + kSymmHeaderBytes;
+    const uintptr_t hi = lo + comm->symm_bytes;
     for (uint32_t i = 0; i < count; ++i) {
-        const uint8_t* o = reinterpret_cast<const uint8_t*>(probs[i].out);
-        if (o < lo || o + (size_t)m * probs[i].out_dim * sizeof(float) > hi) return false;
+        const uintptr_t o = reinterpret_cast<uintptr_t>(probs[i].out);
+        if (o < lo || o > hi || (uint64_t)m * probs[i].out_dim * sizeof(float) > hi - o) return false;
     }
     return true;
 }
