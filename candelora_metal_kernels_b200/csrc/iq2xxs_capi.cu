@@ -317,6 +317,19 @@ int iq2_matmul_with_activation_quant(const void* x, int x_dtype, uint32_t m,
             rc = iq2::capi_validate_matmul(op, x, x_dtype, m, weight_bytes, weight_bytes_len, weight_scales,
                                            weight_scales_len, out_dim, in_dim, out, variant);
             if (rc != IQ2_OK || m == 0) return rc;
+            if (variant == IQ2_VARIANT_IQ2_XXS && m <= iq2::kGemvW8A8MaxM &&
+                iq2::gemv_fast_path_ok(m, in_dim, weight_bytes, weight_scales)) {
+                // decode: the int8 activations go straight into the GEMV as its single limb
+                const size_t need = iq2::gemv_w8a8_workspace_size(m, out_dim, in_dim);
+                if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+                    return fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
+                                workspace ? workspace_bytes : (size_t)0);
+                const cudaError_t e = iq2::launch_gemv_w8a8(x, x_dtype, m, weight_bytes, weight_scales, out_dim, in_dim,
+                                                            out, workspace, num_sms_for_current_device(),
+                                                            reinterpret_cast<cudaStream_t>(stream));
+                if (e != cudaSuccess) return cuda_fail(op, e);
+                return IQ2_OK;
+            }
             const size_t xq_bytes = ((size_t)m * in_dim * sizeof(float) + 255) / 256 * 256;
             const size_t need = xq_bytes + (variant == IQ2_VARIANT_IQ2_XXS
                                                 ? workspace_for(m, out_dim, in_dim, IQ2_DTYPE_F32, num_sms_for_current_device())
@@ -349,9 +362,16 @@ size_t iq2_matmul_with_activation_quant_workspace_size(uint32_t m, uint32_t out_
                                                       int x_dtype, int variant, int act_mode) {
     if (act_mode != IQ2_ACT_QUANT_W8A8) return iq2_matmul_workspace_size(m, out_dim, in_dim, x_dtype, variant);
     if (m == 0 || out_dim == 0 || in_dim == 0 || variant < IQ2_VARIANT_IQ2_XXS || variant > IQ2_VARIANT_IQ3_S) return 0;
-    return ((size_t)m * in_dim * sizeof(float) + 255) / 256 * 256 +
-           (variant == IQ2_VARIANT_IQ2_XXS ? workspace_for(m, out_dim, in_dim, IQ2_DTYPE_F32, num_sms_for_current_device())
-                                           : 0);
+    const size_t qdq = ((size_t)m * in_dim * sizeof(float) + 255) / 256 * 256 +
+                       (variant == IQ2_VARIANT_IQ2_XXS
+                            ? workspace_for(m, out_dim, in_dim, IQ2_DTYPE_F32, num_sms_for_current_device())
+                            : 0);
+    // the decode path (int8 activations into the GEMV) needs less; the larger of the two is asked
+    // for so that either path can run with it
+    const size_t gemv = (variant == IQ2_VARIANT_IQ2_XXS && m <= iq2::kGemvW8A8MaxM)
+                            ? iq2::gemv_w8a8_workspace_size(m, out_dim, in_dim)
+                            : 0;
+    return std::max(qdq, gemv);
 }
 
 size_t iq2_matmul_grouped_workspace_size(const iq2_matmul_problem* problems, uint32_t count,

@@ -55,16 +55,18 @@ constexpr int MAX_CLUSTERS = 96;          // >= SMs / 2 of the device (74 on B20
 constexpr int SMEM_LIMIT = 227 * 1024;
 
 // LB: x limbs per token (4: the 28-bit decode path, m <= 16; 2: 14 bits for 16 < m <= 32, where
-// the eight columns of an n8 tile carry four tokens instead of two).
+// the eight columns of an n8 tile carry four tokens instead of two; 1: the int8 activations of
+// the W8A8 mode, eight tokens per n8 tile).
 template <int NT, int LB = 4>
 struct GemvShape {
-    static constexpr int T = NT <= 2 ? 2 : 1;          // 16-row mma tiles per warp
+    static constexpr int T = ((NT <= 2 && LB != 1) || (NT == 1 && LB == 1)) ? 2 : 1;  // 16-row mma tiles per warp
     static constexpr int ROWS = 16 * T;                // rows of a tile
     static constexpr int TPN = 8 / LB;                 // tokens per n8 tile
     static constexpr int TOK = TPN * NT;               // tokens incl. the zero padding of the last n8 tile
     static constexpr int STAGE_QS = ROWS * 64;         // one block of qs per row
     static constexpr int STAGE_BYTES = STAGE_QS + ROWS * 4;  // + the aligned scale word per row
-    static constexpr int NSTAGES = T == 2 ? 3 : (LB == 4 ? 6 : 4);  // (LB 2: the partials are twice as large)
+    // fewer stages where the partials (TOK x ROWS per warp slot) are large
+    static constexpr int NSTAGES = T == 2 ? 3 : ((LB == 4 || (LB == 1 && NT <= 2)) ? 6 : 4);
     static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;  // per warp
     static constexpr int PART_BYTES = GEMV_WARPS * 2 * TOK * ROWS * 4;  // [warp][first|last][token][row]
     // The table sits at the first 64 KB-aligned shared address of the block's window and the
@@ -75,6 +77,7 @@ struct GemvShape {
 int nt_for(uint32_t m) { return m <= 2 ? 1 : (m <= 4 ? 2 : (m <= 8 ? 4 : 8)); }
 int rows_for(uint32_t m) { return nt_for(m) <= 2 ? 32 : 16; }
 int limbs_for(uint32_t m) { return m <= 16 ? 4 : 2; }
+int nt_w8a8(uint32_t m) { return m <= 8 ? 1 : (m <= 16 ? 2 : 4); }  // one limb: 8 tokens per n8 tile
 
 // x limbs of one block (256 k) of one x, for the kernel-side layout
 __host__ __device__ inline size_t xs_bytes(uint32_t nb, int nt) { return (size_t)nb * 8 * nt * 256; }
@@ -182,6 +185,57 @@ __global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ 
     if (local >= (uint32_t)GemvShape<NT, LB>::TOK * P.nb) return;
     limb_job<XT, NT, LB>(static_cast<const XT*>(P.x), L.M, P.K, local / P.nb, local % P.nb, P.xb, P.colscale,
                          lane);
+}
+
+// W8A8 activations (the reference's per-row int8 quantisation, src/metal_src/iq2_matmul.metal:
+// 85-102): inv = 127 / max|x| over the row (1 when that is below 1e-8), q = clamp(round(x * inv),
+// -127, 127). The int8 q is the GEMV's single limb (col = m % 8, n8 tile m / 8); the column scale
+// (1/inv)/8 is the same for every block of the row (the /8 is the weight scale's (2s+1)/8), so
+// x' = q / inv times the weights is computed with one rounding of 1/inv instead of one per
+// element. A row with a non-finite value gets NaN scales (its outputs are NaN). One warp per
+// (x item, token m < 8*NT, block b), each reading its whole row for the maximum (from L2);
+// tokens m >= M get zeros.
+template <typename XT, int NT, int CAP>
+__global__ void __launch_bounds__(256) gemv_prep_w8a8_kernel(const __grid_constant__ PrepLaunch<CAP> L) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    uint32_t it = 0;
+    while (it + 1 < L.count && L.item[it + 1].warp_begin <= wid) ++it;
+    const PrepItem& P = L.item[it];
+    const uint32_t local = wid - P.warp_begin;
+    if (local >= 8u * NT * P.nb) return;
+    const uint32_t m = local / P.nb, b = local % P.nb;
+    const XT* xr = static_cast<const XT*>(P.x) + (size_t)min(m, L.M - 1u) * P.K;
+    const bool live = m < L.M;
+    float amax = 0.0f;
+    if (live)
+        for (uint32_t k = lane; k < P.K; k += 32) amax = fmaxf(amax, fabsf(to_f32(xr[k])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+    const bool bad = !isfinite(amax);
+    const float inv = amax < 1e-8f ? 1.0f : 127.0f / amax;
+    const float scale = bad ? __int_as_float(0x7FC00000) : (live ? __fdiv_rn(1.0f, inv) * 0.125f : 0.0f);
+    const int sbi = lane >> 2, t = lane & 3;
+    const uint32_t nt = m >> 3, col = m & 7u;
+    {
+        const size_t k0 = (size_t)b * QK + sbi * 32 + t * 8;
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const size_t k = k0 + i;
+            float q = 0.0f;
+            if (live && !bad && k < P.K)
+                q = fminf(fmaxf(roundf(__fmul_rn(to_f32(xr[k]), inv)), -127.0f), 127.0f);
+            const uint32_t byte = (uint32_t)(uint8_t)(int8_t)(int)q;
+            if (i < 4) lo |= byte << (8 * i);
+            else hi |= byte << (8 * (i - 4));
+        }
+        const size_t sb = (size_t)b * 8 + sbi;
+        *reinterpret_cast<uint2*>(P.xb + ((sb * NT + nt) * 32 + col * 4 + t) * 8) = make_uint2(lo, hi);
+        if (lane == 0) P.colscale[(size_t)b * (NT * 8) + nt * 8 + col] = scale;
+    }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -295,11 +349,10 @@ __device__ __forceinline__ void decode_group(const DecodeK& k, uint32_t aux_g, u
 // sub-block initialises I, so I needs no clearing. PARTIAL: only sub-blocks [s_lo, s_hi) count
 // (the first/last stage of a warp's range); the others see zero x fragments. FUSED: fragments
 // from shared memory (xsp: shared address), else from global memory (xbp).
-template <int NT, bool PARTIAL, bool FUSED>
+template <int NT, int T, bool PARTIAL, bool FUSED>
 __device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, const uint8_t* xbp, uint32_t xsp,
                                               uint32_t s_lo, uint32_t s_hi, uint32_t rowbase, uint32_t swz,
-                                              int (&I)[GemvShape<NT>::T][NT][4]) {
-    constexpr int T = GemvShape<NT>::T;
+                                              int (&I)[T][NT][4]) {
 #pragma unroll
     for (int pair = 0; pair < 4; ++pair) {
         // one 16-byte chunk = sub-blocks 2*pair and 2*pair+1 of a row
@@ -592,9 +645,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         const uint8_t* xbp = FUSED ? nullptr : P.xb + (size_t)cc.blk * 8 * NT * 256 + lane * 8;
         const uint32_t xsp = xs_s + cc.blk * 8 * NT * 256 + lane * 8;
         if (s_lo == 0 && s_hi == 8)
-            stage_compute<NT, false, FUSED>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
+            stage_compute<NT, T, false, FUSED>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
         else
-            stage_compute<NT, true, FUSED>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
+            stage_compute<NT, T, true, FUSED>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
 
         // Block epilogue: s32 -> f32 with d (per row) and the limb scale (per column).
         {
@@ -645,6 +698,31 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         for (int tt = 0; tt < T; ++tt) {
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
+                const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
+                if (LB == 1) {
+                    // one limb: the lane's four values are four outputs (tokens nt*8 + 2t and
+                    // nt*8 + 2t + 1, rows r0 and r1)
+                    const uint32_t m0 = nt * 8 + 2 * t, m1 = m0 + 1;
+                    if (complete) {
+                        if (m0 < L.M) {
+                            float* o = P.out + (size_t)m0 * P.ldo;
+                            if (row0 + r0 < P.N) put(o + row0 + r0, F[tt][nt][0]);
+                            if (row0 + r1 < P.N) put(o + row0 + r1, F[tt][nt][2]);
+                        }
+                        if (m1 < L.M) {
+                            float* o = P.out + (size_t)m1 * P.ldo;
+                            if (row0 + r0 < P.N) put(o + row0 + r0, F[tt][nt][1]);
+                            if (row0 + r1 < P.N) put(o + row0 + r1, F[tt][nt][3]);
+                        }
+                    } else {
+                        pslot[m0 * ROWS + r0] = F[tt][nt][0];
+                        pslot[m1 * ROWS + r0] = F[tt][nt][1];
+                        pslot[m0 * ROWS + r1] = F[tt][nt][2];
+                        pslot[m1 * ROWS + r1] = F[tt][nt][3];
+                    }
+                    F[tt][nt][0] = F[tt][nt][1] = F[tt][nt][2] = F[tt][nt][3] = 0.0f;
+                    continue;
+                }
                 // this lane's columns 2t, 2t+1: with four limbs half of a token's (the other
                 // half in lane t^1), with two limbs all of token nt*4 + t
                 float v0 = F[tt][nt][0] + F[tt][nt][1];
@@ -654,7 +732,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                     v1 += __shfl_xor_sync(0xFFFFFFFFu, v1, 1);
                 }
                 const uint32_t m = LB == 4 ? nt * 2 + (t >> 1) : nt * 4 + t;
-                const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
                 if (LB == 2 || (t & 1) == 0) {
                     if (complete) {
                         if (m < L.M) {
@@ -817,6 +894,13 @@ size_t smem_for(bool fused, uint32_t nb) {
 }
 
 size_t smem_for_nt(int nt, int limbs, bool fused, uint32_t nb) {
+    if (limbs == 1) {
+        switch (nt) {
+            case 1: return smem_for<1, 1>(fused, nb);
+            case 2: return smem_for<2, 1>(fused, nb);
+            default: return smem_for<4, 1>(fused, nb);
+        }
+    }
     switch (nt) {
         case 1: return smem_for<1>(fused, nb);
         case 2: return smem_for<2>(fused, nb);
@@ -856,11 +940,12 @@ int max_active_clusters(int num_sms) {
 }
 
 // max_cl: clusters the device can run at once (0 when only the workspace size is wanted).
-GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int max_cl) {
+// w8a8: the activations as the W8A8 mode's int8 (one limb, m <= 32).
+GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int max_cl, bool w8a8 = false) {
     GroupPlan pl;
-    pl.nt = nt_for(m);
-    pl.rows = rows_for(m);
-    pl.limbs = limbs_for(m);
+    pl.nt = w8a8 ? nt_w8a8(m) : nt_for(m);
+    pl.rows = w8a8 ? (pl.nt == 1 ? 32 : 16) : rows_for(m);
+    pl.limbs = w8a8 ? 1 : limbs_for(m);
     uint64_t tbs = 0, total_tiles = 0;
     for (uint32_t i = 0; i < count; ++i) {
         const uint32_t nb = (probs[i].k + QK - 1) / QK;
@@ -879,7 +964,7 @@ GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, i
         pl.x_of.push_back(xi);
     }
     // one projection whose limbs fit in shared memory: the GEMV makes them itself
-    pl.fused = count == 1 && pl.nt <= 2 && smem_for_nt(pl.nt, pl.limbs, true, pl.nb[0]) <= (size_t)SMEM_LIMIT;
+    pl.fused = !w8a8 && count == 1 && pl.nt <= 2 && smem_for_nt(pl.nt, pl.limbs, true, pl.nb[0]) <= (size_t)SMEM_LIMIT;
     pl.smem = smem_for_nt(pl.nt, pl.limbs, pl.fused, count ? pl.nb[0] : 0);
     // clusters: whole tiles, about equal numbers of tile-blocks each
     uint64_t cl = (uint64_t)(max_cl > 0 ? max_cl : 1);
@@ -977,7 +1062,7 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
             it.nb = (pl.xk[xi] + QK - 1) / QK;
             it.warp_begin = warps;
             it.pad = 0;
-            warps += (uint32_t)GemvShape<NT, LB>::TOK * it.nb;
+            warps += (uint32_t)GemvShape<NT, LB>::TOK * it.nb;  // one warp per (token, block)
         }
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -989,10 +1074,18 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
         cfg.stream = stream;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        switch (x_dtype) {
-            case 0: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<float, NT, CAP, LB>, pre); break;
-            case 1: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__half, NT, CAP, LB>, pre); break;
-            default: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__nv_bfloat16, NT, CAP, LB>, pre); break;
+        if constexpr (LB == 1) {
+            switch (x_dtype) {
+                case 0: e = cudaLaunchKernelEx(&cfg, gemv_prep_w8a8_kernel<float, NT, CAP>, pre); break;
+                case 1: e = cudaLaunchKernelEx(&cfg, gemv_prep_w8a8_kernel<__half, NT, CAP>, pre); break;
+                default: e = cudaLaunchKernelEx(&cfg, gemv_prep_w8a8_kernel<__nv_bfloat16, NT, CAP>, pre); break;
+            }
+        } else {
+            switch (x_dtype) {
+                case 0: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<float, NT, CAP, LB>, pre); break;
+                case 1: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__half, NT, CAP, LB>, pre); break;
+                default: e = cudaLaunchKernelEx(&cfg, gemv_prep_kernel<__nv_bfloat16, NT, CAP, LB>, pre); break;
+            }
         }
         if (e != cudaSuccess) return e;
     }
@@ -1082,6 +1175,23 @@ cudaError_t launch_gemv_group(const GemvProblemHost* probs, uint32_t count, uint
         case 2: return launch_group_nt<2>(probs, count, m, x_dtype, ws, pl, stream, peers);
         case 4: return launch_group_nt<4>(probs, count, m, x_dtype, ws, pl, stream, peers);
         default: return launch_group_nt<8>(probs, count, m, x_dtype, ws, pl, stream, peers);
+    }
+}
+
+size_t gemv_w8a8_workspace_size(uint32_t m, uint32_t n, uint32_t k) {
+    GemvProblemHost p{nullptr, nullptr, nullptr, n, k, nullptr};
+    return plan_group(&p, 1, m, 0, true).total;
+}
+
+cudaError_t launch_gemv_w8a8(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
+                             uint32_t n, uint32_t k, float* out, void* workspace, int num_sms, cudaStream_t stream) {
+    GemvProblemHost p{x, qs, sc, n, k, out};
+    const GroupPlan pl = plan_group(&p, 1, m, max_active_clusters(num_sms), true);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    switch (pl.nt) {
+        case 1: return launch_group_cap<1, 1, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
+        case 2: return launch_group_cap<2, 1, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
+        default: return launch_group_cap<4, 1, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
     }
 }
 

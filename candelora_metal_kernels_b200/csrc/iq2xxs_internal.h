@@ -57,6 +57,12 @@ size_t gemv_group_workspace_size(const GemvProblemHost* probs, uint32_t count, u
 cudaError_t launch_gemv_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
                               void* workspace, int num_sms, cudaStream_t stream, const GemvPeers* peers = nullptr);
 size_t gemv_workspace_size(uint32_t m, uint32_t n, uint32_t k, int num_sms);
+// The W8A8 mode's decode (m <= kGemvW8A8MaxM): x quantised per row to int8 (the reference's
+// numerics), the int8 values fed to the GEMV as its only limb.
+constexpr uint32_t kGemvW8A8MaxM = 32;
+size_t gemv_w8a8_workspace_size(uint32_t m, uint32_t n, uint32_t k);
+cudaError_t launch_gemv_w8a8(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
+                             uint32_t n, uint32_t k, float* out, void* workspace, int num_sms, cudaStream_t stream);
 cudaError_t launch_gemv(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
                         uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,
                         cudaStream_t stream);
