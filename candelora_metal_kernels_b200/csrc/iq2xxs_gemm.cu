@@ -30,6 +30,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstring>
 
 namespace iq2 {
 
@@ -66,6 +67,7 @@ struct GemmParams {
     uint32_t* err;  // error word (0 = ok); set on a pipeline timeout
     uint32_t M, N, K, nb;
     uint32_t splits;  // K split into this many ranges of whole 256-blocks (blockIdx.z)
+    uint32_t tma_out;  // the epilogue stores through the output tensor map (N % 4 == 0, aligned out)
 };
 
 // ---- mbarrier / tcgen05 / TMA wrappers (inline PTX) ----
@@ -125,6 +127,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "l"(map), "r"(bar), "r"(x), "r"(y)
         : "memory");
 }
+
+// TMA store of a 32 x 32 f32 tile (128-byte swizzled rows in shared memory) to the output tensor
+// [splits][M][N]; rows and columns outside the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+                 "r"(src), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -220,6 +233,7 @@ __device__ __forceinline__ void decode_sub(uint2 q, float d, uint32_t sel_l, uin
 // layout is always sized for 256 rows.
 template <int BN>
 __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                            const __grid_constant__ CUtensorMap tmap_out,
                                                             const GemmParams p) {
     static_assert(BN % 32 == 0 && BN <= G_BN, "BN");
     extern __shared__ uint8_t smem_raw[];
@@ -386,7 +400,42 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
         ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;  // the TMEM loads below are warp-wide
         // accumulator, TMEM lane quadrant (fixed by the warp's rank in its group of 4), column half
         const uint32_t acc = (warp >> 2) & 1, quad = warp & 3, chalf = warp >> 3;
-        if (ok && (acc == 0 || upper)) {
+        if (ok && (acc == 0 || upper) && p.tma_out) {
+            // each warp's 32 x 32 tiles leave through TMA stores, staged in two 4 KB buffers of
+            // the (now idle) stage ring: row `lane` of a tile in the 128-byte swizzle the tensor
+            // map expects (16-byte chunk j at j ^ (lane % 8)), so the stores are whole lines and
+            // overlap the next tile's TMEM load
+            tc_fence_after();
+            const uint32_t token0 = m0 + acc * 128 + quad * 32;
+            const uint32_t buf0 = base_s + (uint32_t)warp * 8192u;
+            int it = 0;
+#pragma unroll 1
+            for (int c = (int)chalf; c < BN / 32; c += 2, ++it) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((quad * 32u) << 16) + acc * 256u + c * 32u, v);
+                const uint32_t buf = buf0 + (uint32_t)(it & 1) * 4096u;
+                if (it >= 2) {  // the store two tiles back has finished reading this buffer
+                    if (lane == 0) bulk_wait_read_1();
+                    __syncwarp();
+                }
+                const uint32_t row = buf + (uint32_t)lane * 128u;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    st_shared_v4(row + (((uint32_t)j ^ ((uint32_t)lane & 7u)) << 4),
+                                 make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+                fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA engine
+                __syncwarp();
+                if (lane == 0) {
+                    // a tile wholly outside the tensor stores nothing, but still closes a (then
+                    // empty) group, so that "one group back" is always the other buffer's store
+                    if (n0 + c * 32 < p.N && token0 < p.M)
+                        tma_store_3d(&tmap_out, buf, (int)(n0 + c * 32), (int)token0, (int)blockIdx.z);
+                    bulk_commit();
+                }
+            }
+            if (lane == 0) bulk_wait_all();  // the stores are done before the CTA's memory goes
+            __syncwarp();
+        } else if (ok && (acc == 0 || upper)) {
             tc_fence_after();
             const uint32_t token = m0 + acc * 128 + quad * 32 + lane;
             float* orow = p.out + (size_t)blockIdx.z * p.M * p.N + (size_t)token * p.N;
@@ -581,9 +630,23 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     p.splits = pl.splits;
     float* part = reinterpret_cast<float*>(ws + ws_off);
     if (pl.splits > 1) p.out = part;
+    // the output (or the K-split partials) as a [splits][M][N] f32 tensor for the TMA-store epilogue
+    CUtensorMap omap;
+    std::memset(&omap, 0, sizeof(omap));
+    bool tma_out = n % 4 == 0 && reinterpret_cast<uintptr_t>(p.out) % 16 == 0;
+    if (tma_out) {
+        const cuuint64_t od[3] = {n, m, pl.splits};
+        const cuuint64_t os[2] = {(cuuint64_t)n * 4, (cuuint64_t)n * m * 4};
+        const cuuint32_t ob[3] = {32, 32, 1};
+        const cuuint32_t oe[3] = {1, 1, 1};
+        tma_out = encode_fn()(&omap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, p.out, od, os, ob, oe,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    p.tma_out = tma_out ? 1u : 0u;
     dim3 grid((n + pl.bn - 1) / pl.bn, (m + G_BM - 1) / G_BM, pl.splits);
-    if (pl.bn == 224) gemm_kernel<224><<<grid, G_THREADS, G_SMEM, stream>>>(map, p);
-    else gemm_kernel<256><<<grid, G_THREADS, G_SMEM, stream>>>(map, p);
+    if (pl.bn == 224) gemm_kernel<224><<<grid, G_THREADS, G_SMEM, stream>>>(map, omap, p);
+    else gemm_kernel<256><<<grid, G_THREADS, G_SMEM, stream>>>(map, omap, p);
     e = cudaGetLastError();
     if (e != cudaSuccess || pl.splits == 1) return e;
     const size_t mn = (size_t)m * n;
