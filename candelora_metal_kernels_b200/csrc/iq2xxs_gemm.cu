@@ -60,14 +60,22 @@ constexpr uint32_t idesc_for() {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
+// The launch's work units (blockIdx.x): tiles t = (m-tile t / nt, n-tile t % nt). The first `full`
+// tiles are computed whole, one unit each; each of the R tiles after them is split into `s`
+// ranges of whole 256-blocks of K (units full + (t - full) * s + z), whose partial sums go to
+// part[(t - full) * s + z][row][col] and are added up in z order by splitk_tile_sum_kernel. The
+// split fills the last wave of CTAs (or the only one, when there are fewer tiles than SMs).
 struct GemmParams {
     const uint8_t* qs;
     const uint8_t* sc;
-    float* out;     // [M, N]; with splits > 1 the [splits, M, N] partial sums instead
+    float* out;     // [M, N]
+    float* part;    // [R * s][PR][BN] partial sums of the split tiles (null when none is split)
     uint32_t* err;  // error word (0 = ok); set on a pipeline timeout
     uint32_t M, N, K, nb;
-    uint32_t splits;  // K split into this many ranges of whole 256-blocks (blockIdx.z)
-    uint32_t tma_out;  // the epilogue stores through the output tensor map (N % 4 == 0, aligned out)
+    uint32_t nt, full, s;
+    uint32_t PR;    // rows of a partial tile: 256, or M rounded up to 32 below that
+    uint32_t tma;   // the epilogue stores through the tensor maps (else per thread)
+    uint32_t vec;   // per-thread stores may be 16 bytes wide (N % 4 == 0 and out 16-byte aligned)
 };
 
 // ---- mbarrier / tcgen05 / TMA wrappers (inline PTX) ----
@@ -234,6 +242,7 @@ __device__ __forceinline__ void decode_sub(uint2 q, float d, uint32_t sel_l, uin
 template <int BN>
 __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                             const __grid_constant__ CUtensorMap tmap_out,
+                                                            const __grid_constant__ CUtensorMap tmap_part,
                                                             const GemmParams p) {
     static_assert(BN % 32 == 0 && BN <= G_BN, "BN");
     extern __shared__ uint8_t smem_raw[];
@@ -251,11 +260,26 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
     volatile uint32_t* abort_flag = tmem_addr_word + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * G_BM;
-    // this CTA's share of K: the 256-blocks [b0, b1) of split blockIdx.z, i.e. the 64-k stages
-    // [kt0, kt0 + NKT) (at least one: the host never makes more splits than blocks)
-    const uint32_t b0 = (uint32_t)((uint64_t)blockIdx.z * p.nb / p.splits);
-    const uint32_t b1 = (uint32_t)((uint64_t)(blockIdx.z + 1) * p.nb / p.splits);
+    // this CTA's unit: tile t, K range z of nz; pu = its partial tile (-1: the tile is whole)
+    uint32_t t, z, nz;
+    int pu;
+    if (blockIdx.x < p.full) {
+        t = blockIdx.x;
+        z = 0;
+        nz = 1;
+        pu = -1;
+    } else {
+        const uint32_t v = blockIdx.x - p.full;
+        t = p.full + v / p.s;
+        z = v % p.s;
+        nz = p.s;
+        pu = (int)v;
+    }
+    const uint32_t n0 = (t % p.nt) * BN, m0 = (t / p.nt) * G_BM;
+    // this CTA's share of K: the 256-blocks [b0, b1) of range z, i.e. the 64-k stages
+    // [kt0, kt0 + NKT) (at least one: the host never makes more ranges than blocks)
+    const uint32_t b0 = (uint32_t)((uint64_t)z * p.nb / nz);
+    const uint32_t b1 = (uint32_t)((uint64_t)(z + 1) * p.nb / nz);
     const uint32_t kt0 = b0 * (QK / G_BK);
     const uint32_t NKT = min(b1 * (QK / G_BK), (p.K + G_BK - 1) / G_BK) - kt0;
     const bool upper = m0 + 128 < p.M;  // the tile's second 128-token half holds tokens
@@ -400,13 +424,13 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
         ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;  // the TMEM loads below are warp-wide
         // accumulator, TMEM lane quadrant (fixed by the warp's rank in its group of 4), column half
         const uint32_t acc = (warp >> 2) & 1, quad = warp & 3, chalf = warp >> 3;
-        if (ok && (acc == 0 || upper) && p.tma_out) {
+        if (ok && (acc == 0 || upper) && p.tma) {
             // each warp's 32 x 32 tiles leave through TMA stores, staged in two 4 KB buffers of
             // the (now idle) stage ring: row `lane` of a tile in the 128-byte swizzle the tensor
             // map expects (16-byte chunk j at j ^ (lane % 8)), so the stores are whole lines and
             // overlap the next tile's TMEM load
             tc_fence_after();
-            const uint32_t token0 = m0 + acc * 128 + quad * 32;
+            const uint32_t lrow0 = acc * 128 + quad * 32, token0 = m0 + lrow0;
             const uint32_t buf0 = base_s + (uint32_t)warp * 8192u;
             int it = 0;
 #pragma unroll 1
@@ -426,10 +450,12 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
                 fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA engine
                 __syncwarp();
                 if (lane == 0) {
-                    // a tile wholly outside the tensor stores nothing, but still closes a (then
+                    // a tile wholly outside the output stores nothing, but still closes a (then
                     // empty) group, so that "one group back" is always the other buffer's store
-                    if (n0 + c * 32 < p.N && token0 < p.M)
-                        tma_store_3d(&tmap_out, buf, (int)(n0 + c * 32), (int)token0, (int)blockIdx.z);
+                    if (n0 + c * 32 < p.N && token0 < p.M) {
+                        if (pu < 0) tma_store_3d(&tmap_out, buf, (int)(n0 + c * 32), (int)token0, 0);
+                        else tma_store_3d(&tmap_part, buf, c * 32, (int)lrow0, pu);
+                    }
                     bulk_commit();
                 }
             }
@@ -437,25 +463,27 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
             __syncwarp();
         } else if (ok && (acc == 0 || upper)) {
             tc_fence_after();
-            const uint32_t token = m0 + acc * 128 + quad * 32 + lane;
-            float* orow = p.out + (size_t)blockIdx.z * p.M * p.N + (size_t)token * p.N;
-            const bool vec = (p.N % 4) == 0;
+            const uint32_t lrow = acc * 128 + quad * 32 + lane, token = m0 + lrow;
+            // the output row, or this unit's partial tile row (columns relative to n0)
+            float* orow = pu < 0 ? p.out + (size_t)token * p.N
+                                 : p.part + ((size_t)pu * p.PR + lrow) * BN;
+            const bool vec = pu >= 0 || p.vec;
 #pragma unroll 1
             for (int c = (int)chalf; c < BN / 32; c += 2) {
                 uint32_t v[32];
                 tmem_ld32(tmem + ((quad * 32u) << 16) + acc * 256u + c * 32u, v);
                 if (token < p.M) {
-                    const uint32_t nc = n0 + c * 32;
+                    const uint32_t nc = n0 + c * 32, oc = pu < 0 ? nc : c * 32u;
                     if (vec && nc + 32 <= p.N) {
 #pragma unroll
                         for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(orow + nc + j) =
+                            *reinterpret_cast<float4*>(orow + oc + j) =
                                 make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
                                             __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
                     } else {
 #pragma unroll
                         for (int j = 0; j < 32; ++j)
-                            if (nc + j < p.N) orow[nc + j] = __uint_as_float(v[j]);
+                            if (nc + j < p.N) orow[oc + j] = __uint_as_float(v[j]);
                     }
                 }
             }
@@ -478,32 +506,34 @@ __global__ void __launch_bounds__(256) to_bf16_kernel(const XT* __restrict__ x, 
         y[i] = __float2bfloat16_rn(to_f32(x[i]));
 }
 
-// out = the sum of the K splits' partial products, in split order (deterministic).
-template <bool V4>
-__global__ void __launch_bounds__(256) splitk_sum_kernel(const float* __restrict__ part, float* __restrict__ out,
-                                                         size_t mn, uint32_t splits) {
-    const size_t step = (size_t)gridDim.x * blockDim.x;
-    if (V4) {
-        const float4* p4 = reinterpret_cast<const float4*>(part);
-        float4* o4 = reinterpret_cast<float4*>(out);
-        const size_t n4 = mn / 4;
-        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += step) {
-            float4 a = p4[i];
-            for (uint32_t z = 1; z < splits; ++z) {
-                const float4 b = p4[z * n4 + i];
-                a.x += b.x;
-                a.y += b.y;
-                a.z += b.z;
-                a.w += b.w;
-            }
-            o4[i] = a;
+// The split tiles' outputs: out = the sum of each tile's K ranges, in range order (deterministic).
+// One thread per 4 columns of a partial tile row.
+__global__ void __launch_bounds__(256) splitk_tile_sum_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                                              uint32_t M, uint32_t N, uint32_t nt, uint32_t full,
+                                                              uint32_t R, uint32_t s, uint32_t BN, uint32_t PR) {
+    const uint32_t q = BN / 4;  // column quads per row
+    const size_t total = (size_t)R * PR * q;
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t i = (uint32_t)(e / ((size_t)PR * q));
+        const uint32_t rem = (uint32_t)(e % ((size_t)PR * q));
+        const uint32_t row = rem / q, c4 = (rem % q) * 4;
+        const uint32_t t = full + i;
+        const uint32_t token = (t / nt) * G_BM + row, n = (t % nt) * BN + c4;
+        if (token >= M || n >= N) continue;
+        const float4* src = reinterpret_cast<const float4*>(part + (((size_t)i * s) * PR + row) * BN + c4);
+        float4 a = src[0];
+        for (uint32_t z = 1; z < s; ++z) {
+            const float4 b = src[(size_t)z * PR * BN / 4];
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
         }
-    } else {
-        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += step) {
-            float a = part[i];
-            for (uint32_t z = 1; z < splits; ++z) a += part[z * mn + i];
-            out[i] = a;
-        }
+        float* o = out + (size_t)token * N + n;
+        o[0] = a.x;
+        if (n + 1 < N) o[1] = a.y;
+        if (n + 2 < N) o[2] = a.z;
+        if (n + 3 < N) o[3] = a.w;
     }
 }
 
@@ -527,32 +557,47 @@ EncodeTiledFn encode_fn() {
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 struct GemmPlan {
-    uint32_t bn;      // weight rows per CTA: 256 or 224
-    uint32_t splits;  // K splits (blockIdx.z)
+    uint32_t bn;          // weight rows per tile: 256 or 224
+    uint32_t nt, tiles;   // tiles along N, all tiles
+    uint32_t full, R, s;  // whole tiles; the split ones after them, and their K ranges
+    uint32_t PR;          // rows of a partial tile
 };
 
-// Tile width and K split. With at least one CTA per SM the tile width whose last wave is fullest
-// and no split; with fewer tiles than SMs (small m x n) K is split into ranges of whole 256-blocks,
-// at least two per range, so that one wave fills as many SMs as it can: the decode of the weight
-// tile, not the tensor core, bounds a CTA, and it runs only on the SMs that hold one.
+// Tile width and split. The CTAs (one per SM) run in waves of `sms`; the tiles of the full waves
+// are computed whole, and the tiles of the last, part-full wave (all of them when there are
+// fewer tiles than SMs) are split into ranges of whole 256-blocks of K, at least two blocks per
+// range, so that the last wave fills the SMs and ends after 1/s of a tile's time (plus a fixed
+// cost of about 1/20 of one: set-up, the partial tiles' stores, the sum). Of the two tile widths
+// the cheaper is taken; a tile's time is nearly independent of its width (the decode of a stage
+// takes its warps the same time whether 224 or 256 rows are live), measured on B200 as
+// 0.7 + 0.3 * BN / 256 of a 256-wide tile's.
 GemmPlan gemm_plan(uint32_t m, uint32_t n, uint32_t k, int num_sms) {
     const uint64_t sms = num_sms > 0 ? (uint64_t)num_sms : 148u;
     const uint64_t mt = (m + G_BM - 1) / G_BM, nb = (k + QK - 1) / QK;
-    auto tiles = [&](uint32_t bn) { return (uint64_t)((n + bn - 1) / bn) * mt; };
-    auto fill = [&](uint64_t ctas) {
-        const uint64_t waves = (ctas + sms - 1) / sms;
-        return (double)ctas / (double)(waves * sms);
-    };
-    if (tiles(G_BN) >= sms) return {fill(tiles(224)) > fill(tiles(G_BN)) + 0.02 ? 224u : (uint32_t)G_BN, 1u};
-    GemmPlan best{(uint32_t)G_BN, 1u};
-    double best_fill = -1.0;
+    GemmPlan best{};
+    double best_cost = 1e300;
     for (uint32_t bn : {(uint32_t)G_BN, 224u}) {
-        const uint64_t t = tiles(bn);
-        const uint64_t sp = std::max<uint64_t>(1, std::min<uint64_t>(sms / t, nb / 2));
-        const double f = fill(t * sp);
-        if (f > best_fill + 1e-9) {
-            best_fill = f;
-            best = {bn, (uint32_t)sp};
+        GemmPlan pl{};
+        pl.bn = bn;
+        pl.nt = (n + bn - 1) / bn;
+        pl.tiles = (uint32_t)(pl.nt * mt);
+        pl.PR = m >= (uint32_t)G_BM ? (uint32_t)G_BM : (m + 31) / 32 * 32;
+        const uint64_t T = pl.tiles;
+        uint64_t R = T <= sms ? T : T - ((T + sms - 1) / sms - 1) * sms;
+        if (R == sms) R = 0;
+        uint64_t sp = R ? std::max<uint64_t>(1, std::min<uint64_t>(sms / R, nb / 2)) : 1;
+        if (sp <= 1) {
+            R = 0;
+            sp = 1;
+        }
+        pl.R = (uint32_t)R;
+        pl.s = (uint32_t)sp;
+        pl.full = (uint32_t)(T - R);
+        const double waves = (double)((pl.full + sms - 1) / sms) + (R ? 1.0 / (double)sp + 0.05 : 0.0);
+        const double cost = waves * (0.7 + 0.3 * (double)bn / (double)G_BN);
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = pl;
         }
     }
     return best;
@@ -575,7 +620,7 @@ size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype, int 
     size_t ws = 256;  // error word
     if (x_dtype != kDtypeBf16) ws += align256((size_t)m * k * 2);  // bf16 copy of x
     const GemmPlan pl = gemm_plan(m, n, k, num_sms);
-    if (pl.splits > 1) ws += align256((size_t)pl.splits * m * n * sizeof(float));  // partial sums
+    if (pl.R) ws += align256((size_t)pl.R * pl.s * pl.PR * pl.bn * sizeof(float));  // partial tiles
     return ws;
 }
 
@@ -627,34 +672,38 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     p.K = k;
     p.nb = (k + QK - 1) / QK;
     const GemmPlan pl = gemm_plan(m, n, k, num_sms);
-    p.splits = pl.splits;
-    float* part = reinterpret_cast<float*>(ws + ws_off);
-    if (pl.splits > 1) p.out = part;
-    // the output (or the K-split partials) as a [splits][M][N] f32 tensor for the TMA-store epilogue
-    CUtensorMap omap;
+    p.nt = pl.nt;
+    p.full = pl.full;
+    p.s = pl.s;
+    p.PR = pl.PR;
+    p.part = pl.R ? reinterpret_cast<float*>(ws + ws_off) : nullptr;
+    p.vec = n % 4 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
+    // tensor maps of the TMA-store epilogue: the output [1][M][N] and the partial tiles
+    // [R*s][PR][BN] (f32, 32x32 boxes, 128-byte swizzle)
+    auto encode_out = [&](CUtensorMap* map, void* base, cuuint64_t d0, cuuint64_t d1, cuuint64_t d2) {
+        const cuuint64_t dims[3] = {d0, d1, d2};
+        const cuuint64_t str[2] = {d0 * 4, d0 * d1 * 4};
+        const cuuint32_t box[3] = {32, 32, 1};
+        const cuuint32_t es[3] = {1, 1, 1};
+        return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, str, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    CUtensorMap omap, pmap;
     std::memset(&omap, 0, sizeof(omap));
-    bool tma_out = n % 4 == 0 && reinterpret_cast<uintptr_t>(p.out) % 16 == 0;
-    if (tma_out) {
-        const cuuint64_t od[3] = {n, m, pl.splits};
-        const cuuint64_t os[2] = {(cuuint64_t)n * 4, (cuuint64_t)n * m * 4};
-        const cuuint32_t ob[3] = {32, 32, 1};
-        const cuuint32_t oe[3] = {1, 1, 1};
-        tma_out = encode_fn()(&omap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, p.out, od, os, ob, oe,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-    }
-    p.tma_out = tma_out ? 1u : 0u;
-    dim3 grid((n + pl.bn - 1) / pl.bn, (m + G_BM - 1) / G_BM, pl.splits);
-    if (pl.bn == 224) gemm_kernel<224><<<grid, G_THREADS, G_SMEM, stream>>>(map, omap, p);
-    else gemm_kernel<256><<<grid, G_THREADS, G_SMEM, stream>>>(map, omap, p);
+    std::memset(&pmap, 0, sizeof(pmap));
+    bool tma = p.vec && encode_out(&omap, out, n, m, 1);
+    if (tma && pl.R) tma = encode_out(&pmap, p.part, pl.bn, pl.PR, (cuuint64_t)pl.R * pl.s);
+    p.tma = tma ? 1u : 0u;
+    const unsigned units = pl.full + pl.R * pl.s;
+    if (pl.bn == 224) gemm_kernel<224><<<units, G_THREADS, G_SMEM, stream>>>(map, omap, pmap, p);
+    else gemm_kernel<256><<<units, G_THREADS, G_SMEM, stream>>>(map, omap, pmap, p);
     e = cudaGetLastError();
-    if (e != cudaSuccess || pl.splits == 1) return e;
-    const size_t mn = (size_t)m * n;
-    const bool v4 = mn % 4 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
+    if (e != cudaSuccess || pl.R == 0) return e;
+    const size_t quads = (size_t)pl.R * pl.PR * (pl.bn / 4);
     const int sms = num_sms > 0 ? num_sms : 148;
-    const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((mn / (v4 ? 4 : 1) + 255) / 256, (size_t)sms * 8));
-    if (v4) splitk_sum_kernel<true><<<blocks, 256, 0, stream>>>(part, out, mn, pl.splits);
-    else splitk_sum_kernel<false><<<blocks, 256, 0, stream>>>(part, out, mn, pl.splits);
+    const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((quads + 255) / 256, (size_t)sms * 8));
+    splitk_tile_sum_kernel<<<blocks, 256, 0, stream>>>(p.part, out, m, n, pl.nt, pl.full, pl.R, pl.s, pl.bn, pl.PR);
     return cudaGetLastError();
 }
 
