@@ -5,7 +5,7 @@
 // dense bf16 x bf16 -> f32 contraction:
 //   * A = x, bf16 [M, K] (f32/f16 x is first narrowed to bf16 into the workspace), loaded by TMA
 //     as 128-row x 64-k boxes with the 128-byte swizzle;
-//   * B = W, dequantised to bf16 in shared memory by 8 decode warps, directly in the canonical
+//   * B = W, dequantised to bf16 in shared memory by 16 decode warps, directly in the canonical
 //     SW128 K-major layout the MMA reads. Each weight is bf16(d*(2s+1)/8 * g) for g in {8,25,43}:
 //     the three products of a 32-weight sub-block are rounded once and a `prmt` picks the bf16
 //     pairs by grid code (IQ2XXS_BF16_SEL), an XOR applies the signs (the 7 stored sign bits and
@@ -15,13 +15,14 @@
 //     own copy, never share a bank) because the tensor core reads its operands through the same
 //     shared memory.
 //   * D: two 128 x BN f32 accumulators in TMEM (512 columns allocated): one CTA computes a tile of
-//     256 tokens x BN weight rows (BN = 256, or 224 when that leaves fewer SMs idle in the last
-//     wave, e.g. 512 tiles instead of 448 on 148 SMs for N = 14336), issuing per 64-k stage
-//     2 x 4 tcgen05.mma (M=128, N=BN, K=16) from one thread; tcgen05.commit frees each stage when
-//     the tensor core has read it.
+//     256 tokens x BN weight rows (BN = 256 or 224, from the cost model of gemm_plan), issuing per
+//     64-k stage 2 x 4 tcgen05.mma (M=128, N=BN, K=16) from one thread; tcgen05.commit frees each
+//     stage when the tensor core has read it. The tiles of the last, part-full wave of CTAs are
+//     split over K (partial tiles, summed in order by splitk_tile_sum_kernel).
 //   * Pipeline: 3 stages of 64 KB, mbarriers for "x landed" (TMA transaction bytes), "weights
 //     written" (decode warps) and "stage free" (MMA commit). Every wait is bounded: on timeout
 //     the kernel records an error code, stops issuing work and still frees its TMEM.
+//   * Epilogue: TMEM -> registers -> a 32 x 32 tile in the idle stage ring -> TMA store.
 // No TMA multicast is used anywhere (this library also runs on multi-GPU jobs).
 #include "iq2xxs_common.cuh"
 #include "iq2xxs_codebook.h"
@@ -136,8 +137,8 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-// TMA store of a 32 x 32 f32 tile (128-byte swizzled rows in shared memory) to the output tensor
-// [splits][M][N]; rows and columns outside the tensor are not written.
+// TMA store of a 32 x 32 f32 tile (128-byte swizzled rows in shared memory) to a 3-D f32 tensor
+// (the output [1][M][N] or the partial tiles [R*s][PR][BN]); what lies outside it is not written.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y, int z) {
     asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
                  "r"(src), "r"(x), "r"(y), "r"(z)
