@@ -292,18 +292,6 @@ __device__ __forceinline__ void cursor_seek(const GemvLaunch<CAP>& L, uint32_t p
     c.blk = local % L.prob[p].nb;
 }
 
-template <int CAP>
-__device__ __forceinline__ void cursor_next(const GemvLaunch<CAP>& L, TbCursor& c) {
-    ++c.tb;
-    if (++c.blk == L.prob[c.p].nb) {
-        c.blk = 0;
-        if (++c.rg == L.prob[c.p].tiles) {
-            c.rg = 0;
-            ++c.p;
-        }
-    }
-}
-
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -455,59 +443,89 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     const uint32_t p0 = L.cl_p[cl];
 
     // ---- issue side: cp.async stages of one tile-block each, NSTAGES ahead ----
+    // State of the issue cursor: this lane's 16-byte chunk t of row g (iq; rows g+8c at
+    // iq + c*i_rstep) and the scale of row `lane` (isp). With up to four n8 tiles it is set up
+    // once per tile (iss_tile) and advanced by one block per stage, so that a stage costs no
+    // 64-bit index arithmetic (+4..7 % at m <= 8); the eight-tile kernels have no registers to
+    // keep it across the loop and recompute it per stage.
+    constexpr bool LEAN = NT <= 4;
     TbCursor ic;
+    ic.tb = tb1;
     if (a < b) cursor_seek(L, p0, tb0, ic);
+    const uint32_t tbf_lo = (a + 7) >> 3, tbf_hi = b >> 3;  // tile-blocks whose 8 sub-blocks are all this warp's
+    const uint32_t lane_off = (uint32_t)g * 64u + ((((uint32_t)t) ^ (((uint32_t)g >> 1) & 3u)) << 4);
+    const uint8_t* iq = nullptr;
+    const uint8_t* isp = nullptr;
+    const uint8_t* i_scend = nullptr;
+    uint32_t i_rstep = 0, i_nb = 1, i_tiles = 1;
+    bool i_full = false;
+    auto iss_tile = [&]() {
+        const GemvProblem& P = L.prob[ic.p];
+        const uint32_t row0 = ic.rg * ROWS;
+        i_nb = P.nb;
+        i_tiles = P.tiles;
+        i_full = row0 + ROWS <= P.N;
+        i_rstep = P.nb * (uint32_t)QS_BYTES * 8u;
+        iq = P.qs + ((size_t)(row0 + g) * P.nb + ic.blk) * QS_BYTES + t * 16;
+        isp = P.sc + ((size_t)(row0 + lane) * P.nb + ic.blk) * SC_BYTES;
+        i_scend = P.sc + (size_t)P.N * P.nb * SC_BYTES;
+    };
+    if (LEAN && ic.tb < tb1) iss_tile();
     int islot = 0;
     auto issue = [&]() {
-        if (a < b && ic.tb < tb1) {
-            const GemvProblem& P = L.prob[ic.p];
+        if (ic.tb < tb1) {
+            if (!LEAN) iss_tile();
             const uint32_t st_s = ring_s + islot * STAGE_BYTES;
-            const uint32_t row0 = ic.rg * ROWS;
-            if (ic.tb * 8 >= a && ic.tb * 8 + 8 <= b && row0 + ROWS <= P.N) {
-                // the common case: every sub-block and every row of the stage is needed
+            if (ic.tb >= tbf_lo && ic.tb < tbf_hi && i_full) {
+                // the common case: every sub-block and every row of the stage is needed; chunk t
+                // of row r = 8c + g goes to chunk t ^ ((r >> 1) & 3) of the row's 64 bytes
+#pragma unroll
+                for (int c = 0; c < ROWS * 4 / 32; ++c)
+                    cp_async_16(st_s + c * 512 + lane_off, iq + (size_t)((uint32_t)c * i_rstep), 16u);
+                if (lane < ROWS) {
+                    // the 4-byte aligned word holding this row's d (the buffer is 4-byte aligned);
+                    // at the end of the buffer only the bytes that exist are read
+                    const uint8_t* ea = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(isp) & ~(uintptr_t)3);
+                    const size_t rem = (size_t)(i_scend - ea);
+                    cp_async_4(st_s + STAGE_QS + lane * 4, ea, rem < 4 ? (uint32_t)rem : 4u);
+                }
+            } else {
+                const GemvProblem& P = L.prob[ic.p];
+                const uint32_t row0 = ic.rg * ROWS;
+                const uint32_t s_lo = ic.tb * 8 < a ? a - ic.tb * 8 : 0u;        // first sub-block needed
+                const uint32_t s_hi = min(8u, b - ic.tb * 8);                     // one past the last
+                const uint32_t ch_lo = s_lo >> 1, ch_hi = (s_hi + 1) >> 1;        // 16-byte chunks needed
+                const uint8_t* qrow = P.qs + ((size_t)row0 * P.nb + ic.blk) * QS_BYTES;
                 const size_t row_bytes = (size_t)P.nb * QS_BYTES;
-                const uint8_t* qrow = P.qs + ((size_t)row0 * P.nb + ic.blk) * QS_BYTES +
-                                      (size_t)(lane >> 2) * row_bytes + (lane & 3) * 16;
 #pragma unroll
                 for (int c = 0; c < ROWS * 4 / 32; ++c) {
-                    const int r = c * 8 + (lane >> 2), ch = lane & 3;
-                    cp_async_16(st_s + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4), qrow + (size_t)c * 8 * row_bytes, 16u);
+                    const int idx = c * 32 + lane;
+                    const int r = idx >> 2, ch = idx & 3;
+                    const bool ok = row0 + r < P.N && (uint32_t)ch >= ch_lo && (uint32_t)ch < ch_hi;
+                    const uint8_t* src = ok ? qrow + (size_t)r * row_bytes + ch * 16 : P.qs;
+                    // swizzle: chunk ch of row r goes to chunk ch ^ ((r >> 1) & 3)
+                    cp_async_16(st_s + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4), src, ok ? 16u : 0u);
                 }
                 if (lane < ROWS) {
-                    const size_t e = ((size_t)(row0 + lane) * P.nb + ic.blk) * SC_BYTES;
+                    const uint32_t row = row0 + lane;
+                    const bool ok = row < P.N;
+                    const size_t e = ((size_t)row * P.nb + ic.blk) * SC_BYTES;
                     const size_t ea = e & ~(size_t)3, total = (size_t)P.N * P.nb * SC_BYTES;
-                    cp_async_4(st_s + STAGE_QS + lane * 4, P.sc + ea, (uint32_t)min((size_t)4, total - ea));
+                    const uint32_t nbytes = ok ? (uint32_t)min((size_t)4, total - ea) : 0u;
+                    cp_async_4(st_s + STAGE_QS + lane * 4, P.sc + (ok ? ea : 0), nbytes);
                 }
-                cursor_next(L, ic);
-                cp_async_commit();
-                islot = (islot + 1 == NSTAGES) ? 0 : islot + 1;
-                return;
             }
-            const uint32_t s_lo = ic.tb * 8 < a ? a - ic.tb * 8 : 0u;        // first sub-block needed
-            const uint32_t s_hi = min(8u, b - ic.tb * 8);                     // one past the last
-            const uint32_t ch_lo = s_lo >> 1, ch_hi = (s_hi + 1) >> 1;        // 16-byte chunks needed
-            const uint8_t* qrow = P.qs + ((size_t)row0 * P.nb + ic.blk) * QS_BYTES;
-            const size_t row_bytes = (size_t)P.nb * QS_BYTES;
-#pragma unroll
-            for (int c = 0; c < ROWS * 4 / 32; ++c) {
-                const int idx = c * 32 + lane;
-                const int r = idx >> 2, ch = idx & 3;
-                const bool ok = row0 + r < P.N && (uint32_t)ch >= ch_lo && (uint32_t)ch < ch_hi;
-                const uint8_t* src = ok ? qrow + (size_t)r * row_bytes + ch * 16 : P.qs;
-                // swizzle: chunk ch of row r goes to chunk ch ^ ((r >> 1) & 3)
-                cp_async_16(st_s + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4), src, ok ? 16u : 0u);
+            ++ic.tb;
+            iq += QS_BYTES;
+            isp += SC_BYTES;
+            if (++ic.blk == i_nb) {
+                ic.blk = 0;
+                if (++ic.rg == i_tiles) {
+                    ic.rg = 0;
+                    ++ic.p;
+                }
+                if (LEAN && ic.tb < tb1) iss_tile();
             }
-            if (lane < ROWS) {
-                // the 4-byte aligned word holding this row's d; near the end of the buffer only
-                // the bytes that exist are read (the rest of the word is zero-filled)
-                const uint32_t row = row0 + lane;
-                const bool ok = row < P.N;
-                const size_t e = ((size_t)row * P.nb + ic.blk) * SC_BYTES;
-                const size_t ea = e & ~(size_t)3, total = (size_t)P.N * P.nb * SC_BYTES;
-                const uint32_t nbytes = ok ? (uint32_t)min((size_t)4, total - ea) : 0u;
-                cp_async_4(st_s + STAGE_QS + lane * 4, P.sc + (ok ? ea : 0), nbytes);
-            }
-            cursor_next(L, ic);
         }
         cp_async_commit();
         islot = (islot + 1 == NSTAGES) ? 0 : islot + 1;
@@ -629,12 +647,26 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
 #pragma unroll
             for (int k = 0; k < 4; ++k) F[i][j][k] = 0.0f;
 
+    // Consumer cursor; per tile it keeps the problem's x fragments, column scales and block count.
     TbCursor cc;
+    cc.tb = tb1;
     if (a < b) cursor_seek(L, p0, tb0, cc);
-    else cc.tb = tb1;
+    const uint8_t* c_xb = nullptr;
+    const float* c_cs = nullptr;
+    uint32_t c_nb = 1, c_tiles = 1, c_dpar = 0;
+    auto cons_tile = [&]() {
+        const GemvProblem& P = L.prob[cc.p];
+        c_nb = P.nb;
+        c_tiles = P.tiles;
+        c_xb = FUSED ? nullptr : P.xb + lane * 8;
+        c_cs = FUSED ? nullptr : P.colscale + 2 * t;
+        // d sits in the high half of its aligned word when row*nb + blk is odd; this lane's rows
+        // all have the parity of g (tiles start at multiples of 16 rows)
+        c_dpar = (uint32_t)g & P.nb & 1u;
+    };
+    if (cc.tb < tb1) cons_tile();
     int slot = 0;
     for (; cc.tb < tb1;) {
-        const GemvProblem& P = L.prob[cc.p];
         cp_async_wait<NSTAGES - 1>();
         __syncwarp();
         const uint32_t st_s = ring_s + slot * STAGE_BYTES;
@@ -642,7 +674,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         const uint32_t s_hi = min(8u, b - cc.tb * 8);
 
         int I[T][NT][4];
-        const uint8_t* xbp = FUSED ? nullptr : P.xb + (size_t)cc.blk * 8 * NT * 256 + lane * 8;
+        const uint8_t* xbp = FUSED ? nullptr : c_xb + (size_t)(cc.blk * (8u * NT * 256u));
         const uint32_t xsp = xs_s + cc.blk * 8 * NT * 256 + lane * 8;
         if (s_lo == 0 && s_hi == 8)
             stage_compute<NT, T, false, FUSED>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
@@ -654,13 +686,11 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
             float2 cs[NT];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                const uint32_t ci = cc.blk * (NT * 8) + nt * 8 + 2 * t;
-                if (FUSED) cs[nt] = *reinterpret_cast<const float2*>(smem + cs_off + ci * 4);
-                else cs[nt] = __ldg(reinterpret_cast<const float2*>(P.colscale + ci));
+                const uint32_t ci = cc.blk * (NT * 8) + nt * 8;
+                if (FUSED) cs[nt] = *reinterpret_cast<const float2*>(smem + cs_off + (ci + 2 * t) * 4);
+                else cs[nt] = __ldg(reinterpret_cast<const float2*>(c_cs + ci));
             }
-            // d sits in the high half of its aligned word when row*nb + blk is odd; this lane's
-            // rows all have the parity of g (tiles start at multiples of 16 rows)
-            const uint32_t dsel = ((cc.blk ^ ((uint32_t)g & P.nb)) & 1u) ? 0x3232u : 0x1010u;
+            const uint32_t dsel = ((cc.blk & 1u) ^ c_dpar) ? 0x3232u : 0x1010u;
 #pragma unroll
             for (int tt = 0; tt < T; ++tt) {
                 const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
@@ -678,13 +708,22 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
             }
         }
 
-        const uint32_t rg = cc.rg;
-        const bool rg_done = (cc.blk + 1 == P.nb) || (cc.tb + 1 == tb1);
-        cursor_next(L, cc);
+        const uint32_t rg = cc.rg, pdone = cc.p;
+        const bool rg_done = (cc.blk + 1 == c_nb) || (cc.tb + 1 == tb1);
+        ++cc.tb;
+        if (++cc.blk == c_nb) {
+            cc.blk = 0;
+            if (++cc.rg == c_tiles) {
+                cc.rg = 0;
+                ++cc.p;
+            }
+            if (cc.tb < tb1) cons_tile();
+        }
         __syncwarp();
         issue();  // refill the slot just consumed
         slot = (slot + 1 == NSTAGES) ? 0 : slot + 1;
         if (!rg_done) continue;
+        const GemvProblem& P = L.prob[pdone];
 
         // ---- tile epilogue: reduce limb columns to tokens; write out, or a partial for the
         // ---- tile's first warp to finish after the cluster barrier
