@@ -199,6 +199,23 @@ def test_grouped_matches_oracle_and_single_calls(oracle):
         assert rel_l2(y.cpu().numpy(), single.cpu().numpy()) <= 1e-6
 
 
+@pytest.mark.parametrize("m", [1, 4, 8])
+def test_grouped_ragged_mix_every_cursor_width(oracle, m):
+    """One grouped launch over projections with ragged rows (N not a multiple of the row tile),
+    ragged K, a one-block K and a one-row N, for the n8-tile widths whose issue side keeps a
+    running cursor: tile and problem changes fall inside warps' ranges."""
+    shapes = [(97, 2816), (64, 256), (1, 4096), (130, 320), (33, 768), (512, 1000), (45, 256)]
+    probs, refs = [], []
+    for i, (n, k) in enumerate(shapes):
+        x = synth.activations(m, k, seed=40 + i, device="cuda")
+        qs, sc = synth.iq2xxs_weights(n, k, seed=900 + 10 * m + i)
+        probs.append((x, qs.cuda(), sc.cuda(), n, k))
+        refs.append(oracle.matmul(x.cpu().numpy(), qs.numpy(), sc.numpy(), n, k))
+    outs = c.iq2_matmul_grouped(probs)
+    for (n, k), y, ref in zip(shapes, outs, refs):
+        assert rel_l2(y.cpu().numpy(), ref) <= GEMV_TOL, (m, n, k)
+
+
 def test_grouped_many_problems_beyond_one_launch(oracle):
     """More projections than one launch holds (256): split into several launches."""
     m, n, k = 1, 64, 512
