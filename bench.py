@@ -390,6 +390,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             line["config3_ffn70b"] = models["ffn70b"]
         if not args.no_gemm:
             line["gemm"] = gemm_bench(args, device, stream, peaks, peak_src)
+        if not args.no_next_rows and world == 1:
+            line["next_rows"] = next_rows_bench(args, device, stream, peaks, peak_src)
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args)
     return line
@@ -589,6 +591,102 @@ def gemm_bench(args, device, stream, peaks, peak_src):
             "shapes": res, "l2": "each shape rotates over distinct (x, W) pairs totalling > 260 MB"}
 
 
+def next_rows_bench(args, device, stream, peaks, peak_src):
+    """The rows beside the benchmarked path, each on a Llama-3-8B gate/up shape (K=4096, N=14336),
+    one GPU, inputs resident, HBM-bound, against measured HBM:
+      w8a8      iq2_matmul_with_activation_quant (IQ2_XXS, W8A8) at M=1 and M=16; packed weight GB/s
+      variants  iq2_xs_matmul / iq2_s_matmul / iq3_s_matmul at M=1, f32 x; packed weight GB/s
+      dequant   iq2_dequantize to f16 (IQ2_XXS); GB/s of packed bytes read + f16 bytes written
+      gguf      split_interleaved of ggml IQ2_XXS blocks; GB/s of block bytes read + written
+    Matmuls rotate over distinct weights totalling > 260 MB (CUDA graph of back-to-back calls);
+    dequant and repack run on inputs and outputs larger than L2 (CUDA events around eager calls)."""
+    import candelora_metal_kernels_b200 as c
+    from candelora_metal_kernels_b200 import gguf, synth
+    V = c.Iq2MatmulVariant
+    hbm = peaks["hbm_gbs"]
+    n, k = 14336, 4096
+    nb = k // 256
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7)
+
+    def variant_weights(var):
+        bpb, spb = gguf.SPLIT[var]
+        wb = torch.randint(0, 256, (n * nb * bpb,), dtype=torch.uint8, device=device, generator=gen)
+        ws = torch.randint(0, 256, (n * nb, spb), dtype=torch.uint8, device=device, generator=gen)
+        d = (torch.rand(n * nb, device=device, generator=gen) * 9e-3 + 1e-3).to(torch.float16)
+        ws[:, :2] = d.view(torch.uint8).view(-1, 2)
+        return wb, ws.reshape(-1)
+
+    def matmul_gbs(fn, var, m, xdt=torch.float32):
+        bpb, spb = gguf.SPLIT[var]
+        wbytes = n * nb * (bpb + spb)
+        copies = max(2, int(260e6 // wbytes) + 1)
+        ws_list = [synth.iq2xxs_weights(n, k, seed=700 + i, device=device) if var == V.Iq2Xxs
+                   else variant_weights(var) for i in range(copies)]
+        x = synth.activations(m, k, seed=77, dtype=xdt, device=device)
+        out = torch.empty(m, n, device=device)
+        wsp = torch.empty(max(1, c.workspace_bytes(m, n, k, xdt, var)), dtype=torch.uint8, device=device)
+        with torch.cuda.stream(stream):
+            for (wb, sc) in ws_list:
+                fn(x, wb, sc, out, wsp)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for (wb, sc) in ws_list:
+                fn(x, wb, sc, out, wsp)
+        with torch.cuda.stream(stream):
+            g.replay()
+        reps = 10
+        ms = _time_graph(g, reps, stream) / (reps * copies)
+        del g
+        gbs = wbytes / (ms * 1e-3) / 1e9
+        return {"us": round(ms * 1e3, 2), "weight_gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4)}
+
+    aq = c.ActivationQuantConfig(c.ActivationQuantMode.W8A8)
+    w8a8 = {f"m{m}": matmul_gbs(lambda x, wb, sc, o, w: c.iq2_matmul_with_activation_quant(
+        x, wb, sc, n, k, V.Iq2Xxs, aq, out=o, workspace=w), V.Iq2Xxs, m) for m in (1, 16)}
+    variants = {}
+    for name, var in (("iq2_xs", V.Iq2Xs), ("iq2_s", V.Iq2S), ("iq3_s", V.Iq3S)):
+        variants[name] = matmul_gbs(lambda x, wb, sc, o, w, var=var: c.iq2_matmul(
+            x, wb, sc, n, k, var, out=o, workspace=w), var, 1)
+
+    def eager_ms(fn, reps=20):
+        with torch.cuda.stream(stream):
+            fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    # dequant: two 14336x4096 matrices in rotation (2 x 132 MB of traffic per pair of calls)
+    mats = [synth.iq2xxs_weights(n, k, seed=710 + i, device=device) for i in range(2)]
+    outs = [torch.empty(n, k, dtype=torch.float16, device=device) for _ in range(2)]
+    state = [0]
+
+    def deq():
+        i = state[0] = state[0] ^ 1
+        c.iq2_dequantize(mats[i][0], mats[i][1], n, k, dtype=torch.float16, out=outs[i])
+    ms = eager_ms(deq)
+    dbytes = synth.packed_bytes(n, k) + n * k * 2
+    dq = {"us": round(ms * 1e3, 2), "gbs": round(dbytes / (ms * 1e-3) / 1e9, 1),
+          "frac_hbm": round(dbytes / (ms * 1e-3) / 1e9 / hbm, 4), "bytes": dbytes}
+    del mats, outs
+
+    # ggml interleaved blocks -> split tensors: 8 x (14336 x 4096) of IQ2_XXS blocks (121 MB each way)
+    nblk = 8 * n * nb
+    blocks = torch.randint(0, 256, (nblk * 66,), dtype=torch.uint8, device=device, generator=gen)
+    ms = eager_ms(lambda: gguf.split_interleaved(blocks, nblk, V.Iq2Xxs), reps=10)
+    gbytes = 2 * nblk * 66
+    gg = {"us": round(ms * 1e3, 2), "gbs": round(gbytes / (ms * 1e-3) / 1e9, 1),
+          "frac_hbm": round(gbytes / (ms * 1e-3) / 1e9 / hbm, 4), "bytes": gbytes}
+    del blocks
+    return {"shape": "K=4096, N=14336 (Llama-3-8B gate/up)", "peak_hbm_gbs": hbm, "peak_source": peak_src,
+            "w8a8": w8a8, "variants": variants, "dequant_f16": dq, "gguf_split_interleaved": gg}
+
+
 # ---------------------------------------------------------------------------------------- CPU
 def cpu_baseline(args, seconds: float = 10.0, steps: int | None = None):
     """The reference's own kernels (compiled from source for the host) on a bounded sample of
@@ -699,6 +797,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
+    ap.add_argument("--no-next-rows", action="store_true",
+                    help="skip the W8A8 / IQ2_XS / IQ2_S / IQ3_S / dequant / ggml-repack measurements")
     ap.add_argument("--no-models", action="store_true", help="skip the configuration 3 and 4 measurements")
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
                     help="N > 1: how the sharded decode's output slices reach every rank")
