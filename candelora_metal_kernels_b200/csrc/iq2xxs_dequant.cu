@@ -7,8 +7,12 @@
 // whatever the evaluation order, and f16/bf16 outputs are its round-to-nearest-even: the f16
 // output is bit-identical to the reference's.
 //
-// One thread produces one 8-weight group (one 16-byte f16/bf16 store or two f32 stores); the
-// kernel is bound by the output write stream (2 bytes per weight vs 0.26 read).
+// One warp per weight row: lane (sub-block sb, group gi) of each 256-weight block turns its 8-byte
+// sub-block word into the group's eight signed int8 grid values with one selector lookup and two
+// `prmt`s (the decode of the GEMV), scales them by the exact block factor in f32 and writes one
+// 16-byte f16/bf16 store (or two f32 stores): a warp writes 512 contiguous bytes per block and
+// four blocks' words are loaded before any is decoded. No index division: the kernel is meant to
+// run at the output write stream's speed (2 bytes per weight written vs 0.26 read).
 #include "iq2xxs_common.cuh"
 #include "iq2xxs_codebook.h"
 #include "iq2xxs_internal.h"
@@ -22,68 +26,80 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
                                                       const uint8_t* __restrict__ sc,
                                                       void* __restrict__ out, uint32_t N,
                                                       uint32_t K, uint32_t nb, bool aligned) {
-    __shared__ uint64_t grid_s[256];
-    __shared__ uint8_t ksigns_s[128];
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) grid_s[i] = IQ2XXS_GRID[i];
-    for (int i = threadIdx.x; i < 128; i += blockDim.x) ksigns_s[i] = IQ2_KSIGNS[i];
+    constexpr int U = 4;  // blocks whose words are in flight together
+    __shared__ uint32_t sel_s[384];  // grid selectors (256), then sign selectors (128)
+    for (int i = threadIdx.x; i < 384; i += blockDim.x) sel_s[i] = IQ2XXS_SEL_COMPACT[i];
     __syncthreads();
-    const size_t groups_per_row = (size_t)nb * 32;
-    const size_t total = (size_t)N * groups_per_row;
-    for (size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x; gid < total;
-         gid += (size_t)gridDim.x * blockDim.x) {
-        const uint32_t n = (uint32_t)(gid / groups_per_row);
-        const uint32_t q = (uint32_t)(gid % groups_per_row);
-        const uint32_t sbk = q >> 2, gi = q & 3, blk = sbk >> 3;
-        const size_t k0 = (size_t)sbk * 32 + gi * 8;
-        if (k0 >= K) continue;
-        const uint8_t* pq = qs + (size_t)n * nb * QS_BYTES + (size_t)sbk * 8;
-        uint32_t aux_g, aux_s, dbits;
-        if (aligned) {
-            const uint2 w = *reinterpret_cast<const uint2*>(pq);
-            aux_g = w.x;
-            aux_s = w.y;
-            dbits = *reinterpret_cast<const uint16_t*>(sc + ((size_t)n * nb + blk) * SC_BYTES);
-        } else {
-            aux_g = ld_u32_le_unaligned(pq);
-            aux_s = ld_u32_le_unaligned(pq + 4);
-            dbits = ld_u16_le_unaligned(sc + ((size_t)n * nb + blk) * SC_BYTES);
-        }
-        const float d = half_bits_to_float(dbits);
-        const float dl = d * (0.5f + (float)(aux_s >> 28)) * 0.25f;
-        const uint64_t gw = grid_s[(aux_g >> (8 * gi)) & 0xFF];
-        const uint32_t signs = ksigns_s[(aux_s >> (7 * gi)) & 0x7F];
-        float v[8];
+    const uint32_t lane = threadIdx.x & 31, gi = lane & 3, sb = lane >> 2;
+    const uint32_t wpb = blockDim.x >> 5;
+    const uint32_t warps = gridDim.x * wpb;
+    for (uint32_t n = blockIdx.x * wpb + (threadIdx.x >> 5); n < N; n += warps) {
+        const uint8_t* qrow = qs + (size_t)n * nb * QS_BYTES + sb * 8;
+        const uint8_t* srow = sc + (size_t)n * nb * SC_BYTES;
+        for (uint32_t b0 = 0; b0 < nb; b0 += U) {
+            uint32_t ag[U], as[U], db[U];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            v[j] = dl * (float)((gw >> (8 * j)) & 0xFF) * (((signs >> j) & 1u) ? -1.0f : 1.0f);
-        }
-        const size_t base = (size_t)n * K + k0;
-        const bool full = k0 + 8 <= K;
-        if (OUT_DTYPE == 0) {
-            float* o = static_cast<float*>(out) + base;
-            if (full && aligned && (base % 4) == 0) {
-                reinterpret_cast<float4*>(o)[0] = make_float4(v[0], v[1], v[2], v[3]);
-                reinterpret_cast<float4*>(o)[1] = make_float4(v[4], v[5], v[6], v[7]);
-            } else {
-                for (int j = 0; j < 8 && k0 + j < K; ++j) o[j] = v[j];
+            for (int u = 0; u < U; ++u) {
+                const uint32_t blk = b0 + u;
+                ag[u] = as[u] = db[u] = 0u;
+                if (blk < nb) {
+                    const uint8_t* pq = qrow + (size_t)blk * QS_BYTES;
+                    if (aligned) {
+                        const uint2 w = *reinterpret_cast<const uint2*>(pq);
+                        ag[u] = w.x;
+                        as[u] = w.y;
+                        db[u] = *reinterpret_cast<const uint16_t*>(srow + (size_t)blk * SC_BYTES);
+                    } else {
+                        ag[u] = ld_u32_le_unaligned(pq);
+                        as[u] = ld_u32_le_unaligned(pq + 4);
+                        db[u] = ld_u16_le_unaligned(srow + (size_t)blk * SC_BYTES);
+                    }
+                }
             }
-        } else {
-            uint16_t h[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                h[j] = OUT_DTYPE == 1 ? __half_as_ushort(__float2half_rn(v[j]))
-                                      : __bfloat16_as_ushort(__float2bfloat16_rn(v[j]));
-            }
-            uint16_t* o = static_cast<uint16_t*>(out) + base;
-            if (full && aligned && (base % 8) == 0) {
-                uint4 pk;
-                pk.x = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
-                pk.y = (uint32_t)h[2] | ((uint32_t)h[3] << 16);
-                pk.z = (uint32_t)h[4] | ((uint32_t)h[5] << 16);
-                pk.w = (uint32_t)h[6] | ((uint32_t)h[7] << 16);
-                *reinterpret_cast<uint4*>(o) = pk;
-            } else {
-                for (int j = 0; j < 8 && k0 + j < K; ++j) o[j] = h[j];
+            for (int u = 0; u < U; ++u) {
+                const uint32_t blk = b0 + u;
+                const uint32_t k0 = blk * QK + sb * 32 + gi * 8;
+                if (blk >= nb || k0 >= K) continue;
+                // every factor is exact in f32, so dl * (signed grid byte) is the exact value
+                const float dl = half_bits_to_float(db[u]) * (0.5f + (float)(as[u] >> 28)) * 0.25f;
+                const uint32_t sel = sel_s[(ag[u] >> (8 * gi)) & 0xFFu] | sel_s[256 + ((as[u] >> (7 * gi)) & 0x7Fu)];
+                const uint32_t lo = prmt(KPOS, KNEG, sel), hi = prmt(KPOS, KNEG, sel >> 16);
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    v[j] = dl * (float)(int8_t)(lo >> (8 * j));
+                    v[4 + j] = dl * (float)(int8_t)(hi >> (8 * j));
+                }
+                const size_t base = (size_t)n * K + k0;
+                const bool full = k0 + 8 <= K;
+                if (OUT_DTYPE == 0) {
+                    float* o = static_cast<float*>(out) + base;
+                    if (full && aligned && (base % 4) == 0) {
+                        reinterpret_cast<float4*>(o)[0] = make_float4(v[0], v[1], v[2], v[3]);
+                        reinterpret_cast<float4*>(o)[1] = make_float4(v[4], v[5], v[6], v[7]);
+                    } else {
+                        for (int j = 0; j < 8 && k0 + j < K; ++j) o[j] = v[j];
+                    }
+                } else {
+                    uint32_t h2[4];  // round to nearest even, two values per conversion
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (OUT_DTYPE == 1) {
+                            const __half2 t = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+                            h2[j] = *reinterpret_cast<const uint32_t*>(&t);
+                        } else {
+                            const __nv_bfloat162 t = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+                            h2[j] = *reinterpret_cast<const uint32_t*>(&t);
+                        }
+                    }
+                    uint16_t* o = static_cast<uint16_t*>(out) + base;
+                    if (full && aligned && (base % 8) == 0) {
+                        *reinterpret_cast<uint4*>(o) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+                    } else {
+                        for (int j = 0; j < 8 && k0 + j < K; ++j) o[j] = (uint16_t)(h2[j >> 1] >> (16 * (j & 1)));
+                    }
+                }
             }
         }
     }
@@ -142,14 +158,62 @@ __global__ void __launch_bounds__(256) split_interleaved_kernel(const uint8_t* _
     }
 }
 
+// The same repack for whole chunks of SPLIT_CHUNK blocks, one chunk per CTA pass: the chunk's
+// interleaved bytes (a multiple of 16: every format's block size is even) come in as 16-byte loads
+// to shared memory, the packed weights leave as 8-byte stores (every format's weight bytes per
+// block are a multiple of 8, so no store straddles two blocks) and the scale bytes as 2-byte
+// stores (every field is 2-byte aligned). Needs 16-byte aligned blocks and 8-byte aligned wb.
+constexpr uint32_t SPLIT_CHUNK = 64;
+constexpr uint32_t SPLIT_MAX_BLOCK = 112;  // >= the largest block (IQ3_S: 110 bytes)
+
+__global__ void __launch_bounds__(256) split_chunks_kernel(const uint8_t* __restrict__ blocks, uint64_t nchunks,
+                                                           uint32_t ib, uint32_t bpb, uint32_t spb,
+                                                           uint8_t* __restrict__ wb, uint8_t* __restrict__ ws) {
+    __shared__ __align__(16) uint8_t buf[SPLIT_CHUNK * SPLIT_MAX_BLOCK];
+    const uint32_t in16 = SPLIT_CHUNK * ib / 16, out8 = SPLIT_CHUNK * bpb / 8, out2 = SPLIT_CHUNK * spb / 2;
+    for (uint64_t ch = blockIdx.x; ch < nchunks; ch += gridDim.x) {
+        const uint4* src = reinterpret_cast<const uint4*>(blocks + ch * SPLIT_CHUNK * ib);
+        for (uint32_t i = threadIdx.x; i < in16; i += blockDim.x) reinterpret_cast<uint4*>(buf)[i] = src[i];
+        __syncthreads();
+        uint2* dw = reinterpret_cast<uint2*>(wb + ch * SPLIT_CHUNK * bpb);
+        for (uint32_t c = threadIdx.x; c < out8; c += blockDim.x) {
+            const uint32_t o = c * 8, blk = o / bpb;
+            const uint16_t* p = reinterpret_cast<const uint16_t*>(buf + blk * ib + 2 + (o - blk * bpb));
+            dw[c] = make_uint2((uint32_t)p[0] | ((uint32_t)p[1] << 16), (uint32_t)p[2] | ((uint32_t)p[3] << 16));
+        }
+        uint16_t* dsc = reinterpret_cast<uint16_t*>(ws + ch * SPLIT_CHUNK * spb);
+        for (uint32_t j = threadIdx.x; j < out2; j += blockDim.x) {
+            const uint32_t o = j * 2, blk = o / spb, off = o - blk * spb;  // d at 0..1, the rest after the weights
+            dsc[j] = *reinterpret_cast<const uint16_t*>(buf + blk * ib + (off < 2 ? off : bpb + off));
+        }
+        __syncthreads();
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_split_interleaved(const uint8_t* blocks, uint64_t nblocks, uint32_t bytes_per_block,
                                      uint32_t scales_per_block, uint8_t* wb, uint8_t* ws, int num_sms,
                                      cudaStream_t stream) {
     const uint32_t ib = bytes_per_block + scales_per_block;
+    if (nblocks == 0 || ib == 0) return cudaSuccess;
+    const uint64_t nchunks = nblocks / SPLIT_CHUNK;
+    if (nchunks > 0 && ib % 2 == 0 && ib <= SPLIT_MAX_BLOCK && bytes_per_block % 8 == 0 &&
+        scales_per_block % 2 == 0 && (reinterpret_cast<uintptr_t>(blocks) % 16) == 0 &&
+        (reinterpret_cast<uintptr_t>(wb) % 8) == 0 && (reinterpret_cast<uintptr_t>(ws) % 2) == 0) {
+        uint64_t g = nchunks;
+        const uint64_t gcap = (uint64_t)(num_sms > 0 ? num_sms : 148) * 8;
+        if (g > gcap) g = gcap;
+        split_chunks_kernel<<<(unsigned)g, 256, 0, stream>>>(blocks, nchunks, ib, bytes_per_block, scales_per_block,
+                                                             wb, ws);
+        const uint64_t done = nchunks * SPLIT_CHUNK;
+        blocks += done * ib;
+        wb += done * bytes_per_block;
+        ws += done * scales_per_block;
+        nblocks -= done;
+        if (nblocks == 0) return cudaGetLastError();
+    }
     const uint64_t total = nblocks * ib;
-    if (total == 0) return cudaSuccess;
     uint64_t grid = (total + 255) / 256;
     const uint64_t cap = (uint64_t)(num_sms > 0 ? num_sms : 148) * 16;
     if (grid > cap) grid = cap;
@@ -176,10 +240,11 @@ cudaError_t launch_dequant(const uint8_t* qs, const uint8_t* sc, uint32_t n, uin
     const bool aligned = (reinterpret_cast<uintptr_t>(qs) % 8) == 0 &&
                          (reinterpret_cast<uintptr_t>(sc) % 2) == 0 &&
                          (reinterpret_cast<uintptr_t>(out) % 16) == 0;
-    const size_t total = (size_t)n * nb * 32;
-    size_t blocks = (total + 255) / 256;
-    const size_t cap = (size_t)num_sms * 16;
+    // one warp per row, eight per CTA; at most 16 CTAs per SM, the rows dealt round-robin
+    size_t blocks = ((size_t)n + 7) / 8;
+    const size_t cap = (size_t)(num_sms > 0 ? num_sms : 148) * 16;
     if (blocks > cap) blocks = cap;
+    if (blocks == 0) return cudaSuccess;
     switch (out_dtype) {
         case 0: dequant_kernel<0><<<(unsigned)blocks, 256, 0, stream>>>(qs, sc, out, n, k, nb, aligned); break;
         case 1: dequant_kernel<1><<<(unsigned)blocks, 256, 0, stream>>>(qs, sc, out, n, k, nb, aligned); break;

@@ -77,12 +77,17 @@ def test_interleave_is_the_ggml_block_layout():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("gtype", [16, 17, 22, 21])
-def test_split_interleaved_inverts_the_blocks(gtype):
+@pytest.mark.parametrize("nblocks,offset", [(37, 0), (64 * 3 + 37, 0), (128, 0), (64 * 2 + 5, 2)])
+def test_split_interleaved_inverts_the_blocks(gtype, nblocks, offset):
+    """Fewer blocks than one 64-block chunk, whole chunks plus a tail, whole chunks only, and a
+    source that is not 16-byte aligned (the byte-wise path)."""
     bpb, spb = SPLIT[gtype]
-    nblocks = 37
-    rng = np.random.default_rng(gtype)
+    rng = np.random.default_rng(gtype * 1000 + nblocks)
     wb, ws = rng.integers(0, 256, nblocks * bpb, dtype=np.uint8), rng.integers(0, 256, nblocks * spb, dtype=np.uint8)
-    blocks = torch.from_numpy(interleave(wb, ws, bpb, spb)).cuda()
+    inter = interleave(wb, ws, bpb, spb)
+    buf = torch.zeros(inter.size + offset, dtype=torch.uint8)
+    buf[offset:] = torch.from_numpy(inter)
+    blocks = buf.cuda()[offset:]
     got_b, got_s = gguf.split_interleaved(blocks, nblocks, gguf.GGML_TYPE[gtype])
     assert np.array_equal(got_b.cpu().numpy(), wb) and np.array_equal(got_s.cpu().numpy(), ws)
 
