@@ -12,9 +12,10 @@
 // Every weight dl * grid_byte * sign is exact in f32 (at most 22 significant bits), so the f16
 // and bf16 dequantisations are the round-to-nearest-even of the exact value, as the reference's.
 //
-// These formats are outside the benchmarked IQ2_XXS path: one warp per (weight row, 8 tokens)
-// decodes each 8-weight group to f32 once and applies it to the warp's tokens (f32 FMA); the
-// lanes split the row's groups and reduce at the end.
+// These formats are outside the benchmarked IQ2_XXS path: one warp per (weight row, up to 8
+// tokens) walks the row two blocks at a time, lane l decoding group l of each block (8 weights)
+// to f32 from decode tables staged in shared memory and applying it to the warp's tokens with
+// f32 FMAs on x read as 16-byte vectors; the lanes reduce at the end.
 #include "iq2xxs_common.cuh"
 #include "iq2xxs_codebook.h"
 #include "iq2_variant_grids.h"
@@ -35,15 +36,16 @@ struct Geom {
 // The 8 f32 weights of group gi (0..31, weights 8*gi .. 8*gi+7) of one block.
 template <int V>
 __device__ __forceinline__ void decode8(const uint8_t* __restrict__ q, const uint8_t* __restrict__ s, uint32_t gi,
-                                        float (&w)[8]) {
+                                        float (&w)[8], const uint64_t* __restrict__ g64,
+                                        const uint32_t* __restrict__ g32, const uint8_t* __restrict__ ks) {
     const float d = half_bits_to_float((uint32_t)s[0] | ((uint32_t)s[1] << 8));
     const uint32_t ib32 = gi >> 2, sub = gi & 3;
     if (V == V_XS) {
         const uint32_t word = (uint32_t)q[ib32 * 8 + 2 * sub] | ((uint32_t)q[ib32 * 8 + 2 * sub + 1] << 8);
         const uint32_t sb = s[2 + ib32];
         const float dl = d * (0.5f + (float)(sub < 2 ? (sb & 15u) : (sb >> 4))) * 0.25f;
-        const uint64_t grid = __ldg(IQ2XS_GRID + (word & 0x1FFu));
-        const uint32_t sg = IQ2_KSIGNS[(word >> 9) & 0x7Fu];
+        const uint64_t grid = g64[word & 0x1FFu];
+        const uint32_t sg = ks[(word >> 9) & 0x7Fu];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
             w[j] = dl * (float)((grid >> (8 * j)) & 0xFF) * (((sg >> j) & 1u) ? -1.0f : 1.0f);
@@ -53,7 +55,7 @@ __device__ __forceinline__ void decode8(const uint8_t* __restrict__ q, const uin
         const uint32_t idx = (uint32_t)q[off + h] | ((nib << (h ? 6 : 8)) & 0x300u);
         const uint32_t sg = q[32 + off + h];
         const float dl = d * (0.5f + (float)(((uint32_t)s[2 + ib32] >> (4 * il)) & 15u)) * 0.25f;
-        const uint64_t grid = __ldg(IQ2S_GRID + idx);
+        const uint64_t grid = g64[idx];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
             w[j] = dl * (float)((grid >> (8 * j)) & 0xFF) * (((sg >> j) & 1u) ? -1.0f : 1.0f);
@@ -64,7 +66,7 @@ __device__ __forceinline__ void decode8(const uint8_t* __restrict__ q, const uin
         const uint32_t i1 = (uint32_t)q[8 * ib32 + 2 * l] | (((qh >> (2 * l)) & 1u) << 8);
         const uint32_t i2 = (uint32_t)q[8 * ib32 + 2 * l + 1] | (((qh >> (2 * l + 1)) & 1u) << 8);
         const uint32_t sg = q[72 + 4 * ib32 + l];
-        const uint32_t g1 = __ldg(IQ3S_GRID + i1), g2 = __ldg(IQ3S_GRID + i2);
+        const uint32_t g1 = g32[i1], g2 = g32[i2];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             w[j] = dl * (float)((g1 >> (8 * j)) & 0xFF) * (((sg >> j) & 1u) ? -1.0f : 1.0f);
@@ -73,36 +75,85 @@ __device__ __forceinline__ void decode8(const uint8_t* __restrict__ q, const uin
     }
 }
 
-template <int V, typename XT>
+// x[k0 .. k0+7] of one token as f32; VEC: 16-byte aligned and the eight values inside K.
+template <typename XT>
+__device__ __forceinline__ void load_x8(const XT* __restrict__ xr, size_t k0, uint32_t K, bool vec, float (&v)[8]) {
+    if (vec && k0 + 8 <= K) {
+        if constexpr (sizeof(XT) == 4) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(xr + k0));
+            const float4 b = __ldg(reinterpret_cast<const float4*>(xr + k0) + 1);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+            const uint4 a = __ldg(reinterpret_cast<const uint4*>(xr + k0));
+            const uint32_t u[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                XT lo, hi;
+                const uint16_t l16 = (uint16_t)(u[j] & 0xFFFFu), h16 = (uint16_t)(u[j] >> 16);
+                memcpy(&lo, &l16, 2);
+                memcpy(&hi, &h16, 2);
+                v[2 * j] = to_f32(lo);
+                v[2 * j + 1] = to_f32(hi);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = k0 + j < K ? to_f32(xr[k0 + j]) : 0.0f;
+    }
+}
+
+// MT tokens per warp pass (1 for m = 1, else 8 with the last pass masked).
+template <int V, typename XT, int MT>
 __global__ void __launch_bounds__(256) variant_matmul_kernel(const XT* __restrict__ x, const uint8_t* __restrict__ qs,
                                                              const uint8_t* __restrict__ sc, float* __restrict__ out,
-                                                             uint32_t M, uint32_t N, uint32_t K, uint32_t nb) {
-    const int lane = threadIdx.x & 31;
-    const uint32_t mchunks = (M + 7) / 8;
+                                                             uint32_t M, uint32_t N, uint32_t K, uint32_t nb,
+                                                             bool xvec) {
+    __shared__ uint64_t g64_s[V == V_S ? 1024 : (V == V_XS ? 512 : 1)];
+    __shared__ uint32_t g32_s[V == V_3S ? 512 : 1];
+    __shared__ uint8_t ks_s[128];
+    if (V == V_XS)
+        for (int i = threadIdx.x; i < 512; i += blockDim.x) g64_s[i] = IQ2XS_GRID[i];
+    if (V == V_S)
+        for (int i = threadIdx.x; i < 1024; i += blockDim.x) g64_s[i] = IQ2S_GRID[i];
+    if (V == V_3S)
+        for (int i = threadIdx.x; i < 512; i += blockDim.x) g32_s[i] = IQ3S_GRID[i];
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) ks_s[i] = IQ2_KSIGNS[i];
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t mchunks = (M + MT - 1) / MT;
     const size_t total = (size_t)N * mchunks;
     for (size_t wi = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5; wi < total;
          wi += (size_t)gridDim.x * blockDim.x / 32) {
-        const uint32_t n = (uint32_t)(wi / mchunks), mc = (uint32_t)(wi % mchunks) * 8;
-        float acc[8];
+        const uint32_t n = (uint32_t)(wi / mchunks), mc = (uint32_t)(wi % mchunks) * MT;
+        const uint8_t* qrow = qs + (size_t)n * nb * Geom<V>::BYTES;
+        const uint8_t* srow = sc + (size_t)n * nb * Geom<V>::SCALES;
+        float acc[MT];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-        for (uint32_t g = lane; g < nb * 32; g += 32) {
-            const uint32_t blk = g >> 5;
-            const size_t bi = (size_t)n * nb + blk;
-            float w[8];
-            decode8<V>(qs + bi * Geom<V>::BYTES, sc + bi * Geom<V>::SCALES, g & 31, w);
-            const size_t k0 = (size_t)g * 8;
+        for (int i = 0; i < MT; ++i) acc[i] = 0.0f;
+        // lane l takes group l of every block, in block order (the FMA order of each lane's sum)
+        for (uint32_t b0 = 0; b0 < nb; b0 += 2) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const size_t k = k0 + j;
-                if (k >= K) break;
+            for (int u = 0; u < 2; ++u) {
+                const uint32_t blk = b0 + u;
+                if (blk >= nb) break;
+                const size_t k0 = (size_t)blk * QK + lane * 8;
+                if (k0 >= K) continue;
+                float w[8];
+                decode8<V>(qrow + (size_t)blk * Geom<V>::BYTES, srow + (size_t)blk * Geom<V>::SCALES, lane, w, g64_s,
+                           g32_s, ks_s);
 #pragma unroll
-                for (int mm = 0; mm < 8; ++mm)
-                    if (mc + mm < M) acc[mm] = fmaf(to_f32(x[(size_t)(mc + mm) * K + k]), w[j], acc[mm]);
+                for (int mm = 0; mm < MT; ++mm) {
+                    if (MT > 1 && mc + mm >= M) break;
+                    float xv[8];
+                    load_x8<XT>(x + (size_t)(mc + mm) * K, k0, K, xvec, xv);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (k0 + j < K) acc[mm] = fmaf(xv[j], w[j], acc[mm]);
+                }
             }
         }
 #pragma unroll
-        for (int mm = 0; mm < 8; ++mm) {
+        for (int mm = 0; mm < MT; ++mm) {
             float v = acc[mm];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
@@ -121,7 +172,8 @@ __global__ void __launch_bounds__(256) variant_dequant_kernel(const uint8_t* __r
         const size_t n = i / groups_per_row, g = i % groups_per_row;
         const size_t bi = n * nb + g / 32;
         float w[8];
-        decode8<V>(qs + bi * Geom<V>::BYTES, sc + bi * Geom<V>::SCALES, (uint32_t)(g & 31), w);
+        decode8<V>(qs + bi * Geom<V>::BYTES, sc + bi * Geom<V>::SCALES, (uint32_t)(g & 31), w, V == V_S ? IQ2S_GRID : IQ2XS_GRID,
+                   IQ3S_GRID, IQ2_KSIGNS);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const size_t k = g * 8 + j;
@@ -145,11 +197,23 @@ template <int V>
 cudaError_t launch_matmul_v(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc, uint32_t n,
                             uint32_t k, float* out, int num_sms, cudaStream_t s) {
     const uint32_t nb = (k + QK - 1) / QK;
-    const unsigned blocks = grid_for((size_t)n * ((m + 7) / 8), 8, num_sms);
-    switch (x_dtype) {
-        case 0: variant_matmul_kernel<V, float><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), qs, sc, out, m, n, k, nb); break;
-        case 1: variant_matmul_kernel<V, __half><<<blocks, 256, 0, s>>>(static_cast<const __half*>(x), qs, sc, out, m, n, k, nb); break;
-        default: variant_matmul_kernel<V, __nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), qs, sc, out, m, n, k, nb); break;
+    const uint32_t mt = m == 1 ? 1u : 8u;
+    const unsigned blocks = grid_for((size_t)n * ((m + mt - 1) / mt), 8, num_sms);
+    const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
+    const bool xvec = x_dtype == 0 ? (xa % 16 == 0 && k % 4 == 0) : (xa % 16 == 0 && k % 8 == 0);
+    const uint8_t* q = qs;
+    if (mt == 1) {
+        switch (x_dtype) {
+            case 0: variant_matmul_kernel<V, float, 1><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), q, sc, out, m, n, k, nb, xvec); break;
+            case 1: variant_matmul_kernel<V, __half, 1><<<blocks, 256, 0, s>>>(static_cast<const __half*>(x), q, sc, out, m, n, k, nb, xvec); break;
+            default: variant_matmul_kernel<V, __nv_bfloat16, 1><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), q, sc, out, m, n, k, nb, xvec); break;
+        }
+    } else {
+        switch (x_dtype) {
+            case 0: variant_matmul_kernel<V, float, 8><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), q, sc, out, m, n, k, nb, xvec); break;
+            case 1: variant_matmul_kernel<V, __half, 8><<<blocks, 256, 0, s>>>(static_cast<const __half*>(x), q, sc, out, m, n, k, nb, xvec); break;
+            default: variant_matmul_kernel<V, __nv_bfloat16, 8><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), q, sc, out, m, n, k, nb, xvec); break;
+        }
     }
     return cudaGetLastError();
 }
