@@ -58,6 +58,25 @@ def test_variant_matmul_matches_oracle(oracle, variant, m, n, k, xdt):
 
 
 @pytest.mark.parametrize("variant", list(VARIANTS))
+@pytest.mark.parametrize("m,offset,xdt", [(1, 0, torch.float32), (1, 1, torch.float32), (9, 3, torch.float32),
+                                          (1, 0, torch.float16)])
+def test_variant_matmul_chunks_and_unaligned(oracle, variant, m, offset, xdt):
+    """Rows of more blocks than the kernel stages at a time (17 blocks, ragged K), weight buffers
+    that start off any alignment (byte-wise loads), one token and a masked 8-token pass."""
+    var = VARIANTS[variant][0]
+    n, k = 40, 17 * 256 - 96
+    wb, ws = _blocks(variant, n, k, seed=11 + m + offset)
+
+    def dev(a):
+        b = torch.zeros(a.size + offset, dtype=torch.uint8)
+        b[offset:] = torch.from_numpy(a)
+        return b.cuda()[offset:]
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(m)).to(xdt)
+    y = c.iq2_matmul(x.cuda(), dev(wb), dev(ws), n, k, var).cpu().numpy()
+    assert rel_l2(y, oracle.matmul(x.float().numpy(), wb, ws, n, k, variant=variant)) <= 1e-4
+
+
+@pytest.mark.parametrize("variant", list(VARIANTS))
 @pytest.mark.parametrize("dtype,name", [(torch.float32, "f32"), (torch.float16, "f16"), (torch.bfloat16, "bf16")])
 def test_variant_dequant_bit_exact(oracle, variant, dtype, name):
     var = VARIANTS[variant][0]
