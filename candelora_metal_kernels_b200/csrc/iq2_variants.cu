@@ -47,8 +47,10 @@ __device__ __forceinline__ void decode8(const uint8_t* __restrict__ q, const uin
         const uint64_t grid = g64[word & 0x1FFu];
         const uint32_t sg = ks[(word >> 9) & 0x7Fu];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            w[j] = dl * (float)((grid >> (8 * j)) & 0xFF) * (((sg >> j) & 1u) ? -1.0f : 1.0f);
+        for (int j = 0; j < 8; ++j) {
+            const float p = dl * (float)((grid >> (8 * j)) & 0xFF);
+            w[j] = ((sg >> j) & 1u) ? -p : p;
+        }
     } else if (V == V_S) {
         const uint32_t il = sub >> 1, h = sub & 1, off = 4 * ib32 + 2 * il;
         const uint32_t nib = (uint32_t)q[64 + ib32] >> (4 * il);
@@ -57,8 +59,10 @@ __device__ __forceinline__ void decode8(const uint8_t* __restrict__ q, const uin
         const float dl = d * (0.5f + (float)(((uint32_t)s[2 + ib32] >> (4 * il)) & 15u)) * 0.25f;
         const uint64_t grid = g64[idx];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            w[j] = dl * (float)((grid >> (8 * j)) & 0xFF) * (((sg >> j) & 1u) ? -1.0f : 1.0f);
+        for (int j = 0; j < 8; ++j) {
+            const float p = dl * (float)((grid >> (8 * j)) & 0xFF);
+            w[j] = ((sg >> j) & 1u) ? -p : p;
+        }
     } else {
         const uint32_t l = sub, qh = q[64 + ib32];
         const uint32_t nib = ((uint32_t)s[2 + ib32 / 2] >> (4 * (ib32 & 1))) & 15u;
@@ -69,8 +73,9 @@ __device__ __forceinline__ void decode8(const uint8_t* __restrict__ q, const uin
         const uint32_t g1 = g32[i1], g2 = g32[i2];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            w[j] = dl * (float)((g1 >> (8 * j)) & 0xFF) * (((sg >> j) & 1u) ? -1.0f : 1.0f);
-            w[4 + j] = dl * (float)((g2 >> (8 * j)) & 0xFF) * (((sg >> (4 + j)) & 1u) ? -1.0f : 1.0f);
+            const float p = dl * (float)((g1 >> (8 * j)) & 0xFF), p4 = dl * (float)((g2 >> (8 * j)) & 0xFF);
+            w[j] = ((sg >> j) & 1u) ? -p : p;
+            w[4 + j] = ((sg >> (4 + j)) & 1u) ? -p4 : p4;
         }
     }
 }
@@ -141,14 +146,20 @@ __global__ void __launch_bounds__(256) variant_matmul_kernel(const XT* __restric
                 float w[8];
                 decode8<V>(qrow + (size_t)blk * Geom<V>::BYTES, srow + (size_t)blk * Geom<V>::SCALES, lane, w, g64_s,
                            g32_s, ks_s);
+                const bool full = k0 + 8 <= K;  // only the last group of a ragged K is not
 #pragma unroll
                 for (int mm = 0; mm < MT; ++mm) {
                     if (MT > 1 && mc + mm >= M) break;
                     float xv[8];
                     load_x8<XT>(x + (size_t)(mc + mm) * K, k0, K, xvec, xv);
+                    if (full) {
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (k0 + j < K) acc[mm] = fmaf(xv[j], w[j], acc[mm]);
+                        for (int j = 0; j < 8; ++j) acc[mm] = fmaf(xv[j], w[j], acc[mm]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            if (k0 + j < K) acc[mm] = fmaf(xv[j], w[j], acc[mm]);
+                    }
                 }
             }
         }
