@@ -747,7 +747,8 @@ def run_case(args):
     """Only the dominant kernel on its roofline shape, `--steps` times after two warm calls: the
     command the profiler captures. gemv: 4096x14336 (K x N) at M=1, f32 x, two weight copies
     (30 MB) in turn; gemm: M=2048 on the same projection, bf16 x; grouped: the benchmark step
-    (every projection of `--layers` layers in one iq2_matmul_grouped call, M=1)."""
+    (every projection of `--layers` layers in one iq2_matmul_grouped call, M=1); variant: the
+    IQ2_XS matmul on the gemv shape (random blocks, d ~U[1e-3, 1e-2]), M=1, f32 x."""
     import candelora_metal_kernels_b200 as c
     from candelora_metal_kernels_b200 import synth
     torch.cuda.set_device(0)
@@ -767,6 +768,29 @@ def run_case(args):
               flush=True)
         return
     n, k = 14336, 4096
+    if args.case == "variant":
+        nb = k // 256
+        g = torch.Generator(device="cuda")
+        g.manual_seed(1)
+        wb = torch.randint(0, 256, (n * nb * 64,), dtype=torch.uint8, device="cuda", generator=g)
+        sc = torch.randint(0, 256, (n * nb, 10), dtype=torch.uint8, device="cuda", generator=g)
+        sc[:, :2] = (torch.rand(n * nb, device="cuda", generator=g) * 9e-3 + 1e-3).to(torch.float16).view(
+            torch.uint8).view(-1, 2)
+        sc = sc.reshape(-1)
+        x = synth.activations(1, k, seed=1, device="cuda")
+        out = torch.empty(1, n, device="cuda")
+        for _ in range(2):
+            c.iq2_matmul(x, wb, sc, n, k, c.Iq2MatmulVariant.Iq2Xs, out=out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            c.iq2_matmul(x, wb, sc, n, k, c.Iq2MatmulVariant.Iq2Xs, out=out)
+        e1.record()
+        e1.synchronize()
+        print(json.dumps({"case": "variant", "m": 1, "k": k, "n": n, "calls": args.steps,
+                          "us_per_call": round(e0.elapsed_time(e1) * 1e3 / args.steps, 2)}), flush=True)
+        return
     m = 1 if args.case == "gemv" else 2048
     dtype = torch.float32 if args.case == "gemv" else torch.bfloat16
     ws_ = [tuple(t.cuda() for t in synth.iq2xxs_weights(n, k, seed=i)) for i in range(2)]
@@ -803,7 +827,7 @@ def main():
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
                     help="N > 1: how the sharded decode's output slices reach every rank")
     ap.add_argument("--gemm-reps", type=int, default=5)
-    ap.add_argument("--case", choices=["gemv", "gemm", "grouped"], default=None,
+    ap.add_argument("--case", choices=["gemv", "gemm", "grouped", "variant"], default=None,
                     help="run only the dominant kernel's shape (the profiler's small case) and exit")
     args = ap.parse_args()
     if args.case:
