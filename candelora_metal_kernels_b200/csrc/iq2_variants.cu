@@ -107,19 +107,67 @@ __device__ __forceinline__ void load_x8(const XT* __restrict__ xr, size_t k0, ui
     }
 }
 
+// IQ2_XS / IQ2_S grids hold the IQ2_XXS magnitudes {8, 25, 43}: group `lane` of a block becomes
+// eight signed int8 weights with one grid-selector lookup (nibble j: which magnitude byte j
+// holds), one sign-selector lookup (nibble j: 4 when weight j is negative) and two `prmt`s of the
+// magnitude words; w = dl * int8 is the exact value dl * grid * sign.
+template <int V>
+__device__ __forceinline__ void decode8_sel(const uint8_t* __restrict__ q, const uint8_t* __restrict__ s,
+                                            uint32_t lane, float (&w)[8], const uint32_t* gsel,
+                                            const uint32_t* ssel, const uint8_t* ks) {
+    const float d = half_bits_to_float((uint32_t)s[0] | ((uint32_t)s[1] << 8));
+    const uint32_t ib32 = lane >> 2, sub = lane & 3;
+    uint32_t sel;
+    float dl;
+    if (V == V_XS) {
+        const uint32_t word = (uint32_t)q[2 * lane] | ((uint32_t)q[2 * lane + 1] << 8);
+        const uint32_t sb = s[2 + ib32];
+        dl = d * (0.5f + (float)(sub < 2 ? (sb & 15u) : (sb >> 4))) * 0.25f;
+        sel = gsel[word & 0x1FFu] | ssel[ks[(word >> 9) & 0x7Fu]];
+    } else {
+        const uint32_t il = sub >> 1, h = sub & 1;
+        const uint32_t nib = (uint32_t)q[64 + ib32] >> (4 * il);
+        const uint32_t idx = (uint32_t)q[lane] | ((nib << (h ? 6 : 8)) & 0x300u);
+        dl = d * (0.5f + (float)(((uint32_t)s[2 + ib32] >> (4 * il)) & 15u)) * 0.25f;
+        sel = gsel[idx] | ssel[q[32 + lane]];
+    }
+    const uint32_t lo = prmt(KPOS, KNEG, sel), hi = prmt(KPOS, KNEG, sel >> 16);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        w[j] = dl * (float)(int8_t)(lo >> (8 * j));
+        w[4 + j] = dl * (float)(int8_t)(hi >> (8 * j));
+    }
+}
+
 // MT tokens per warp pass (1 for m = 1, else 8 with the last pass masked).
 template <int V, typename XT, int MT>
 __global__ void __launch_bounds__(256) variant_matmul_kernel(const XT* __restrict__ x, const uint8_t* __restrict__ qs,
                                                              const uint8_t* __restrict__ sc, float* __restrict__ out,
                                                              uint32_t M, uint32_t N, uint32_t K, uint32_t nb,
                                                              bool xvec) {
-    __shared__ uint64_t g64_s[V == V_S ? 1024 : (V == V_XS ? 512 : 1)];
+    __shared__ uint32_t gsel_s[V == V_S ? 1024 : (V == V_XS ? 512 : 1)];  // grid selectors (IQ2_XS / IQ2_S)
+    __shared__ uint32_t ssel_s[V == V_3S ? 1 : 256];                       // sign selectors by sign byte
     __shared__ uint32_t g32_s[V == V_3S ? 512 : 1];
     __shared__ uint8_t ks_s[128];
-    if (V == V_XS)
-        for (int i = threadIdx.x; i < 512; i += blockDim.x) g64_s[i] = IQ2XS_GRID[i];
-    if (V == V_S)
-        for (int i = threadIdx.x; i < 1024; i += blockDim.x) g64_s[i] = IQ2S_GRID[i];
+    if (V != V_3S) {
+        const uint32_t entries = V == V_S ? 1024u : 512u;
+        for (uint32_t i = threadIdx.x; i < entries; i += blockDim.x) {
+            const uint64_t gw = V == V_S ? IQ2S_GRID[i] : IQ2XS_GRID[i];
+            uint32_t sel = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t b = (uint32_t)(gw >> (8 * j)) & 0xFFu;
+                sel |= (b == 8u ? 0u : (b == 25u ? 1u : 2u)) << (4 * j);
+            }
+            gsel_s[i] = sel;
+        }
+        for (uint32_t i = threadIdx.x; i < 256; i += blockDim.x) {
+            uint32_t sel = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sel |= ((i >> j) & 1u) << (4 * j + 2);
+            ssel_s[i] = sel;
+        }
+    }
     if (V == V_3S)
         for (int i = threadIdx.x; i < 512; i += blockDim.x) g32_s[i] = IQ3S_GRID[i];
     for (int i = threadIdx.x; i < 128; i += blockDim.x) ks_s[i] = IQ2_KSIGNS[i];
@@ -144,8 +192,12 @@ __global__ void __launch_bounds__(256) variant_matmul_kernel(const XT* __restric
                 const size_t k0 = (size_t)blk * QK + lane * 8;
                 if (k0 >= K) continue;
                 float w[8];
-                decode8<V>(qrow + (size_t)blk * Geom<V>::BYTES, srow + (size_t)blk * Geom<V>::SCALES, lane, w, g64_s,
-                           g32_s, ks_s);
+                if constexpr (V == V_3S)
+                    decode8<V>(qrow + (size_t)blk * Geom<V>::BYTES, srow + (size_t)blk * Geom<V>::SCALES, lane, w,
+                               nullptr, g32_s, ks_s);
+                else
+                    decode8_sel<V>(qrow + (size_t)blk * Geom<V>::BYTES, srow + (size_t)blk * Geom<V>::SCALES, lane, w,
+                                   gsel_s, ssel_s, ks_s);
                 const bool full = k0 + 8 <= K;  // only the last group of a ragged K is not
 #pragma unroll
                 for (int mm = 0; mm < MT; ++mm) {
