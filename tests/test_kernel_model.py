@@ -165,3 +165,32 @@ def test_gemm_bf16_decode_tables_match_rounded_dequant(oracle):
                     col = sb * 32 + t * 8 + 2 * i
                     got[r, col], got[r, col + 1] = w & 0xFFFF, w >> 16
     assert np.array_equal(got, want)
+
+
+def test_variant_selector_rules_decode_the_xs_and_s_grids():
+    """The IQ2_XS / IQ2_S matmul (csrc/iq2_variants.cu, decode8_sel) builds its tables at run time:
+    grid selector nibble j = 0, 1, 2 for magnitude byte j = 8, 25, 43; sign selector nibble j = 4
+    when bit j of the sign byte is set. Decoded through `prmt` of the IQ2_XXS magnitude words, every
+    grid entry and sign pattern must give exactly grid * sign."""
+    import re
+    from pathlib import Path
+    text = (Path(__file__).resolve().parent.parent / "candelora_metal_kernels_b200" / "csrc" /
+            "iq2_variant_grids.h").read_text()
+
+    def table(name):
+        m = re.search(name + r"\[\d+\]\s*=\s*\{(.*?)\};", text, re.S)
+        return [int(t, 16) for t in re.findall(r"0x[0-9a-fA-F]+", m.group(1))]
+
+    code = {8: 0, 25: 1, 43: 2}
+    ssel = [sum((((i >> j) & 1) << (4 * j + 2)) for j in range(8)) for i in range(256)]
+    for name in ("IQ2XS_GRID", "IQ2S_GRID"):
+        grid = table(name)
+        gsel = [sum(code[(g >> (8 * j)) & 0xFF] << (4 * j) for j in range(8)) for g in grid]
+        cases = [(e, s) for e in range(len(grid)) for s in (0x00, 0xFF, 0xA5, 0x5A, 0x01, 0x80, 0x3C, 0xC3)]
+        cases += [(e, s) for e in range(0, len(grid), len(grid) // 32) for s in range(256)]
+        for e, s in cases:
+            sel = gsel[e] | ssel[s]
+            got = prmt(KPOS, KNEG, sel & 0xFFFF).to_bytes(4, "little") + prmt(KPOS, KNEG, sel >> 16).to_bytes(4, "little")
+            mags = [(grid[e] >> (8 * j)) & 0xFF for j in range(8)]
+            want = bytes(((-mags[j]) & 0xFF) if (s >> j) & 1 else mags[j] for j in range(8))
+            assert got == want, (name, e, s)
