@@ -26,6 +26,19 @@ ORACLE_SO = HERE / "_build" / "libiq2oracle.so"
 REF_SO = HERE / "_ref" / "libiq2ref.so"
 
 QK = 256
+# Where a checkout of the reference crate is looked for: $CANDELORA_REFERENCE_DIR, else a directory
+# named "reference" beside this repository. It is needed only to (re)build oracle/_ref and to
+# regenerate tables; nothing run on a GPU box reads it.
+REFERENCE_ENV = "CANDELORA_REFERENCE_DIR"
+
+
+def reference_dir() -> Path | None:
+    """The reference checkout (see REFERENCE_ENV), or None when there is none."""
+    cand = os.environ.get(REFERENCE_ENV) or str(HERE.parent.parent / "reference")
+    p = Path(cand)
+    return p if (p / "src/metal_src/iq2_matmul.metal").is_file() else None
+
+
 DTYPE_CODE = {"f32": 0, "f16": 1, "bf16": 2}
 VARIANT_CODE = {"iq2_xxs": 0, "iq2_xs": 1, "iq2_s": 2, "iq3_s": 3}
 # (weight bytes, scale bytes) per 256-weight block (src/iq2_matmul.rs:15-29)
@@ -44,10 +57,12 @@ def _ptr(a: np.ndarray, t):
 def build(ref: str | None = None) -> None:
     """Compile the checkers (make -C oracle). `_ref` is built only when the reference exists."""
     targets = ["oracle"]
-    ref = ref or "/root/reference"
-    if Path(ref, "src/metal_src/iq2_matmul.metal").is_file():
+    ref_path = Path(ref) if ref else reference_dir()
+    args = []
+    if ref_path is not None and (ref_path / "src/metal_src/iq2_matmul.metal").is_file():
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", str(HERE), f"REF={ref}", *targets], check=True)
+        args.append(f"REF={ref_path}")
+    subprocess.run(["make", "-s", "-C", str(HERE), *args, *targets], check=True)
 
 
 # ----------------------------------------------------------------------------- fixtures

@@ -8,10 +8,11 @@ import torch
 
 from conftest import GOLDEN, ROOT, parse_codebook, rel_l2
 from oracle.oracle import (deterministic_x, force_f16_one_per_block, lcg_fill,
-                           reference_parity_fixture)
+                           reference_dir, reference_parity_fixture)
 from candelora_metal_kernels_b200 import synth
 
-REF_TABLES = Path("/root/reference/src/metal_src/iq2_tables.metal")
+_REF = reference_dir()
+REF_TABLES = _REF / "src/metal_src/iq2_tables.metal" if _REF is not None else Path("-missing-")
 
 
 def _bits(x: np.ndarray) -> np.ndarray:
