@@ -129,12 +129,15 @@ def test_tables_match_reference_source():
     import tempfile
     root = Path(__file__).resolve().parents[1]
     with tempfile.TemporaryDirectory() as d:
-        subprocess.run([sys.executable, str(root / "oracle" / "gen_tables.py"), "--out", f"{d}/t.h"], check=True)
+        subprocess.run([sys.executable, str(root / "oracle" / "gen_tables.py"), "--ref", str(_REF),
+                        "--out", f"{d}/t.h"], check=True)
         assert Path(f"{d}/t.h").read_text() == (root / "oracle" / "iq2_tables_ref.h").read_text()
         subprocess.run([sys.executable, str(root / "candelora_metal_kernels_b200" / "csrc" / "gen_codebook.py"),
-                        "--out", f"{d}/c.h"], check=True)
+                        "--tables", str(REF_TABLES), "--out", f"{d}/c.h", "--out-variants", f"{d}/v.h"], check=True)
         assert Path(f"{d}/c.h").read_text() == (root / "candelora_metal_kernels_b200" / "csrc" /
                                                 "iq2xxs_codebook.h").read_text()
+        assert Path(f"{d}/v.h").read_text() == (root / "candelora_metal_kernels_b200" / "csrc" /
+                                                "iq2_variant_grids.h").read_text()
 
 
 def test_oracle_w8a8_matches_reference_golden(oracle, golden):
