@@ -9,6 +9,7 @@ from .activation_quant import ActivationQuantConfig, ActivationQuantMode
 from .iq2_matmul import (
     Iq2MatmulOp,
     Iq2MatmulVariant,
+    device_check,
     iq2_dequantize,
     iq2_dequantize_to_f16,
     grouped_workspace_bytes,
@@ -29,6 +30,7 @@ __all__ = [
     "Iq2MatmulOp",
     "Iq2MatmulVariant",
     "LIB_PATH",
+    "device_check",
     "iq2_dequantize",
     "iq2_dequantize_to_f16",
     "grouped_workspace_bytes",

@@ -22,16 +22,20 @@ IQ2_ERR_UNSUPPORTED = 7
 IQ2_ERR_WORKSPACE = 8
 IQ2_ERR_CUDA = 9
 IQ2_ERR_COMM = 10
+IQ2_ERR_TIMEOUT = 11
 IQ2_COMM_ID_BYTES = 128
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 ACT_QUANT_OFF, ACT_QUANT_W8A8, ACT_QUANT_W4A8 = 0, 1, 2
 
-# Every symbol the header declares, with its C signature.
+# Every symbol the headers (include/candelora_iq2.h, include/candelora_iq2_testing.h) declare,
+# with its C signature.
 _vp, _u32, _sz, _int = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_size_t, ctypes.c_int
 SIGNATURES = {
     "iq2_last_error": ([], ctypes.c_char_p),
     "iq2_abi_version": ([], _int),
+    "iq2_device_check": ([], _int),
+    "iq2_testing_set_gemm_stall": ([ctypes.c_uint64, _u32], _int),
     "iq2_matmul_workspace_size": ([_u32, _u32, _u32, _int, _int], _sz),
     "iq2_matmul": ([_vp, _int, _u32, _vp, _sz, _vp, _sz, _u32, _u32, _int, _vp, _vp, _sz, _vp], _int),
     "iq2_matmul_with_activation_quant": (
@@ -45,6 +49,7 @@ SIGNATURES = {
     "iq2_split_interleaved": ([_vp, _sz, ctypes.c_uint64, _int, _vp, _vp, _vp], _int),
     "iq2_comm_unique_id": ([_vp], _int),
     "iq2_comm_init": ([_vp, _int, _int, _vp], _int),
+    "iq2_comm_init_with_timeout": ([_vp, _int, _int, _u32, _vp], _int),
     "iq2_comm_destroy": ([_vp], _int),
     "iq2_comm_symmetric_alloc": ([_vp, _sz, _vp], _int),
     "iq2_comm_check": ([_vp], _int),

@@ -35,7 +35,8 @@ def _stale() -> bool:
     if not LIB.is_file():
         return True
     t = LIB.stat().st_mtime
-    deps = [CSRC / s for s in SOURCES + HEADERS] + [PKG.parent / "include" / "candelora_iq2.h", Path(__file__)]
+    deps = [CSRC / s for s in SOURCES + HEADERS] + [PKG.parent / "include" / h for h in
+                                                    ("candelora_iq2.h", "candelora_iq2_testing.h")] + [Path(__file__)]
     return any(d.stat().st_mtime > t for d in deps if d.is_file())
 
 

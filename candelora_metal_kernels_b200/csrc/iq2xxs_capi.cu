@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "../../include/candelora_iq2.h"
+#include "../../include/candelora_iq2_testing.h"
 #include "iq2xxs_internal.h"
 
 namespace {
@@ -231,6 +232,21 @@ int grouped_impl(const iq2_matmul_problem* probs, uint32_t count, uint32_t m, in
 // Helpers shared with iq2xxs_noalloc.cu (declared in iq2xxs_internal.h).
 namespace iq2 {
 
+void* current_context_handle() {
+    using CtxGetCurrentFn = int (*)(void**);  // CUresult cuCtxGetCurrent(CUcontext*)
+    static const CtxGetCurrentFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<CtxGetCurrentFn>(p);
+    }();
+    void* ctx = nullptr;
+    if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+    return ctx;
+}
+
 int capi_fail(int code, const char* fmt, ...) {
     char buf[512];
     va_list ap;
@@ -281,6 +297,27 @@ extern "C" {
 const char* iq2_last_error(void) { return g_last_error.c_str(); }
 
 int iq2_abi_version(void) { return IQ2_ABI_VERSION; }
+
+int iq2_device_check(void) {
+    g_last_error.clear();
+    unsigned int status = 0;
+    const cudaError_t e = (cudaError_t)iq2::gemm_take_status(&status);
+    if (e != cudaSuccess) return cuda_fail("iq2_device_check", e);
+    if (status != 0u)
+        return fail(IQ2_ERR_TIMEOUT,
+                    "iq2_device_check: a prefill GEMM gave up on a pipeline wait (status 0x%x:%s%s%s%s%s%s); the "
+                    "outputs of that call are incomplete",
+                    status, (status & 1u) ? " x producer" : "", (status & 2u) ? " x tile" : "",
+                    (status & 4u) ? " decoded weights" : "", (status & 8u) ? " stage release" : "",
+                    (status & 16u) ? " accumulator" : "", (status & 32u) ? " x tile after abort" : "");
+    return IQ2_OK;
+}
+
+int iq2_testing_set_gemm_stall(uint64_t wait_limit_ns, uint32_t stall_stage) {
+    g_last_error.clear();
+    iq2::gemm_testing_set_stall(wait_limit_ns, stall_stage);
+    return IQ2_OK;
+}
 
 size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, int x_dtype,
                                  int variant) {

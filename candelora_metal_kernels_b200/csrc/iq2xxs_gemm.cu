@@ -32,6 +32,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 
 namespace iq2 {
 
@@ -55,6 +56,15 @@ constexpr int G_SMEM = 1024 /*align*/ + G_STAGES * G_STAGE_BYTES + G_SEL_BYTES +
 constexpr uint32_t G_TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: only a broken pipeline waits that long
 
+// Per-device sticky status of the GEMM's bounded waits (the bits of the waits that ran out since
+// the last iq2_device_check; 0 = none). Every GPU that loads the library has its own copy.
+__device__ unsigned int g_gemm_status;
+
+// Test knobs (iq2_testing_set_gemm_stall): the wait bound, and a stage whose "weights written"
+// arrival the decode warps withhold, so that the MMA thread's wait on it runs out.
+uint64_t g_wait_limit_ns = WAIT_LIMIT_NS;
+uint32_t g_stall_stage = 0;  // 0: none; s > 0: stage s - 1 of every CTA
+
 // Instruction descriptor, kind::f16: F32 accumulate, BF16 A and B, both K-major, M=128, N=BN.
 template <int BN>
 constexpr uint32_t idesc_for() {
@@ -71,7 +81,9 @@ struct GemmParams {
     const uint8_t* sc;
     float* out;     // [M, N]
     float* part;    // [R * s][PR][BN] partial sums of the split tiles (null when none is split)
-    uint32_t* err;  // error word (0 = ok); set on a pipeline timeout
+    unsigned int* err;  // the device's sticky status word (g_gemm_status); set on a pipeline timeout
+    uint64_t wait_ns;   // bound of every mbarrier wait
+    uint32_t stall;     // test hook: see g_stall_stage
     uint32_t M, N, K, nb;
     uint32_t nt, full, s;
     uint32_t PR;    // rows of a partial tile: 256, or M rounded up to 32 below that
@@ -108,14 +120,15 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 // Bounded wait: false (and the error code recorded) if the phase does not complete within
-// WAIT_LIMIT_NS of wall time.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* err, uint32_t code) {
+// `limit` ns of wall time.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned int* err, uint32_t code,
+                                          uint64_t limit) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
         for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > WAIT_LIMIT_NS) {
+        if (global_ns() - t0 > limit) {
             atomicOr(err, code);
             return false;
         }
@@ -316,19 +329,31 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
     if (warp == G_TMA_WARP) {
         // ---------------- x producer ----------------
         if (lane == 0) {
+            uint32_t issued = 0;
+            bool aborted = false;
             for (uint32_t i = 0; i < NKT; ++i) {
                 const int s = i % G_STAGES;
-                if (i >= G_STAGES && !mbar_wait(empty(s), ((i / G_STAGES) - 1) & 1, p.err, 1u)) {
+                if (i >= G_STAGES && !mbar_wait(empty(s), ((i / G_STAGES) - 1) & 1, p.err, 1u, p.wait_ns)) {
                     *abort_flag = 1u;
+                    aborted = true;
                     break;
                 }
-                if (*abort_flag) break;
+                if (*abort_flag) {
+                    aborted = true;
+                    break;
+                }
                 const uint32_t a_s = base_s + s * G_STAGE_BYTES;
                 const int kx = (int)((kt0 + i) * G_BK);
                 mbar_expect_tx(full_a(s), upper ? G_A_BYTES : G_A_HALF);
                 tma_load_2d(a_s, &tmap_x, full_a(s), kx, (int)m0);
                 if (upper) tma_load_2d(a_s + G_A_HALF, &tmap_x, full_a(s), kx, (int)(m0 + 128));
+                ++issued;
             }
+            // after an abort, the loads already issued (at most one per stage slot, each the last
+            // use of its slot) land before the CTA's shared memory goes away (bounded as well)
+            if (aborted)
+                for (uint32_t j = issued > G_STAGES ? issued - G_STAGES : 0u; j < issued; ++j)
+                    mbar_wait(full_a(j % G_STAGES), (j / G_STAGES) & 1u, p.err, 32u, p.wait_ns);
         }
     } else if (warp == G_MMA_WARP) {
         // ---------------- MMA issuer ----------------
@@ -337,7 +362,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
             for (uint32_t i = 0; i < NKT && ok; ++i) {
                 const int s = i % G_STAGES;
                 const uint32_t ph = (i / G_STAGES) & 1;
-                ok = mbar_wait(full_a(s), ph, p.err, 2u) && mbar_wait(full_b(s), ph, p.err, 4u);
+                ok = mbar_wait(full_a(s), ph, p.err, 2u, p.wait_ns) && mbar_wait(full_b(s), ph, p.err, 4u, p.wait_ns);
                 if (!ok || *abort_flag) {
                     *abort_flag = 1u;
                     break;
@@ -397,7 +422,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
                 // a wait that runs out (only a broken pipeline) stops this warp; the MMA thread
                 // then runs out of its own waits and stops too
                 bool go = true;
-                if (lane == 0) go = mbar_wait(empty(s), ph ^ 1u, p.err, 8u);
+                if (lane == 0) go = mbar_wait(empty(s), ph ^ 1u, p.err, 8u, p.wait_ns);
                 go = __shfl_sync(0xFFFFFFFFu, go ? 1 : 0, 0) != 0;  // one decision for the whole warp
                 if (!go) {
                     *abort_flag = 1u;
@@ -412,7 +437,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
             }
             fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
             __syncwarp();
-            if (lane == 0) mbar_arrive(full_b(s));
+            if (lane == 0 && i + 1 != p.stall) mbar_arrive(full_b(s));
             if (++s == G_STAGES) {
                 s = 0;
                 ph ^= 1u;
@@ -421,7 +446,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
 
         // ---------------- epilogue: TMEM -> registers -> global ----------------
         bool ok = true;
-        if (lane == 0) ok = mbar_wait(acc_full, 0, p.err, 16u) && !*abort_flag;
+        if (lane == 0) ok = mbar_wait(acc_full, 0, p.err, 16u, p.wait_ns) && !*abort_flag;
         ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;  // the TMEM loads below are warp-wide
         // accumulator, TMEM lane quadrant (fixed by the warp's rank in its group of 4), column half
         const uint32_t acc = (warp >> 2) & 1, quad = warp & 3, chalf = warp >> 3;
@@ -604,7 +629,49 @@ GemmPlan gemm_plan(uint32_t m, uint32_t n, uint32_t k, int num_sms) {
     return best;
 }
 
+// Device address of g_gemm_status on the current device, looked up with cudaGetSymbolAddress once
+// per device and context (a new primary context, e.g. after cudaDeviceReset, is looked up again).
+std::mutex g_status_mu;
+struct StatusSlot {
+    void* ctx = nullptr;
+    unsigned int* ptr = nullptr;
+};
+StatusSlot g_status_slot[64];
+
+cudaError_t status_word_for_current_device(unsigned int** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    void* const ctx = current_context_handle();
+    std::lock_guard<std::mutex> lock(g_status_mu);
+    StatusSlot& slot = g_status_slot[dev];
+    if (slot.ptr == nullptr || slot.ctx != ctx) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_gemm_status);
+        if (e != cudaSuccess) return e;
+        slot.ptr = static_cast<unsigned int*>(p);
+        slot.ctx = ctx;
+    }
+    *out = slot.ptr;
+    return cudaSuccess;
+}
+
 }  // namespace
+
+int gemm_take_status(unsigned int* status) {
+    unsigned int* word = nullptr;
+    cudaError_t e = status_word_for_current_device(&word);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(status, word, sizeof(unsigned int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && *status != 0u) e = cudaMemset(word, 0, sizeof(unsigned int));
+    return (int)e;
+}
+
+void gemm_testing_set_stall(uint64_t wait_limit_ns, uint32_t stall_stage) {
+    g_wait_limit_ns = wait_limit_ns ? wait_limit_ns : WAIT_LIMIT_NS;
+    g_stall_stage = stall_stage;
+}
 
 bool gemm_path_ok(uint32_t m, uint32_t n, uint32_t k, const void* x, int x_dtype, const uint8_t* qs,
                   const uint8_t* sc, const float* out) {
@@ -618,7 +685,7 @@ bool gemm_path_ok(uint32_t m, uint32_t n, uint32_t k, const void* x, int x_dtype
 }
 
 size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype, int num_sms) {
-    size_t ws = 256;  // error word
+    size_t ws = 256;  // (reserved)
     if (x_dtype != kDtypeBf16) ws += align256((size_t)m * k * 2);  // bf16 copy of x
     const GemmPlan pl = gemm_plan(m, n, k, num_sms);
     if (pl.R) ws += align256((size_t)pl.R * pl.s * pl.PR * pl.bn * sizeof(float));  // partial tiles
@@ -628,8 +695,8 @@ size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype, int 
 cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc, uint32_t n,
                         uint32_t k, float* out, void* workspace, int num_sms, cudaStream_t stream) {
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    uint32_t* err = reinterpret_cast<uint32_t*>(ws);
-    cudaError_t e = cudaMemsetAsync(err, 0, 4, stream);
+    unsigned int* err = nullptr;
+    cudaError_t e = status_word_for_current_device(&err);
     if (e != cudaSuccess) return e;
     const void* xb = x;
     size_t ws_off = 256;
@@ -668,6 +735,8 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     p.sc = sc;
     p.out = out;
     p.err = err;
+    p.wait_ns = g_wait_limit_ns;
+    p.stall = g_stall_stage;
     p.M = m;
     p.N = n;
     p.K = k;

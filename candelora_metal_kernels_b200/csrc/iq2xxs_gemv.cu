@@ -568,16 +568,23 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     // done, so no earlier kernel still reads the outputs); block 0 tells every rank at once. The
     // wait for the others is off the compute path: the first warp that is about to store takes
     // it on (go_owner), waits until every rank has entered, and opens `go` for the rest.
+    // Once an exchange of this communicator has failed (the sticky error word is set, by a timed-out
+    // wait or a rank-local failure of an earlier call) the ranks' call numbers can no longer be
+    // trusted to match, so the call runs local-only: no entry, no waits, no peer stores; its
+    // outputs hold this rank's columns only and iq2_comm_check keeps reporting the error until
+    // the communicator is destroyed.
     unsigned long long epoch = 0;
+    bool dead = false;
     if constexpr (P2P) {
         const GemvPeers& pe = L.peers;
         epoch = *reinterpret_cast<volatile unsigned long long*>(&pe.hdr->epoch) + 1ull;
-        if (blockIdx.x == 0 && threadIdx.x == 0)
+        dead = *reinterpret_cast<volatile unsigned*>(&pe.hdr->err) != 0u;
+        if (!dead && blockIdx.x == 0 && threadIdx.x == 0)
             for (int r = 0; r < pe.world; ++r) st_relaxed_sys_u64(peer_header(pe, r)->entry + pe.rank, epoch);
     }
     // Before its first store a warp sees `go` (one lane waits, bounded); if it never opens the
     // outputs stay local and the error bit is set.
-    bool go_seen = !P2P, peers_ok = P2P;
+    bool go_seen = !P2P || dead, peers_ok = P2P && !dead;
     auto wait_go = [&]() {
         if constexpr (P2P) {
             if (go_seen) return;
@@ -831,7 +838,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
             const unsigned prev = atomicAdd(&pe.hdr->done, 1u);
             if (prev == gridDim.x - 1) {
                 __threadfence();
-                if (ld_acquire_gpu_u64(&pe.hdr->go) >= epoch) {
+                if (!dead && ld_acquire_gpu_u64(&pe.hdr->go) >= epoch) {
                     fence_acq_rel_sys();
                     for (int r = 0; r < pe.world; ++r) st_relaxed_sys_u64(peer_header(pe, r)->data + pe.rank, epoch);
                     bool ok = true;

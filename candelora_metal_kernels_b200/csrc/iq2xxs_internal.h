@@ -42,7 +42,8 @@ struct SymmHeader {
     unsigned long long go_owner;
     unsigned long long epoch;
     unsigned int done;
-    unsigned int err;  // bit 0: entry barrier timed out; bit 1: data barrier timed out
+    unsigned int err;  // bit 0: entry barrier timed out; bit 1: data barrier timed out;
+                       // bit 2: a call failed on this rank before its launch (sticky until destroy)
 };
 constexpr size_t kSymmHeaderBytes = 4096;
 constexpr int kMaxRanks = 8;
@@ -77,6 +78,18 @@ size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype, int 
 cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
                         uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,
                         cudaStream_t stream);
+
+// The prefill GEMM's per-device sticky status (iq2xxs_gemm.cu): synchronises the current device,
+// stores the status bits in *status and clears them; returns a cudaError_t.
+int gemm_take_status(unsigned int* status);
+// Test hook of the GEMM's bounded waits (process-wide): wait bound (0: the default 2 s) and a stage
+// whose "weights written" arrival is withheld (0: none).
+void gemm_testing_set_stall(uint64_t wait_limit_ns, uint32_t stall_stage);
+
+// The current CUDA context of the calling thread (a CUcontext, as an opaque handle; nullptr when
+// none): caches of device addresses are keyed on it so that a new primary context (after
+// cudaDeviceReset) is looked up again.
+void* current_context_handle();
 
 // C ABI helpers (iq2xxs_capi.cu) used by iq2xxs_noalloc.cu and iq2xxs_sharded.cu.
 int capi_fail(int code, const char* fmt, ...);

@@ -8,14 +8,14 @@
 //
 // The scratch is a file-scope __device__ array of IQ2_NOALLOC_SCRATCH_BYTES (8 MiB): every GPU
 // that loads this library holds that much for the life of the process. In host code the array's
-// name is only a host-side stand-in, so its device address is obtained once per device with
-// cudaGetSymbolAddress (with that device current) during the first call on the device and
-// cached; make that first call outside any stream capture. All calls share the one array and it
+// name is only a host-side stand-in, so its device address is obtained with cudaGetSymbolAddress
+// (with that device current) during the first call on the device -- and again after the device's
+// context was replaced (cudaDeviceReset) -- and cached; make that first call outside any stream
+// capture. All calls share the one array and it
 // keeps the previous call's contents. Nothing in it needs to start at zero: the x-limb prep
 // kernel writes every limb and scale before the GEMV reads them, and the GEMV keeps its partial
 // sums in shared memory. Calls whose kernels overlap on the GPU (different streams, or different
 // host threads without ordering) race on the array.
-#include <atomic>
 #include <cstdio>
 #include <mutex>
 
@@ -28,25 +28,31 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[IQ2_NOALLOC_SCRATCH_B
 
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mu;
-std::atomic<void*> g_scratch_ptr[kMaxDevices];
+struct ScratchSlot {
+    void* ctx = nullptr;  // the context the address belongs to
+    void* ptr = nullptr;
+};
+ScratchSlot g_scratch[kMaxDevices];
 
-// Device address of g_noalloc_scratch on the current device (looked up once per device).
+// Device address of g_noalloc_scratch on the current device. It is looked up once per device
+// and context: after cudaDeviceReset the device's next primary context holds a new copy of the
+// array, and the first call in that context looks its address up again.
 cudaError_t scratch_for_current_device(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    void* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
-    if (p == nullptr) {
-        std::lock_guard<std::mutex> lock(g_setup_mu);
-        p = g_scratch_ptr[dev].load(std::memory_order_relaxed);
-        if (p == nullptr) {
-            e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-            if (e != cudaSuccess) return e;
-            g_scratch_ptr[dev].store(p, std::memory_order_release);
-        }
+    void* const ctx = iq2::current_context_handle();
+    std::lock_guard<std::mutex> lock(g_setup_mu);
+    ScratchSlot& slot = g_scratch[dev];
+    if (slot.ptr == nullptr || slot.ctx != ctx) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        slot.ptr = p;
+        slot.ctx = ctx;
     }
-    *out = p;
+    *out = slot.ptr;
     return cudaSuccess;
 }
 

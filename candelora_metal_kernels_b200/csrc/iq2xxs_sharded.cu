@@ -17,7 +17,10 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstring>
+#include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/candelora_iq2.h"
@@ -27,6 +30,8 @@
 struct iq2_comm_s {
     ncclComm_t nccl;
     int world, rank, device;
+    uint32_t timeout_ms = 0;     // bound of every wait on the other ranks (NCCL calls, barriers)
+    bool aborted = false;        // a wait ran out or NCCL failed: the NCCL communicator was aborted
     uint8_t* symm = nullptr;     // this rank's symmetric region (header + user area)
     size_t symm_bytes = 0;       // user area bytes
     void* peer[iq2::kMaxRanks] = {};  // the other ranks' regions mapped here (IPC); peer[rank] = symm
@@ -36,6 +41,57 @@ namespace iq2 {
 namespace {
 
 constexpr uint32_t SCATTER_CAP = 256;
+constexpr uint32_t kDefaultCommTimeoutMs = 120000;  // iq2_comm_init: two minutes
+
+double elapsed_ms(std::chrono::steady_clock::time_point t0) {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
+
+// The communicators are non-blocking (ncclConfig_t.blocking = 0): an NCCL call may return
+// ncclInProgress, and the communicator's state is then polled with ncclCommGetAsyncError until it
+// leaves that state or `timeout_ms` of wall time pass. Returns the final state; ncclInProgress
+// means the wait ran out (the caller aborts the communicator).
+ncclResult_t nccl_settle(ncclComm_t c, ncclResult_t r, uint32_t timeout_ms) {
+    if (r != ncclInProgress) return r;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t st = ncclInProgress;
+        const ncclResult_t q = ncclCommGetAsyncError(c, &st);
+        if (q != ncclSuccess) return q;
+        if (st != ncclInProgress) return st;
+        if (elapsed_ms(t0) > timeout_ms) return ncclInProgress;
+        std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
+}
+
+// Waits for the work queued on `s` (which may hold NCCL kernels waiting for other ranks) while
+// polling the communicator for asynchronous errors, for at most the communicator's timeout.
+ncclResult_t stream_settle(iq2_comm_t comm, cudaStream_t s) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) return ncclSuccess;
+        if (e != cudaErrorNotReady) return ncclUnhandledCudaError;
+        ncclResult_t st = ncclSuccess;
+        if (ncclCommGetAsyncError(comm->nccl, &st) != ncclSuccess) return ncclInternalError;
+        if (st != ncclSuccess && st != ncclInProgress) return st;
+        if (elapsed_ms(t0) > comm->timeout_ms) return ncclInProgress;
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+// A wait on the other ranks ran out or NCCL reported an error: abort the communicator (this
+// ends its pending work and frees its resources) so that the process stays usable.
+int comm_failed(iq2_comm_t comm, const char* op, const char* what, ncclResult_t r) {
+    if (!comm->aborted) {
+        ncclCommAbort(comm->nccl);
+        comm->aborted = true;
+    }
+    if (r == ncclInProgress)
+        return capi_fail(IQ2_ERR_COMM, "%s: %s: no answer from the other ranks within %u ms; communicator aborted", op,
+                         what, comm->timeout_ms);
+    return capi_fail(IQ2_ERR_COMM, "%s: %s: %s; communicator aborted", op, what, ncclGetErrorString(r));
+}
 
 struct ScatterItem {
     float* out;
@@ -64,6 +120,9 @@ __global__ void __launch_bounds__(256) scatter_slices_kernel(const __grid_consta
 }
 
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+// Sets bits of the sticky error word of this rank's symmetric-region header (stream-ordered).
+__global__ void mark_comm_error_kernel(unsigned* err, unsigned bits) { atomicOr(err, bits); }
 
 struct ShardPlan {
     std::vector<uint64_t> off;  // packed offsets (elements)
@@ -113,6 +172,18 @@ bool use_peer_path(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t co
     return true;
 }
 
+// A call that fails on this rank after every rank has chosen the fused exchange never launches
+// here, so this rank's call count falls behind the others'. The failure is therefore recorded in
+// the sticky error word (bit 2): every later fused call of the communicator on this rank runs
+// local-only, the other ranks' bounded waits for this call run out and set their own error words,
+// and iq2_comm_check reports the failure on every rank.
+int peer_local_failure(iq2_comm_t comm, iq2_stream_t stream, int rc) {
+    auto* hdr = reinterpret_cast<SymmHeader*>(comm->symm);
+    mark_comm_error_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(&hdr->err, 4u);
+    (void)cudaGetLastError();  // the call's own error is the one reported
+    return rc;
+}
+
 int sharded_peer(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t count, uint32_t m, int x_dtype,
                  void* workspace, size_t workspace_bytes, iq2_stream_t stream) {
     const char* op = "iq2_matmul_grouped_sharded";
@@ -123,21 +194,24 @@ int sharded_peer(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t coun
         float* out = p.out + (size_t)comm->rank * n_loc;  // this rank's columns of the full [m, out_dim]
         int rc = capi_validate_matmul(op, p.x, x_dtype, m, p.weight_bytes, p.weight_bytes_len, p.weight_scales,
                                       p.weight_scales_len, n_loc, p.in_dim, out, IQ2_VARIANT_IQ2_XXS);
-        if (rc != IQ2_OK) return rc;
+        if (rc != IQ2_OK) return peer_local_failure(comm, stream, rc);
         // no fallback here: the other ranks are already committed to the fused exchange (their
         // bounded waits end in an error that iq2_comm_check reports)
         if (!gemv_fast_path_ok(m, p.in_dim, p.weight_bytes, p.weight_scales))
-            return capi_fail(IQ2_ERR_UNSUPPORTED,
-                             "%s: problem %u: with outputs in the symmetric region the weight slices must be 16-byte "
-                             "(bytes) and 4-byte (scales) aligned",
-                             op, i);
+            return peer_local_failure(
+                comm, stream,
+                capi_fail(IQ2_ERR_UNSUPPORTED,
+                          "%s: problem %u: with outputs in the symmetric region the weight slices must be 16-byte "
+                          "(bytes) and 4-byte (scales) aligned",
+                          op, i));
         loc[i] = GemvProblemHost{p.x, p.weight_bytes, p.weight_scales, n_loc, p.in_dim, out, p.out_dim};
     }
     const int sms = capi_num_sms();
     const size_t need = gemv_group_workspace_size(loc.data(), count, m, sms);
     if (need > 0 && (workspace == nullptr || workspace_bytes < need))
-        return capi_fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
-                         workspace ? workspace_bytes : (size_t)0);
+        return peer_local_failure(comm, stream,
+                                  capi_fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
+                                            workspace ? workspace_bytes : (size_t)0));
     GemvPeers pe;
     pe.hdr = reinterpret_cast<SymmHeader*>(comm->symm);
     pe.world = comm->world;
@@ -146,7 +220,7 @@ int sharded_peer(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t coun
         pe.delta[r] = r < comm->world ? (long long)(static_cast<uint8_t*>(comm->peer[r]) - comm->symm) : 0;
     const cudaError_t e = launch_gemv_group(loc.data(), count, m, x_dtype, workspace, sms,
                                             reinterpret_cast<cudaStream_t>(stream), &pe);
-    if (e != cudaSuccess) return capi_cuda_fail(op, e);
+    if (e != cudaSuccess) return peer_local_failure(comm, stream, capi_cuda_fail(op, e));
     return capi_ok();
 }
 
@@ -166,33 +240,53 @@ int iq2_comm_unique_id(uint8_t* id) {
     return iq2::capi_ok();
 }
 
-int iq2_comm_init(const uint8_t* id, int world, int rank, iq2_comm_t* comm) {
-    if (id == nullptr || comm == nullptr)
-        return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "iq2_comm_init: NULL id or comm");
+int iq2_comm_init_with_timeout(const uint8_t* id, int world, int rank, uint32_t timeout_ms, iq2_comm_t* comm) {
+    const char* op = "iq2_comm_init";
+    if (id == nullptr || comm == nullptr) return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL id or comm", op);
+    *comm = nullptr;
     if (world < 1 || rank < 0 || rank >= world)
-        return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "iq2_comm_init: rank %d of world %d", rank, world);
+        return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "%s: rank %d of world %d", op, rank, world);
+    if (timeout_ms == 0) return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "%s: zero timeout", op);
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return capi_fail(IQ2_ERR_DEVICE, "iq2_comm_init requires a CUDA device");
+    if (e != cudaSuccess) return capi_fail(IQ2_ERR_DEVICE, "%s requires a CUDA device", op);
     ncclUniqueId uid;
     std::memcpy(uid.internal, id, IQ2_COMM_ID_BYTES);
-    ncclComm_t c;
-    const ncclResult_t r = ncclCommInitRank(&c, world, uid, rank);
-    if (r != ncclSuccess) return capi_fail(IQ2_ERR_COMM, "iq2_comm_init: %s", ncclGetErrorString(r));
-    *comm = new iq2_comm_s{c, world, rank, dev};
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;  // every NCCL call returns at once; the waits are polled and bounded here
+    ncclComm_t c = nullptr;
+    ncclResult_t r = ncclCommInitRankConfig(&c, world, uid, rank, &cfg);
+    if (c != nullptr) r = iq2::nccl_settle(c, r, timeout_ms);
+    if (r != ncclSuccess) {
+        if (c != nullptr) ncclCommAbort(c);
+        if (r == ncclInProgress)
+            return capi_fail(IQ2_ERR_COMM, "%s: rank %d of %d: not every rank joined within %u ms; aborted", op, rank,
+                             world, timeout_ms);
+        return capi_fail(IQ2_ERR_COMM, "%s: %s", op, ncclGetErrorString(r));
+    }
+    auto* h = new iq2_comm_s{c, world, rank, dev};
+    h->timeout_ms = timeout_ms;
+    *comm = h;
     return iq2::capi_ok();
+}
+
+int iq2_comm_init(const uint8_t* id, int world, int rank, iq2_comm_t* comm) {
+    return iq2_comm_init_with_timeout(id, world, rank, iq2::kDefaultCommTimeoutMs, comm);
 }
 
 namespace {
 
 // Every rank reaches this point before any goes on (a one-element all-reduce), so that no rank
 // unmaps or frees a region a peer may still store into.
+// Bounded: ncclInProgress when the other ranks did not all arrive within the communicator's timeout.
 ncclResult_t comm_barrier(iq2_comm_t comm, cudaStream_t s) {
+    if (comm->aborted) return ncclInvalidUsage;
     float* one = nullptr;
     if (cudaMalloc(&one, sizeof(float)) != cudaSuccess) return ncclUnhandledCudaError;
-    ncclResult_t r = ncclAllReduce(one, one, 1, ncclFloat, ncclSum, comm->nccl, s);
-    if (r == ncclSuccess && cudaStreamSynchronize(s) != cudaSuccess) r = ncclUnhandledCudaError;
-    cudaFree(one);
+    ncclResult_t r = iq2::nccl_settle(comm->nccl, ncclAllReduce(one, one, 1, ncclFloat, ncclSum, comm->nccl, s),
+                                      comm->timeout_ms);
+    if (r == ncclSuccess) r = iq2::stream_settle(comm, s);
+    if (r == ncclSuccess) cudaFree(one);  // (while NCCL may still use it, the 4 bytes are left)
     return r;
 }
 
@@ -209,19 +303,25 @@ void release_symmetric(iq2_comm_t comm) {
 
 int iq2_comm_destroy(iq2_comm_t comm) {
     if (comm == nullptr) return iq2::capi_ok();
+    const char* op = "iq2_comm_destroy";
     ncclResult_t r = ncclSuccess;
-    if (comm->symm != nullptr) {
+    if (comm->symm != nullptr && !comm->aborted) {
+        // no rank unmaps its region while a peer may still store into it
         cudaStream_t s = nullptr;
         cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
         r = comm_barrier(comm, s);
-        cudaStreamDestroy(s);
-        release_symmetric(comm);
+        if (r == ncclSuccess) cudaStreamDestroy(s);
     }
-    const ncclResult_t r2 = ncclCommDestroy(comm->nccl);
+    int rc = IQ2_OK;
+    if (!comm->aborted) {
+        if (r == ncclSuccess) r = iq2::nccl_settle(comm->nccl, ncclCommFinalize(comm->nccl), comm->timeout_ms);
+        if (r == ncclSuccess) ncclCommDestroy(comm->nccl);
+        else rc = iq2::comm_failed(comm, op, "the final barrier", r);
+    }
+    // after an abort a peer may still hold this rank's region mapped: it is then left allocated
+    if (comm->symm != nullptr && r == ncclSuccess) release_symmetric(comm);
     delete comm;
-    if (r == ncclSuccess) r = r2;
-    if (r != ncclSuccess) return capi_fail(IQ2_ERR_COMM, "iq2_comm_destroy: %s", ncclGetErrorString(r));
-    return iq2::capi_ok();
+    return rc == IQ2_OK ? iq2::capi_ok() : rc;
 }
 
 int iq2_comm_symmetric_alloc(iq2_comm_t comm, size_t bytes, void** ptr) {
@@ -229,6 +329,7 @@ int iq2_comm_symmetric_alloc(iq2_comm_t comm, size_t bytes, void** ptr) {
     if (comm == nullptr || ptr == nullptr) return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "%s: NULL comm or ptr", op);
     *ptr = nullptr;
     if (bytes == 0) return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "%s: zero bytes", op);
+    if (comm->aborted) return capi_fail(IQ2_ERR_COMM, "%s: the communicator was aborted", op);
     if (comm->symm != nullptr) return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "%s: the communicator already has one", op);
     if (comm->world > iq2::kMaxRanks)
         return capi_fail(IQ2_ERR_UNSUPPORTED, "%s: at most %d ranks, got %d", op, iq2::kMaxRanks, comm->world);
@@ -262,8 +363,17 @@ int iq2_comm_symmetric_alloc(iq2_comm_t comm, size_t bytes, void** ptr) {
     if (le == cudaSuccess) le = cudaIpcGetMemHandle(&h[comm->rank].handle, base);
     h[comm->rank].total = le == cudaSuccess ? total : 0ull;
     e = cudaMemcpy(entries + sizeof(Entry) * comm->rank, &h[comm->rank], sizeof(Entry), cudaMemcpyHostToDevice);
-    nr = ncclAllGather(entries + sizeof(Entry) * comm->rank, entries, sizeof(Entry), ncclUint8, comm->nccl, s);
-    if (nr == ncclSuccess && e == cudaSuccess) e = cudaStreamSynchronize(s);
+    nr = iq2::nccl_settle(comm->nccl,
+                          ncclAllGather(entries + sizeof(Entry) * comm->rank, entries, sizeof(Entry), ncclUint8,
+                                        comm->nccl, s),
+                          comm->timeout_ms);
+    if (nr == ncclSuccess) nr = iq2::stream_settle(comm, s);
+    if (nr != ncclSuccess) {
+        // the other ranks did not all take part: nothing was mapped; give up on the communicator
+        const int rc = iq2::comm_failed(comm, op, "the handle exchange", nr);
+        if (base != nullptr) cudaFree(base);
+        return rc;
+    }
     if (e == cudaSuccess && nr == ncclSuccess)
         e = cudaMemcpy(h.data(), entries, sizeof(Entry) * comm->world, cudaMemcpyDeviceToHost);
     if (e == cudaSuccess) e = le;
@@ -275,7 +385,12 @@ int iq2_comm_symmetric_alloc(iq2_comm_t comm, size_t bytes, void** ptr) {
         if (r != comm->rank) e = cudaIpcOpenMemHandle(&comm->peer[r], h[r].handle, cudaIpcMemLazyEnablePeerAccess);
     // every rank takes part in this barrier whatever happened above, so none is left waiting
     const ncclResult_t br = comm_barrier(comm, s);  // every rank has mapped every region
-    if (nr == ncclSuccess) nr = br;
+    if (br != ncclSuccess) {
+        const int rc = iq2::comm_failed(comm, op, "the mapping barrier", br);
+        comm->symm = nullptr;  // a peer may have mapped it: left allocated
+        for (auto& q : comm->peer) q = nullptr;
+        return rc;
+    }
     if (entries != nullptr) cudaFree(entries);
     cudaStreamDestroy(s);
     if (e != cudaSuccess || nr != ncclSuccess || !same_size) {
@@ -291,15 +406,28 @@ int iq2_comm_symmetric_alloc(iq2_comm_t comm, size_t bytes, void** ptr) {
 
 int iq2_comm_check(iq2_comm_t comm) {
     if (comm == nullptr) return capi_fail(IQ2_ERR_INVALID_ARGUMENT, "iq2_comm_check: NULL comm");
+    if (comm->aborted)
+        return capi_fail(IQ2_ERR_COMM, "iq2_comm_check: the communicator was aborted after a wait on the other "
+                                       "ranks ran out or NCCL failed");
+    ncclResult_t st = ncclSuccess;
+    if (ncclCommGetAsyncError(comm->nccl, &st) == ncclSuccess && st != ncclSuccess && st != ncclInProgress)
+        return iq2::comm_failed(comm, "iq2_comm_check", "NCCL", st);
     if (comm->symm == nullptr) return iq2::capi_ok();
     unsigned err = 0;
     const cudaError_t e = cudaMemcpy(&err, &reinterpret_cast<iq2::SymmHeader*>(comm->symm)->err, sizeof(err),
                                      cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return iq2::capi_cuda_fail("iq2_comm_check", e);
-    if (err != 0)
-        return capi_fail(IQ2_ERR_COMM, "iq2_comm_check: a peer exchange timed out (%s%s); outputs of that call are incomplete",
-                         (err & 1u) ? "a rank never entered the call" : "",
-                         (err & 2u) ? ((err & 1u) ? ", a rank never finished" : "a rank never finished") : "");
+    if (err != 0) {
+        std::string why;
+        if (err & 1u) why += "a rank never entered a call";
+        if (err & 2u) why += std::string(why.empty() ? "" : ", ") + "a rank never finished a call";
+        if (err & 4u) why += std::string(why.empty() ? "" : ", ") + "a call failed on this rank before its launch";
+        return capi_fail(IQ2_ERR_COMM,
+                         "iq2_comm_check: a peer exchange failed (%s); the outputs of that call and of every later "
+                         "fused call of this communicator hold this rank's columns only (destroy the communicator "
+                         "to recover)",
+                         why.c_str());
+    }
     return iq2::capi_ok();
 }
 
@@ -320,6 +448,7 @@ int iq2_matmul_grouped_sharded(iq2_comm_t comm, const iq2_matmul_problem* proble
     if (count > iq2::SCATTER_CAP)
         return capi_fail(IQ2_ERR_UNSUPPORTED, "%s: at most %u projections per call, got %u", op, iq2::SCATTER_CAP,
                          count);
+    if (comm->aborted) return capi_fail(IQ2_ERR_COMM, "%s: the communicator was aborted", op);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device)
         return capi_fail(IQ2_ERR_DEVICE, "%s: the current device is not the communicator's Cuda(%d)", op,
@@ -349,8 +478,11 @@ int iq2_matmul_grouped_sharded(iq2_comm_t comm, const iq2_matmul_problem* proble
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     // 2. every rank's slices, rank-major
     float* gathered = pl.direct ? problems[0].out : reinterpret_cast<float*>(ws + pl.packed_bytes);
-    const ncclResult_t r = ncclAllGather(packed, gathered, pl.per_rank, ncclFloat, comm->nccl, s);
-    if (r != ncclSuccess) return capi_fail(IQ2_ERR_COMM, "%s: ncclAllGather: %s", op, ncclGetErrorString(r));
+    // (enqueued on the stream; a non-blocking communicator may still be connecting: bounded)
+    const ncclResult_t r =
+        iq2::nccl_settle(comm->nccl, ncclAllGather(packed, gathered, pl.per_rank, ncclFloat, comm->nccl, s),
+                         comm->timeout_ms);
+    if (r != ncclSuccess) return iq2::comm_failed(comm, op, "ncclAllGather", r);
     if (pl.direct) return iq2::capi_ok();
     // 3. slices -> each projection's [m, out_dim]
     iq2::ScatterLaunch L;

@@ -212,6 +212,15 @@ def grouped_workspace_bytes(problems) -> int:
     return int(lib.iq2_matmul_grouped_workspace_size(arr, len(problems), m, _X_DTYPES[dtype]))
 
 
+def device_check(device=None) -> None:
+    """Raise Iq2Error (IQ2_ERR_TIMEOUT) if a kernel of this library on `device` (default: the
+    current one) gave up on a bounded in-kernel wait since the previous check, i.e. some call's
+    outputs are incomplete although the call returned. Synchronises the device; clears the status."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().iq2_device_check())
+
+
 def iq2_dequantize(weight_bytes, weight_scales, out_dim, in_dim, variant=Iq2MatmulVariant.Iq2Xxs,
                    dtype: torch.dtype = torch.float16, out=None) -> torch.Tensor:
     """Dense [out_dim, in_dim] weights in f16 (reference-identical), bf16 (RNE) or f32 (exact)."""

@@ -41,7 +41,9 @@ class Iq2Comm:
     """The library's NCCL communicator over the ranks of a torch.distributed group (one GPU per
     rank, each rank's device current). Collective: every rank constructs it."""
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, timeout_ms: int = 120_000):
+        """`timeout_ms` bounds every wait on the other ranks (joining, NCCL calls, barriers): a wait
+        that runs out aborts the communicator and raises Iq2Error(IQ2_ERR_COMM)."""
         import torch.distributed as dist
         lib = _lib.load()
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
@@ -53,7 +55,7 @@ class Iq2Comm:
         dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
         uid = (ctypes.c_uint8 * _lib.IQ2_COMM_ID_BYTES).from_buffer_copy(obj[0])
         handle = ctypes.c_void_p()
-        _lib.check(lib.iq2_comm_init(uid, self.world, self.rank, ctypes.byref(handle)))
+        _lib.check(lib.iq2_comm_init_with_timeout(uid, self.world, self.rank, int(timeout_ms), ctypes.byref(handle)))
         self._h = handle
         self._symm = None  # (base address, bytes) of the symmetric region
         self._symm_used = 0
@@ -90,7 +92,8 @@ class Iq2Comm:
         return self._symm is not None
 
     def check(self):
-        """Raise if a fused exchange of this communicator timed out (synchronises the device)."""
+        """Raise if a fused exchange of this communicator failed, NCCL reported an asynchronous
+        error or the communicator was aborted (synchronises the device)."""
         with torch.cuda.device(self.device):
             _lib.check(_lib.load().iq2_comm_check(self._h))
 

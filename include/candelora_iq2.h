@@ -36,7 +36,7 @@ extern "C" {
 /* cudaStream_t without the CUDA headers (same type: struct CUstream_st*). NULL = legacy stream. */
 typedef struct CUstream_st* iq2_stream_t;
 
-#define IQ2_ABI_VERSION 1
+#define IQ2_ABI_VERSION 2
 
 /* Status codes. The reference bails with a message in each of these situations. */
 enum iq2_status {
@@ -50,14 +50,16 @@ enum iq2_status {
     IQ2_ERR_UNSUPPORTED = 7,      /* W4A8 in strict mode :300-302, :581-589; variant not built      */
     IQ2_ERR_WORKSPACE = 8,        /* workspace NULL or smaller than the *_workspace_size query      */
     IQ2_ERR_CUDA = 9,             /* a CUDA runtime call failed                                     */
-    IQ2_ERR_COMM = 10             /* an NCCL call of the sharded path failed                        */
+    IQ2_ERR_COMM = 10,            /* an NCCL call of the sharded path failed, or a wait on the
+                                     other ranks ran out (the communicator is then unusable)         */
+    IQ2_ERR_TIMEOUT = 11          /* a kernel of this library gave up on a bounded in-kernel wait   */
 };
 
 /* Activation dtypes (the reference dispatches on x.dtype(), src/iq2_matmul.rs:59-75). */
 enum iq2_dtype { IQ2_DTYPE_F32 = 0, IQ2_DTYPE_F16 = 1, IQ2_DTYPE_BF16 = 2 };
 
-/* Iq2MatmulVariant (src/iq2_matmul.rs:31-37). Only IQ2_XXS has kernels in this library; the
- * others return IQ2_ERR_UNSUPPORTED. */
+/* Iq2MatmulVariant (src/iq2_matmul.rs:31-37). Every variant has a matmul and a dequantisation
+ * kernel; the grouped, sharded and no-allocation entry points take IQ2_XXS only. */
 enum iq2_variant {
     IQ2_VARIANT_IQ2_XXS = 0,
     IQ2_VARIANT_IQ2_XS = 1,
@@ -73,6 +75,16 @@ const char* iq2_last_error(void);
 
 /* IQ2_ABI_VERSION of the loaded library. */
 int iq2_abi_version(void);
+
+/*
+ * Status of this library's bounded in-kernel waits on the current device. No reference
+ * counterpart: the reference's Metal dispatch has no in-kernel waits. The prefill GEMM's pipeline
+ * waits give up after 2 s (only a broken pipeline waits that long); a call whose kernel gave up
+ * has incomplete outputs although the call itself returned IQ2_OK (it was asynchronous). This
+ * synchronises the device and returns IQ2_ERR_TIMEOUT (with a message naming the waits) when any
+ * kernel gave up since the previous iq2_device_check, else IQ2_OK; the status is then cleared.
+ */
+int iq2_device_check(void);
 
 /* Bytes of device scratch iq2_matmul needs for this problem. 0 means none: workspace may then be NULL. */
 size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, int x_dtype,
@@ -151,7 +163,9 @@ int iq2_matmul_grouped(const iq2_matmul_problem* problems, uint32_t count, uint3
  * calls on a device: problems that would need more (large out_dim x m) fail with
  * IQ2_ERR_WORKSPACE, and calls whose kernels overlap on the GPU race on it. The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress); make it outside any stream
- * capture. m > 16 returns IQ2_ERR_UNSUPPORTED. Same checks and results as iq2_matmul otherwise.
+ * capture. The address is looked up again after the device's context was replaced
+ * (cudaDeviceReset). m > 16 returns IQ2_ERR_UNSUPPORTED. Same checks as iq2_matmul otherwise, and
+ * the same kernels, so the same results bit for bit.
  */
 int iq2_matmul_noalloc(const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
                        size_t weight_bytes_len, const uint8_t* weight_scales, size_t weight_scales_len,
@@ -199,6 +213,13 @@ int iq2_split_interleaved(const uint8_t* blocks, size_t blocks_len, uint64_t nbl
 #define IQ2_COMM_ID_BYTES 128
 typedef struct iq2_comm_s* iq2_comm_t;
 int iq2_comm_unique_id(uint8_t* id /* IQ2_COMM_ID_BYTES */);
+/* The communicator is a non-blocking NCCL communicator: every wait of this library on the other
+ * ranks (joining, NCCL calls, the barriers of iq2_comm_symmetric_alloc / iq2_comm_destroy) is
+ * polled and bounded by timeout_ms of wall time (iq2_comm_init: 120 s). A wait that runs out, or
+ * an asynchronous NCCL error, aborts the communicator and returns IQ2_ERR_COMM; every later call
+ * on it returns IQ2_ERR_COMM (iq2_comm_destroy still frees it). A rank that never calls
+ * iq2_comm_init makes the others' iq2_comm_init return IQ2_ERR_COMM after timeout_ms. */
+int iq2_comm_init_with_timeout(const uint8_t* id, int world, int rank, uint32_t timeout_ms, iq2_comm_t* comm);
 int iq2_comm_init(const uint8_t* id, int world, int rank, iq2_comm_t* comm);
 int iq2_comm_destroy(iq2_comm_t comm);  /* collective when a symmetric region exists */
 
@@ -209,11 +230,16 @@ int iq2_comm_destroy(iq2_comm_t comm);  /* collective when a symmetric region ex
  * One region per communicator, freed by iq2_comm_destroy. When every `out` of an
  * iq2_matmul_grouped_sharded call lies in the region (at the same offsets on all ranks) and
  * m <= 32, the decode GEMV stores each output straight into every rank's region: no NCCL call, no
- * gather buffer, one kernel launch. Its waits for the other ranks are bounded (about a second);
- * a wait that runs out leaves that call's outputs incomplete and is reported by iq2_comm_check.
+ * gather buffer, one kernel launch. Its waits for the other ranks are bounded (about a second).
+ * A wait that runs out, or a call that fails on one rank after the ranks chose this path (e.g. a
+ * misaligned weight slice), sets a sticky error: that call's outputs, and those of every later
+ * fused call of the communicator, hold only this rank's columns (the calls run local-only, with
+ * no waits), and iq2_comm_check reports IQ2_ERR_COMM on every rank until the communicator is
+ * destroyed.
  */
 int iq2_comm_symmetric_alloc(iq2_comm_t comm, size_t bytes, void** ptr);
-/* IQ2_OK, or IQ2_ERR_COMM if a fused exchange of this communicator timed out (synchronising). */
+/* IQ2_OK, or IQ2_ERR_COMM if a fused exchange of this communicator failed (synchronising), if
+ * NCCL reported an asynchronous error, or if the communicator was aborted. */
 int iq2_comm_check(iq2_comm_t comm);
 
 /* Workspace for iq2_matmul_grouped_sharded: the problems describe the rank's slices, with

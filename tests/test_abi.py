@@ -5,7 +5,7 @@ import ctypes
 import pytest
 import torch
 
-from conftest import header_functions
+from conftest import header_functions, header_prototypes
 from candelora_metal_kernels_b200 import _lib
 from candelora_metal_kernels_b200.build import LIB, build
 
@@ -21,6 +21,21 @@ def test_header_declares_the_expected_entry_points():
     assert names == sorted(_lib.SIGNATURES), names
 
 
+# (on 64-bit Linux ctypes.c_size_t is ctypes.c_uint64: size_t and uint64_t compare equal here)
+_CTYPES_CANON = {ctypes.c_void_p: "ptr", ctypes.c_char_p: "ptr", ctypes.c_uint32: "u32", ctypes.c_int: "i32",
+                 ctypes.c_uint64: "u64"}
+
+
+def test_python_binding_argument_lists_match_the_header():
+    """Every ctypes signature has the header's argument count and types, in order."""
+    protos = header_prototypes()
+    as_ctypes = {"usize": "u64"}
+    for name, (args, res) in _lib.SIGNATURES.items():
+        ret, params = protos[name]
+        assert [_CTYPES_CANON[a] for a in args] == [as_ctypes.get(t, t) for t in params], name
+        assert _CTYPES_CANON.get(res, "?") == as_ctypes.get(ret, ret), name
+
+
 def test_library_exports_every_header_symbol(lib):
     raw = ctypes.CDLL(str(LIB))
     for name in header_functions():
@@ -28,7 +43,7 @@ def test_library_exports_every_header_symbol(lib):
 
 
 def test_abi_version(lib):
-    assert lib.iq2_abi_version() == 1
+    assert lib.iq2_abi_version() == 2
 
 
 def _matmul(lib, m=1, out_dim=4, in_dim=256, variant=0, x_dtype=0):
@@ -65,7 +80,7 @@ def test_workspace_query_needs_no_device(lib):
     assert lib.iq2_matmul_workspace_size(16, 4096, 4096, 0, 0) > 0  # x limbs go through the workspace
     assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 0) == 0  # small K: limbs made in shared memory
     assert lib.iq2_matmul_workspace_size(0, 4096, 4096, 0, 0) == 0
-    assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 1) == 0  # no kernels for other variants
+    assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 1) == 0  # the other variants need no scratch
 
 
 def test_activation_quant_modes_without_device(lib):

@@ -82,3 +82,28 @@ def test_c_abi_workspace_contract():
     assert lib.iq2_matmul(*args, ctypes.c_void_p(ws.data_ptr()), need, stream) == _lib.IQ2_OK
     torch.cuda.synchronize()
     assert torch.isfinite(out).all()
+
+
+def test_gemm_wait_that_runs_out_is_reported_and_the_context_stays_usable():
+    """The prefill GEMM's pipeline waits are bounded: with the test hook a stage's "weights
+    written" arrival is withheld (a flag that nothing sets), the MMA thread's wait on it runs out
+    after 20 ms, and iq2_device_check reports IQ2_ERR_TIMEOUT; afterwards the status is clear and
+    the same call computes the right result again. No GPU fault is involved."""
+    lib = _lib.load()
+    m, n, k = 256, 512, 1024
+    qs, sc = synth.iq2xxs_weights(n, k, seed=7)
+    qs, sc = qs.cuda(), sc.cuda()
+    x = synth.activations(m, k, seed=8, dtype=torch.bfloat16, device="cuda")
+    want = c.iq2_xxs_matmul(x, qs, sc, n, k)
+    c.device_check()  # nothing timed out so far
+    assert lib.iq2_testing_set_gemm_stall(20_000_000, 2) == _lib.IQ2_OK
+    try:
+        c.iq2_xxs_matmul(x, qs, sc, n, k)  # returns at once: the kernel is asynchronous
+        with pytest.raises(c.Iq2Error, match="decoded weights") as e:
+            c.device_check()
+        assert e.value.code == _lib.IQ2_ERR_TIMEOUT
+    finally:
+        lib.iq2_testing_set_gemm_stall(0, 0)
+    c.device_check()  # the status was cleared by the check that reported it
+    assert torch.equal(c.iq2_xxs_matmul(x, qs, sc, n, k), want)
+    c.device_check()

@@ -131,12 +131,65 @@ def _rank_fused(rank: int, port: int, q):
             except c.Iq2Error as e:
                 res["timeout reported"] = 0.0 if e.code == _lib.IQ2_ERR_COMM else 1.0
         dist.barrier()
+        # one more call on both ranks: their call numbers now differ by one, so neither rank may
+        # return the other's stale columns as a success; each rank's own columns are still right
+        out2 = comm.symmetric_empty(1, 4096)
+        iq2_matmul_grouped_sharded(comm, [(x, *slices[0], 4096, 4096, out2)])
+        torch.cuda.synchronize()
+        try:
+            comm.check()
+            res["error reported after the mismatched call"] = 1.0
+        except c.Iq2Error as e:
+            res["error reported after the mismatched call"] = 0.0 if e.code == _lib.IQ2_ERR_COMM else 1.0
+        own = slice(rank * 2048, (rank + 1) * 2048)
+        res["own columns after the error"] = rel(out2[:, own], c.iq2_xxs_matmul(x, *full[0], 4096, 4096)[:, own])
+        dist.barrier()
         comm.close()
         dist.destroy_process_group()
         q.put((rank, res))
     except Exception as e:
         import traceback
         q.put((rank, repr(e) + traceback.format_exc()))
+
+
+def _lonely_init(q):
+    # rank 0 of a world of two, whose partner never calls iq2_comm_init
+    try:
+        import ctypes
+        import time
+        torch.cuda.set_device(0)
+        from candelora_metal_kernels_b200 import _lib
+        lib = _lib.load()
+        uid = (ctypes.c_uint8 * _lib.IQ2_COMM_ID_BYTES)()
+        _lib.check(lib.iq2_comm_unique_id(uid))
+        h = ctypes.c_void_p()
+        t0 = time.monotonic()
+        rc = lib.iq2_comm_init_with_timeout(uid, 2, 0, 3000, ctypes.byref(h))
+        q.put((rc, time.monotonic() - t0, lib.iq2_last_error().decode(), h.value))
+    except Exception as e:
+        q.put(repr(e))
+
+
+def test_comm_init_gives_up_when_a_rank_never_joins():
+    """A non-blocking communicator: the rank that waits for a partner that never comes gets
+    IQ2_ERR_COMM after its timeout (3 s here) instead of hanging; no GPU kernel is involved."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_lonely_init, args=(q,))
+    p.start()
+    try:
+        res = q.get(timeout=240)
+    finally:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    from candelora_metal_kernels_b200 import _lib
+    assert isinstance(res, tuple), res
+    rc, dt, msg, handle = res
+    assert rc == _lib.IQ2_ERR_COMM, (rc, msg)
+    assert "not every rank joined within 3000 ms" in msg
+    assert 2.5 <= dt < 120, dt
+    assert handle is None
 
 
 def _spawn(target):
