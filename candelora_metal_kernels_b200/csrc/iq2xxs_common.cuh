@@ -102,6 +102,16 @@ __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 
+// D = A (16x32 s8, row) * B (32x8 u8, col), s32 accumulate from zero.
+__device__ __forceinline__ void mma_s8u8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
 // Programmatic dependent launch (PTX griddepcontrol). `pdl_wait` blocks until every grid this
 // one depends on has completed and its memory is visible (a no-op for a normal launch);
 // `pdl_launch_dependents` lets the next PDL-launched kernel in the stream start early.

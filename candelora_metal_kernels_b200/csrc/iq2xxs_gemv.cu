@@ -14,12 +14,15 @@
 //     `prmt` turns a 16-bit selector (grid code | sign, from two lane-replicated shared-memory
 //     tables that each CTA builds, so a warp's random lookups never share a bank) into four
 //     signed int8 weights.
-//   * x is split per (token, 256-block) into four 7-bit signed limbs of a 28-bit fixed-point
-//     value (two limbs, 14 bits, for 16 < m <= 32, where the tolerance is the tensor-core
-//     path's): x @ W^T becomes mma.m16n8k32 s8 x s8 -> s32 per 32-weight sub-block, scaled by the
-//     odd integer 2s+1 in s32 (exact, |sum| < 2^31) and turned into f32 once per 256-block with d
-//     and the limb scale. The only rounding is the 2^-28-relative quantisation of x and f32
-//     rounding of per-block partial sums (rel. error ~1e-6).
+//   * x is turned per (token, 256-block) into fixed point: for m <= 4 four 7-bit signed limbs of
+//     a 28-bit value (two tokens fill the eight columns of one n8 tile); for 5 <= m <= 32 a
+//     16-bit value split into a signed high byte and an unsigned low byte (eight tokens per pair
+//     of n8 tiles: high bytes in the first half of the tiles, low bytes in the second, multiplied
+//     with mma .s8.u8). x @ W^T becomes mma.m16n8k32 per 32-weight sub-block, scaled by the odd
+//     integer 2s+1 in s32 (exact, |sum| < 2^31) and turned into f32 once per 256-block with d and
+//     the limb scale. The only roundings are the quantisation of x (2^-28 or 2^-16 of the
+//     block's largest |x|) and f32 rounding of per-block partial sums (rel. error ~1e-6 for
+//     m <= 4, ~4e-5 above).
 //   * Weights stream through a per-warp cp.async ring in shared memory (one 256-weight block of
 //     ROWS rows per stage), 16-byte chunks XOR-swizzled so the rows a warp reads together sit in
 //     different banks; one 16-byte read feeds two sub-blocks.
@@ -54,19 +57,21 @@ constexpr int MAX_PROBLEMS = 256;         // per grouped launch
 constexpr int MAX_CLUSTERS = 96;          // >= SMs / 2 of the device (74 on B200)
 constexpr int SMEM_LIMIT = 227 * 1024;
 
-// LB: x limbs per token (4: the 28-bit decode path, m <= 16; 2: 14 bits for 16 < m <= 32, where
-// the eight columns of an n8 tile carry four tokens instead of two; 1: the int8 activations of
-// the W8A8 mode, eight tokens per n8 tile).
+// LB: the x encoding. 4: four 7-bit limbs per token (28 bits, m <= 4, two tokens per n8 tile);
+// 16: the 16-bit split (5 <= m <= 32; tiles [0, NT/2) hold eight tokens' signed high bytes,
+// tiles [NT/2, NT) the same tokens' unsigned low bytes); 1: the int8 activations of the W8A8
+// mode, eight tokens per n8 tile.
 template <int NT, int LB = 4>
 struct GemvShape {
+    static constexpr bool SPLIT = LB == 16;
     static constexpr int T = ((NT <= 2 && LB != 1) || (NT == 1 && LB == 1)) ? 2 : 1;  // 16-row mma tiles per warp
     static constexpr int ROWS = 16 * T;                // rows of a tile
-    static constexpr int TPN = 8 / LB;                 // tokens per n8 tile
-    static constexpr int TOK = TPN * NT;               // tokens incl. the zero padding of the last n8 tile
+    static constexpr int TPN = SPLIT ? 8 : 8 / LB;     // tokens per n8 tile (SPLIT: per high-byte tile)
+    static constexpr int TOK = SPLIT ? 4 * NT : TPN * NT;  // tokens incl. the zero padding
     static constexpr int STAGE_QS = ROWS * 64;         // one block of qs per row
     static constexpr int STAGE_BYTES = STAGE_QS + ROWS * 4;  // + the aligned scale word per row
     // fewer stages where the partials (TOK x ROWS per warp slot) are large
-    static constexpr int NSTAGES = T == 2 ? 3 : ((LB == 4 || (LB == 1 && NT <= 2)) ? 6 : 4);
+    static constexpr int NSTAGES = T == 2 ? 3 : ((LB == 4 || (LB == 1 && NT <= 2) || (SPLIT && NT <= 4)) ? 6 : 4);
     static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;  // per warp
     static constexpr int PART_BYTES = GEMV_WARPS * 2 * TOK * ROWS * 4;  // [warp][first|last][token][row]
     // The table sits at the first 64 KB-aligned shared address of the block's window and the
@@ -74,9 +79,9 @@ struct GemvShape {
     static constexpr int SMEM = LUT_BYTES + (GEMV_WARPS + 1) * RING_BYTES + PART_BYTES;
 };
 
-int nt_for(uint32_t m) { return m <= 2 ? 1 : (m <= 4 ? 2 : (m <= 8 ? 4 : 8)); }
+int nt_for(uint32_t m) { return m <= 2 ? 1 : (m <= 8 ? 2 : (m <= 16 ? 4 : 8)); }
 int rows_for(uint32_t m) { return nt_for(m) <= 2 ? 32 : 16; }
-int limbs_for(uint32_t m) { return m <= 16 ? 4 : 2; }
+int limbs_for(uint32_t m) { return m <= 4 ? 4 : 16; }  // the LB of GemvShape
 int nt_w8a8(uint32_t m) { return m <= 8 ? 1 : (m <= 16 ? 2 : 4); }  // one limb: 8 tokens per n8 tile
 
 // x limbs of one block (256 k) of one x, for the kernel-side layout
@@ -113,45 +118,73 @@ __device__ __forceinline__ void limb_job(const XT* __restrict__ x, uint32_t M, u
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
     bad = __any_sync(0xFFFFFFFFu, bad);
 
-    // E from the exponent field (amax normal); 2^(27-E) is then a normal float for E >= -100,
-    // and x * 2^(27-E) is exact. Tiny or subnormal blocks take the library path.
+    // E from the exponent field (amax normal); 2^(B-E) is then a normal float for E >= -100,
+    // and x * 2^(B-E) is exact. Tiny or subnormal blocks take the library path.
     const uint32_t abits = __float_as_uint(amax);
-    constexpr int B = 7 * LB - 1;
+    constexpr int B = LB == 16 ? 15 : 7 * LB - 1;
     const bool fast = (abits >> 23) >= 27u;  // amax >= 2^-100
     int E = (int)(abits >> 23) - 126;
     if (!fast && !bad && amax > 0.0f) frexpf(amax, &E);
     const float sc = __uint_as_float((uint32_t)(127 + B - E) << 23);
-    uint32_t lo[LB], hi[LB];
+    if constexpr (LB == 16) {
+        // q = rint(x * 2^(15-E)) in [-32768, 32767] (|x| < 2^E; the clamp only touches a value
+        // that rounds up to 2^15), q = 256 * hi + lo with hi = q >> 8 signed, lo = q & 255 unsigned
+        uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+        if (!bad && amax > 0.0f) {
 #pragma unroll
-    for (int l = 0; l < LB; ++l) lo[l] = hi[l] = 0u;
-    if (!bad && amax > 0.0f) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int q = (int)rintf(fast ? v[i] * sc : ldexpf(v[i], B - E));
-            const uint32_t mag = (uint32_t)(q < 0 ? -q : q);
-#pragma unroll
-            for (int l = 0; l < LB; ++l) {
-                const int limb = (l < LB - 1) ? (int)((mag >> (7 * l)) & 127u) : (int)(mag >> (7 * (LB - 1)));
-                const uint32_t byte = (uint32_t)(uint8_t)(int8_t)(q < 0 ? -limb : limb);
-                if (i < 4) lo[l] |= byte << (8 * i);
-                else hi[l] |= byte << (8 * (i - 4));
+            for (int i = 0; i < 8; ++i) {
+                const float f = rintf(fast ? v[i] * sc : ldexpf(v[i], B - E));
+                const int q = (int)fminf(fmaxf(f, -32768.0f), 32767.0f);
+                hw[i >> 2] |= ((uint32_t)(q >> 8) & 255u) << (8 * (i & 3));
+                lw[i >> 2] |= ((uint32_t)q & 255u) << (8 * (i & 3));
             }
         }
-    }
-    constexpr uint32_t TPN = 8 / LB;
-    const uint32_t nt = m / TPN, colbase = (m % TPN) * LB;
-    const size_t sb = (size_t)b * 8 + sbi;
+        const uint32_t ntile = m >> 3, col = m & 7u;
+        const size_t sb = (size_t)b * 8 + sbi;
+        *reinterpret_cast<uint2*>(xb + ((sb * NT + ntile) * 32 + col * 4 + t) * 8) = make_uint2(hw[0], hw[1]);
+        *reinterpret_cast<uint2*>(xb + ((sb * NT + NT / 2 + ntile) * 32 + col * 4 + t) * 8) =
+            make_uint2(lw[0], lw[1]);
+        if (lane < 2) {
+            // column scale of the high byte 2^(E-15+8)/8, of the low byte 2^(E-15)/8
+            float s;
+            if (bad) s = __int_as_float(0x7FC00000);
+            else if (amax == 0.0f) s = 0.0f;
+            else s = ldexpf(1.0f, E - B - 3 + (lane == 0 ? 8 : 0));
+            colscale[(size_t)b * (NT * 8) + (lane == 0 ? ntile : NT / 2 + ntile) * 8 + col] = s;
+        }
+    } else {
+        uint32_t lo[LB], hi[LB];
 #pragma unroll
-    for (int l = 0; l < LB; ++l) {
-        uint2* dst = reinterpret_cast<uint2*>(xb + ((sb * NT + nt) * 32 + (colbase + l) * 4 + t) * 8);
-        *dst = make_uint2(lo[l], hi[l]);
-    }
-    if (lane < LB) {
-        float s;
-        if (bad) s = __int_as_float(0x7FC00000);
-        else if (amax == 0.0f) s = 0.0f;
-        else s = ldexpf(1.0f, E - B - 3 + 7 * lane);
-        colscale[(size_t)b * (NT * 8) + nt * 8 + colbase + lane] = s;
+        for (int l = 0; l < LB; ++l) lo[l] = hi[l] = 0u;
+        if (!bad && amax > 0.0f) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int q = (int)rintf(fast ? v[i] * sc : ldexpf(v[i], B - E));
+                const uint32_t mag = (uint32_t)(q < 0 ? -q : q);
+#pragma unroll
+                for (int l = 0; l < LB; ++l) {
+                    const int limb = (l < LB - 1) ? (int)((mag >> (7 * l)) & 127u) : (int)(mag >> (7 * (LB - 1)));
+                    const uint32_t byte = (uint32_t)(uint8_t)(int8_t)(q < 0 ? -limb : limb);
+                    if (i < 4) lo[l] |= byte << (8 * i);
+                    else hi[l] |= byte << (8 * (i - 4));
+                }
+            }
+        }
+        constexpr uint32_t TPN = 8 / LB;
+        const uint32_t nt = m / TPN, colbase = (m % TPN) * LB;
+        const size_t sb = (size_t)b * 8 + sbi;
+#pragma unroll
+        for (int l = 0; l < LB; ++l) {
+            uint2* dst = reinterpret_cast<uint2*>(xb + ((sb * NT + nt) * 32 + (colbase + l) * 4 + t) * 8);
+            *dst = make_uint2(lo[l], hi[l]);
+        }
+        if (lane < LB) {
+            float s;
+            if (bad) s = __int_as_float(0x7FC00000);
+            else if (amax == 0.0f) s = 0.0f;
+            else s = ldexpf(1.0f, E - B - 3 + 7 * lane);
+            colscale[(size_t)b * (NT * 8) + nt * 8 + colbase + lane] = s;
+        }
     }
 }
 
@@ -337,7 +370,7 @@ __device__ __forceinline__ void decode_group(const DecodeK& k, uint32_t aux_g, u
 // sub-block initialises I, so I needs no clearing. PARTIAL: only sub-blocks [s_lo, s_hi) count
 // (the first/last stage of a warp's range); the others see zero x fragments. FUSED: fragments
 // from shared memory (xsp: shared address), else from global memory (xbp).
-template <int NT, int T, bool PARTIAL, bool FUSED>
+template <int NT, int T, bool PARTIAL, bool FUSED, bool SPLIT>
 __device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, const uint8_t* xbp, uint32_t xsp,
                                               uint32_t s_lo, uint32_t s_hi, uint32_t rowbase, uint32_t swz,
                                               int (&I)[T][NT][4]) {
@@ -376,7 +409,8 @@ __device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, 
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     int d[4];
-                    mma_s8_16832(d, w0, w1, w2, w3, bf[nt][0], bf[nt][1]);
+                    if (SPLIT && nt >= NT / 2) mma_s8u8_16832(d, w0, w1, w2, w3, bf[nt][0], bf[nt][1]);
+                    else mma_s8_16832(d, w0, w1, w2, w3, bf[nt][0], bf[nt][1]);
                     if (sb == 0) {
                         I[tt][nt][0] = c0 * d[0];
                         I[tt][nt][1] = c0 * d[1];
@@ -684,9 +718,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         const uint8_t* xbp = FUSED ? nullptr : c_xb + (size_t)(cc.blk * (8u * NT * 256u));
         const uint32_t xsp = xs_s + cc.blk * 8 * NT * 256 + lane * 8;
         if (s_lo == 0 && s_hi == 8)
-            stage_compute<NT, T, false, FUSED>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
+            stage_compute<NT, T, false, FUSED, S_::SPLIT>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
         else
-            stage_compute<NT, T, true, FUSED>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
+            stage_compute<NT, T, true, FUSED, S_::SPLIT>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
 
         // Block epilogue: s32 -> f32 with d (per row) and the limb scale (per column).
         {
@@ -745,9 +779,19 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
-                if (LB == 1) {
-                    // one limb: the lane's four values are four outputs (tokens nt*8 + 2t and
-                    // nt*8 + 2t + 1, rows r0 and r1)
+                if (LB == 1 || LB == 16) {
+                    // one value per token and column: the lane's four values are four outputs
+                    // (tokens nt*8 + 2t and nt*8 + 2t + 1, rows r0 and r1); with the 16-bit split
+                    // the high-byte tile nt and the low-byte tile nt + NT/2 add up to them
+                    if (LB == 16 && nt >= NT / 2) {
+                        F[tt][nt][0] = F[tt][nt][1] = F[tt][nt][2] = F[tt][nt][3] = 0.0f;
+                        continue;
+                    }
+                    constexpr int LO = LB == 16 ? NT / 2 : 0;
+                    if (LB == 16) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) F[tt][nt][q] += F[tt][nt + LO][q];
+                    }
                     const uint32_t m0 = nt * 8 + 2 * t, m1 = m0 + 1;
                     if (complete) {
                         if (m0 < L.M) {
@@ -769,16 +813,14 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                     F[tt][nt][0] = F[tt][nt][1] = F[tt][nt][2] = F[tt][nt][3] = 0.0f;
                     continue;
                 }
-                // this lane's columns 2t, 2t+1: with four limbs half of a token's (the other
-                // half in lane t^1), with two limbs all of token nt*4 + t
+                // four limbs: this lane's columns 2t, 2t+1 are half of a token's (the other half
+                // in lane t^1)
                 float v0 = F[tt][nt][0] + F[tt][nt][1];
                 float v1 = F[tt][nt][2] + F[tt][nt][3];
-                if (LB == 4) {
-                    v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 1);
-                    v1 += __shfl_xor_sync(0xFFFFFFFFu, v1, 1);
-                }
-                const uint32_t m = LB == 4 ? nt * 2 + (t >> 1) : nt * 4 + t;
-                if (LB == 2 || (t & 1) == 0) {
+                v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, 1);
+                v1 += __shfl_xor_sync(0xFFFFFFFFu, v1, 1);
+                const uint32_t m = nt * 2 + (t >> 1);
+                if ((t & 1) == 0) {
                     if (complete) {
                         if (m < L.M) {
                             float* o = P.out + (size_t)m * P.ldo;
@@ -947,12 +989,14 @@ size_t smem_for_nt(int nt, int limbs, bool fused, uint32_t nb) {
             default: return smem_for<4, 1>(fused, nb);
         }
     }
-    switch (nt) {
-        case 1: return smem_for<1>(fused, nb);
-        case 2: return smem_for<2>(fused, nb);
-        case 4: return smem_for<4>(fused, nb);
-        default: return limbs == 2 ? smem_for<8, 2>(fused, nb) : smem_for<8>(fused, nb);
+    if (limbs == 16) {
+        switch (nt) {
+            case 2: return smem_for<2, 16>(fused, nb);
+            case 4: return smem_for<4, 16>(fused, nb);
+            default: return smem_for<8, 16>(fused, nb);
+        }
     }
+    return nt == 1 ? smem_for<1>(fused, nb) : smem_for<2>(fused, nb);  // four limbs: m <= 4
 }
 
 // How many 2-CTA clusters of the GEMV (one CTA per SM) the current device runs at once; launching
@@ -1162,11 +1206,11 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
     const bool p2p = peers != nullptr;
     if (p2p) L.peers = *peers;
     if (!pl.fused) e = launch_gemv_kernel_p<NT, CAP, -1, LB>(L, pl, p2p, stream);
-    else if constexpr (NT <= 2 && CAP == 1 && LB == 4) {
+    else if constexpr (NT <= 2 && CAP == 1 && (LB == 4 || LB == 16)) {
         switch (x_dtype) {
-            case 0: e = launch_gemv_kernel_p<NT, CAP, 0>(L, pl, p2p, stream); break;
-            case 1: e = launch_gemv_kernel_p<NT, CAP, 1>(L, pl, p2p, stream); break;
-            default: e = launch_gemv_kernel_p<NT, CAP, 2>(L, pl, p2p, stream); break;
+            case 0: e = launch_gemv_kernel_p<NT, CAP, 0, LB>(L, pl, p2p, stream); break;
+            case 1: e = launch_gemv_kernel_p<NT, CAP, 1, LB>(L, pl, p2p, stream); break;
+            default: e = launch_gemv_kernel_p<NT, CAP, 2, LB>(L, pl, p2p, stream); break;
         }
     } else {
         e = cudaErrorInvalidValue;  // the planner never fuses these
@@ -1178,17 +1222,21 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
 template <int NT>
 cudaError_t launch_group_nt(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
                             uint8_t* ws, const GroupPlan& pl, cudaStream_t stream, const GemvPeers* peers) {
-    // parameter capacity: a single projection ships ~1 KB of launch parameters, not 16 KB
-    if constexpr (NT == 8) {
-        if (pl.limbs == 2) {  // 16 < m <= 32
-            if (count <= 1) return launch_group_cap<8, 1, 2>(probs, count, m, x_dtype, ws, pl, stream, peers);
-            if (count <= 16) return launch_group_cap<8, 16, 2>(probs, count, m, x_dtype, ws, pl, stream, peers);
-            return launch_group_cap<8, MAX_PROBLEMS, 2>(probs, count, m, x_dtype, ws, pl, stream, peers);
+    // four limbs for one n8 tile (m <= 2), the 16-bit split for more; parameter capacity: a single
+    // projection ships ~1 KB of launch parameters, not 16 KB
+    if constexpr (NT <= 2) {
+        if (pl.limbs == 4) {  // m <= 4
+            if (count <= 1) return launch_group_cap<NT, 1, 4>(probs, count, m, x_dtype, ws, pl, stream, peers);
+            if (count <= 16) return launch_group_cap<NT, 16, 4>(probs, count, m, x_dtype, ws, pl, stream, peers);
+            return launch_group_cap<NT, MAX_PROBLEMS, 4>(probs, count, m, x_dtype, ws, pl, stream, peers);
         }
     }
-    if (count <= 1) return launch_group_cap<NT, 1>(probs, count, m, x_dtype, ws, pl, stream, peers);
-    if (count <= 16) return launch_group_cap<NT, 16>(probs, count, m, x_dtype, ws, pl, stream, peers);
-    return launch_group_cap<NT, MAX_PROBLEMS>(probs, count, m, x_dtype, ws, pl, stream, peers);
+    if constexpr (NT >= 2) {
+        if (count <= 1) return launch_group_cap<NT, 1, 16>(probs, count, m, x_dtype, ws, pl, stream, peers);
+        if (count <= 16) return launch_group_cap<NT, 16, 16>(probs, count, m, x_dtype, ws, pl, stream, peers);
+        return launch_group_cap<NT, MAX_PROBLEMS, 16>(probs, count, m, x_dtype, ws, pl, stream, peers);
+    }
+    return cudaErrorInvalidValue;  // (NT = 1 always has four limbs)
 }
 
 }  // namespace

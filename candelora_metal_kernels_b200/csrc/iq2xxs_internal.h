@@ -9,8 +9,8 @@ namespace iq2 {
 
 constexpr int kDtypeBf16 = 2;  // IQ2_DTYPE_BF16 of the C ABI
 
-// Decode GEMV (iq2xxs_gemv.cu), m <= kGemvMaxM (x in four 7-bit limbs for m <= 16, two for
-// 16 < m <= 32). A group is up to gemv_max_group() projections with the same m and x dtype,
+// Decode GEMV (iq2xxs_gemv.cu), m <= kGemvMaxM (x in four 7-bit limbs for m <= 4, as a 16-bit
+// value split into a signed and an unsigned byte for 4 < m <= 32). A group is up to gemv_max_group() projections with the same m and x dtype,
 // computed by one prep launch and one GEMV launch.
 constexpr uint32_t kGemvMaxM = 32;
 struct GemvProblemHost {

@@ -96,9 +96,9 @@ size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, 
  * ActivationQuantMode::Off, and through it iq2_xxs_matmul (:604-619).
  * m == 0 is valid and launches nothing (the reference returns an empty [0, out_dim] tensor).
  * weight_*_len are the element counts of the caller's buffers (checked like :246-259).
- * Routing (not part of the contract): IQ2_XXS with m <= 16 runs the decode GEMV (int8 tensor-core
- * decode, f32-accurate), 16 < m <= 32 the same GEMV with x in 14-bit fixed point (rel. error
- * ~1e-4), larger m the tcgen05 GEMM (bf16 operands, f32 accumulate); IQ2_XS, IQ2_S
+ * Routing (not part of the contract): IQ2_XXS with m <= 32 runs the decode GEMV (int8 tensor-core
+ * decode; x in 28-bit fixed point for m <= 4, rel. error ~1e-6, and 16-bit above, ~4e-5), larger
+ * m the tcgen05 GEMM (bf16 operands, f32 accumulate); IQ2_XS, IQ2_S
  * and IQ3_S run a generic f32 kernel (src/iq2_matmul.rs:884-1016 numerics, FMA accumulate).
  */
 int iq2_matmul(const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,
