@@ -53,7 +53,8 @@ def test_config3_ffn70b_decode_m1_single_and_grouped(oracle, ffn70b):
     grouped = c.iq2_matmul_grouped([(xs[i], qs, sc, n, k) for i, (_, k, n, qs, sc) in enumerate(ffn70b)])
     for i, (name, k, n, qs, sc) in enumerate(ffn70b):
         y = c.iq2_xxs_matmul(xs[i], qs, sc, n, k)
-        assert torch.equal(grouped[i], y), name
+        # (the grouped launch splits K over other warps, so only the partial-sum order differs)
+        assert rel_l2(grouped[i].double().cpu().numpy(), y.double().cpu().numpy()) <= 1e-6, name
         cols = _sample_cols(n, i)
         ref = oracle.matmul(xs[i].cpu().numpy(), qs.cpu().numpy(), sc.cpu().numpy(), n, k, cols=cols)
         assert rel_l2(y.cpu().numpy()[:, cols], ref) <= GEMV_TOL, name
@@ -112,13 +113,11 @@ def test_config4_two_layer_chain(oracle, m):
             ref = oracle.matmul(inputs[nm], qs, sc, n, k, cols=cols)
             assert rel_l2(g[nm][:, cols], ref) <= GEMV_TOL, (li, nm)
 
-    # the oracle's own chain, end to end
+    # the oracle's own chain, end to end (the next layer's x depends on up -> down only)
     xo = x0.numpy()
     for lay in Wh:
         def mm(nm, inp):
             k, n, qs, sc = lay[nm]
             return oracle.matmul(inp, qs, sc, n, k)
-        q, up = mm("q", xo), mm("up", xo)
-        mm("o", q)
-        xo = _rms_norm(mm("down", up))
+        xo = _rms_norm(mm("down", mm("up", xo)))
     assert rel_l2(gpu_final, xo) <= CHAIN_TOL
