@@ -392,6 +392,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             line["gemm"] = gemm_bench(args, device, stream, peaks, peak_src)
         if not args.no_next_rows and world == 1:
             line["next_rows"] = next_rows_bench(args, device, stream, peaks, peak_src)
+        if not args.no_config01 and world == 1:
+            line.update(config01_bench(args, device, stream, peaks, peak_src))
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args)
     return line
@@ -540,6 +542,102 @@ def ffn70b_bench(args, device, stream, comm, rank, world, peaks):
                         + (f", column-sharded over {world} GPUs (M=1: "
                            + ("fused peer-memory all-gather" if comm.has_symmetric else "NCCL all-gather")
                            + "; M=2048: NCCL all-gather)" if dist else ""), **res}
+
+
+# ---------------------------------------------------------------------------------------- configs 0/1
+def config01_bench(args, device, stream, peaks, peak_src):
+    """Benchmark configurations 0 and 1 on one GPU, every M the configuration names.
+
+    config1: M in {1, 4, 8, 16}, f32 x ~N(0,1), the Llama-3-8B projection shapes. Per M: the step of
+    8 layers (56 projections, 450 MB of packed weights) as one grouped call and as 56 reference-shaped
+    calls, and per shape one call at a time over enough distinct matrices to exceed 260 MB (> 2x L2).
+    config0: M=1, 4096x4096, one call (the GPU line), and the reference's own kernels on the host
+    cores for the same matvec (its CPU line). CUDA events around replays of CUDA graphs."""
+    import candelora_metal_kernels_b200 as c
+    from candelora_metal_kernels_b200 import synth
+    hbm = peaks["hbm_gbs"]
+
+    def graph_ms(fn, reps):
+        with torch.cuda.stream(stream):
+            fn()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        with torch.cuda.stream(stream):
+            g.replay()
+        ms = _time_graph(g, reps, stream) / reps
+        del g
+        return ms
+
+    def line(nbytes, ms):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        return {"us": round(ms * 1e3, 2), "weight_gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4)}
+
+    shapes = [("q/o", 4096, 4096), ("k/v", 4096, 1024), ("gate/up", 4096, 14336), ("down", 14336, 4096)]
+    mats = {}
+    for (name, k, n) in shapes:
+        copies = max(4, int(260e6 // synth.packed_bytes(n, k)) + 1)
+        mats[name] = [synth.iq2xxs_weights(n, k, seed=3000 + 97 * i + n, device=device) for i in range(copies)]
+    res = {}
+    for m in (1, 4, 8, 16):
+        r = {}
+        for (name, k, n) in shapes:
+            x = synth.activations(m, k, seed=31 + m, device=device)
+            out = torch.empty(m, n, device=device)
+            ws = torch.empty(max(1, c.workspace_bytes(m, n, k, torch.float32)), dtype=torch.uint8, device=device)
+            ml = mats[name]
+
+            def calls(ml=ml, x=x, out=out, ws=ws, n=n, k=k):
+                for (qs, sc) in ml:
+                    c.iq2_xxs_matmul(x, qs, sc, n, k, out=out, workspace=ws)
+            ms = graph_ms(calls, 5) / len(ml)
+            r[f"single_{k}x{n}"] = line(synth.packed_bytes(n, k), ms)
+        probs, wbytes = [], 0
+        for layer in range(8):
+            for pi, (name, k, n) in enumerate(synth.LLAMA3_8B_PROJECTIONS):
+                qs, sc = synth.iq2xxs_weights(n, k, seed=layer * 16 + pi, device=device)
+                probs.append((synth.activations(m, k, seed=pi, device=device), qs, sc, n, k,
+                              torch.empty(m, n, device=device)))
+                wbytes += synth.packed_bytes(n, k)
+        gws = torch.empty(max(1, c.grouped_workspace_bytes(probs)), dtype=torch.uint8, device=device)
+        r["step_8_layers_grouped"] = line(wbytes, graph_ms(lambda: c.iq2_matmul_grouped(probs, workspace=gws), 10))
+        pws = {}
+        for (x, qs, sc, n, k, o) in probs:
+            pws.setdefault((n, k), torch.empty(max(1, c.workspace_bytes(m, n, k, torch.float32)), dtype=torch.uint8,
+                                               device=device))
+
+        def per_call():
+            for (x, qs, sc, n, k, o) in probs:
+                c.iq2_xxs_matmul(x, qs, sc, n, k, out=o, workspace=pws[(n, k)])
+        r["step_8_layers_per_call"] = line(wbytes, graph_ms(per_call, 10))
+        res[f"m{m}"] = r
+        del probs, gws, pws
+    del mats
+    torch.cuda.empty_cache()
+    cfg0 = dict(res["m1"]["single_4096x4096"])
+    if not args.no_cpu_baseline:
+        from oracle.oracle import Oracle, RefKernels
+        kind = "reference" if RefKernels.available() else "port"
+        impl = RefKernels() if kind == "reference" else Oracle()
+        qs, sc = synth.iq2xxs_weights(4096, 4096, seed=0)
+        x = synth.activations(1, 4096, seed=1).numpy()
+        qs, sc = qs.numpy(), sc.numpy()
+        threads = os.cpu_count() or 1
+        run = ((lambda: impl.matmul(x, qs, sc, 4096, 4096, "f32", threads=threads)) if kind == "reference"
+               else (lambda: impl.matmul(x, qs, sc, 4096, 4096, threads=threads)))
+        run()
+        t0, reps = time.perf_counter(), 0
+        while time.perf_counter() - t0 < 2.0:
+            run()
+            reps += 1
+        cms = (time.perf_counter() - t0) / reps * 1e3
+        cfg0["cpu"] = {"ms": round(cms, 3), "weight_gbs": round(synth.packed_bytes(4096, 4096) / (cms * 1e-3) / 1e9, 3),
+                       "cores": threads, "kind": kind}
+    return {"config0": {"workload": "M=1, K=N=4096, f32 x, one call", **cfg0},
+            "config1": {"workload": "Llama-3-8B projection shapes, f32 x, M in {1,4,8,16}; single calls over "
+                                    "> 260 MB of distinct matrices per shape, and the 8-layer step (450 MB) "
+                                    "grouped and per call", "peak_hbm_gbs": hbm, "peak_source": peak_src, **res}}
 
 
 # ---------------------------------------------------------------------------------------- GEMM
@@ -824,6 +922,7 @@ def main():
     ap.add_argument("--no-next-rows", action="store_true",
                     help="skip the W8A8 / IQ2_XS / IQ2_S / IQ3_S / dequant / ggml-repack measurements")
     ap.add_argument("--no-models", action="store_true", help="skip the configuration 3 and 4 measurements")
+    ap.add_argument("--no-config01", action="store_true", help="skip the configuration 0 and 1 sweep (M = 1, 4, 8, 16)")
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
                     help="N > 1: how the sharded decode's output slices reach every rank")
     ap.add_argument("--gemm-reps", type=int, default=5)
