@@ -19,9 +19,14 @@
 //     64-k stage 2 x 4 tcgen05.mma (M=128, N=BN, K=16) from one thread; tcgen05.commit frees each
 //     stage when the tensor core has read it. The tiles of the last, part-full wave of CTAs are
 //     split over K (partial tiles, summed in order by splitk_tile_sum_kernel).
-//   * Pipeline: 3 stages of 64 KB, mbarriers for "x landed" (TMA transaction bytes), "weights
-//     written" (decode warps) and "stage free" (MMA commit). Every wait is bounded: on timeout
-//     the kernel records an error code, stops issuing work and still frees its TMEM.
+//   * Paired CTAs (m > 256): 2-CTA clusters share one 256-row weight tile across two 256-token
+//     tiles with the paired MMA (tcgen05.mma.cta_group::2, M=256): each CTA decodes only its 128
+//     rows of the weights, so the decode per MMA is halved (the decode, not the tensor core or
+//     the x loads, is what bounds the unpaired kernel).
+//   * Pipeline: 3 stages of 64 KB (paired: 4 of 48 KB), mbarriers for "x landed" (TMA transaction
+//     bytes), "weights written" (decode warps) and "stage free" (MMA commit). Every wait is
+//     bounded: on timeout the kernel records an error code, stops issuing work and still frees its
+//     TMEM.
 //   * Epilogue: TMEM -> registers -> a 32 x 32 tile in the idle stage ring -> TMA store.
 // No TMA multicast is used anywhere (this library also runs on multi-GPU jobs).
 #include "iq2xxs_common.cuh"
@@ -53,8 +58,19 @@ constexpr int G_STAGE_BYTES = G_A_BYTES + G_B_BYTES;
 constexpr int G_SEL_COPIES = 16;                 // the decode table, once per lane of a half-warp
 constexpr int G_SEL_BYTES = 256 * G_SEL_COPIES * 8;  // selector pairs per grid code, interleaved copies
 constexpr int G_SMEM = 1024 /*align*/ + G_STAGES * G_STAGE_BYTES + G_SEL_BYTES + 256 /*barriers*/;
+// Paired CTAs hold half of the weight tile each (128 rows): 48 KB stages, four of them in the same
+// shared memory.
+constexpr int G_STAGES_PAIR = 4;
+constexpr int G_STAGE_BYTES_PAIR = G_A_BYTES + (G_BN / 2) * G_BK * 2;
+static_assert(G_STAGES_PAIR * G_STAGE_BYTES_PAIR <= G_STAGES * G_STAGE_BYTES, "paired stages fit the ring");
 constexpr uint32_t G_TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: only a broken pipeline waits that long
+
+// Paired CTAs (see gemm_kernel) for m > 256 (0: always unpaired).
+#ifndef IQ2_GEMM_PAIR
+#define IQ2_GEMM_PAIR 1
+#endif
+constexpr bool g_pair_enabled = IQ2_GEMM_PAIR != 0;
 
 // Per-device sticky status of the GEMM's bounded waits (the bits of the waits that ran out since
 // the last iq2_device_check; 0 = none). Every GPU that loads the library has its own copy.
@@ -66,9 +82,10 @@ uint64_t g_wait_limit_ns = WAIT_LIMIT_NS;
 uint32_t g_stall_stage = 0;  // 0: none; s > 0: stage s - 1 of every CTA
 
 // Instruction descriptor, kind::f16: F32 accumulate, BF16 A and B, both K-major, M=128, N=BN.
-template <int BN>
+// (MM = 256: the paired form, cta_group::2, each CTA holding 128 of the rows.)
+template <int BN, int MM = 128>
 constexpr uint32_t idesc_for() {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(MM >> 4) << 24);
 }
 
 // The launch's work units (blockIdx.x): tiles t = (m-tile t / nt, n-tile t % nt). The first `full`
@@ -135,6 +152,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     }
 }
 
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t map_peer(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// An arrival on a barrier of either CTA of the pair (a shared::cluster address), with the default
+// (CTA-scope release) semantics: a cluster-scope release would also wait for the thread's loads in
+// flight.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -174,6 +211,44 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
 }
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// The paired forms (cta_group::2, issued by the even CTA of a 2-CTA cluster): one MMA of M = 256
+// whose A rows (128 per CTA) and B rows (N/2 per CTA) are read from both CTAs' shared memory at the
+// same offsets, each CTA's 128 rows of D landing in its own TMEM; a commit that arrives on the
+// barrier at this offset in both CTAs (mask 3).
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"((uint16_t)3u)
+        : "memory");
+}
+// TMEM allocation: the whole warp, in both CTAs of a pair for the paired form.
+template <bool PAIR>
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_word, uint32_t cols) {
+    if (PAIR) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_word), "r"(cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_word), "r"(cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+}
+template <bool PAIR>
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    if (PAIR)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+    else
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
 }
 
 // SW128 K-major shared-memory matrix descriptor: start address, LBO = 16 B (unused for swizzled
@@ -250,53 +325,106 @@ __device__ __forceinline__ void decode_sub(uint2 q, float d, uint32_t sel_l, uin
     }
 }
 
+// Half of decode_sub for the paired kernel: groups 2*half and 2*half + 1 of the sub-block (the
+// chunks at dst ^ (t << 4), t = 2*half + tt).
+template <bool TAIL>
+__device__ __forceinline__ void decode_half(uint2 q, float d, uint32_t sel_l, uint32_t dst, uint32_t half,
+                                            uint32_t k_lo, uint32_t K) {
+    const uint32_t aux_g = q.x, aux_s = q.y;
+    const float dl = d * (float)((aux_s >> 27) | 1u) * 0.125f;  // d*(2s+1)/8, exact
+    const uint32_t qlo = cvt_bf16x2(dl * 8.0f, dl * 25.0f);
+    const uint32_t qhi = cvt_bf16x2(dl * 43.0f, 0.0f);
+#pragma unroll
+    for (int tt = 0; tt < 2; ++tt) {
+        const uint32_t t = 2 * half + tt;
+        const uint32_t gi = (aux_g >> (8 * t)) & 0xFFu, si = (aux_s >> (7 * t)) & 0x7Fu;
+        const uint2 sel = ld_shared_v2_const(sel_l + gi * (G_SEL_COPIES * 8));
+        const uint32_t S = si | ((__popc(si) & 1u) << 7);
+        uint4 w;
+        w.x = prmt(qlo, qhi, sel.x) ^ ((S * 0x40008000u) & 0x80008000u);
+        w.y = prmt(qlo, qhi, sel.x >> 16) ^ ((S * 0x10002000u) & 0x80008000u);
+        w.z = prmt(qlo, qhi, sel.y) ^ ((S * 0x04000800u) & 0x80008000u);
+        w.w = prmt(qlo, qhi, sel.y >> 16) ^ ((S * 0x01000200u) & 0x80008000u);
+        if (TAIL && k_lo + t * 8 + 8 > K) {
+            const uint32_t k0 = k_lo + t * 8;
+            const uint32_t keep = k0 >= K ? 0u : K - k0;
+            w.x = keep >= 2 ? w.x : (keep == 1 ? (w.x & 0xFFFFu) : 0u);
+            w.y = keep >= 4 ? w.y : (keep == 3 ? (w.y & 0xFFFFu) : 0u);
+            w.z = keep >= 6 ? w.z : (keep == 5 ? (w.z & 0xFFFFu) : 0u);
+            w.w = keep >= 8 ? w.w : (keep == 7 ? (w.w & 0xFFFFu) : 0u);
+        }
+        st_shared_v4(dst ^ (t << 4), w);
+    }
+}
+
 // ---- the kernel ----
 // BN: weight rows per CTA (256, or 224 where that fills the last wave better); the stage
 // layout is always sized for 256 rows.
-template <int BN>
+// PAIR: 2-CTA clusters on one 256-row weight tile and two consecutive 256-token tiles (CTA rank r
+// takes token tile 2j + r), with the paired tensor-core form (cta_group::2): CTA r decodes weight
+// rows [128r, 128r + 128) of the tile into its own stage, and the even CTA's MMAs (M = 256: its
+// own 128 tokens of a half and the odd CTA's) read both halves of the weights from the two CTAs'
+// shared memory. Every weight is decoded once per 512 tokens instead of once per 256, with no
+// shared-memory traffic between the CTAs. The even CTA's `full_b` counts the decode warps of both
+// CTAs plus one arrival from the odd CTA's idle MMA warp, which relays that the odd CTA's x tile
+// has landed (each CTA's x loads complete on its own `full_a`, so that an aborted CTA can still
+// wait for its own loads). The even CTA's commits arrive on both CTAs' `empty` and `acc_full`. No
+// TMA multicast.
+template <int BN, bool PAIR>
 __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                             const __grid_constant__ CUtensorMap tmap_out,
                                                             const __grid_constant__ CUtensorMap tmap_part,
                                                             const GemmParams p) {
     static_assert(BN % 32 == 0 && BN <= G_BN, "BN");
+    static_assert(!PAIR || BN == G_BN, "paired CTAs split a 256-row tile");
+    constexpr int S = PAIR ? G_STAGES_PAIR : G_STAGES;                 // stages in the ring
+    constexpr uint32_t SB = PAIR ? G_STAGE_BYTES_PAIR : G_STAGE_BYTES;  // bytes per stage
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_s = smem_u32(smem_raw);
     const uint32_t base_s = (raw_s + 1023u) & ~1023u;  // SW128 tiles need 1024-byte alignment
     uint8_t* base = smem_raw + (base_s - raw_s);
-    const uint32_t sel_s = base_s + G_STAGES * G_STAGE_BYTES;
+    const uint32_t sel_s = base_s + S * SB;
     const uint32_t bar_s = sel_s + G_SEL_BYTES;
     // barriers: full_a[S], full_b[S], empty[S], acc_full; then the TMEM address word; abort flag
     auto full_a = [&](int s) { return bar_s + 8u * s; };
-    auto full_b = [&](int s) { return bar_s + 8u * (G_STAGES + s); };
-    auto empty = [&](int s) { return bar_s + 8u * (2 * G_STAGES + s); };
-    const uint32_t acc_full = bar_s + 8u * (3 * G_STAGES);
-    uint32_t* tmem_addr_word = reinterpret_cast<uint32_t*>(base + (bar_s - base_s) + 8 * (3 * G_STAGES + 1));
+    auto full_b = [&](int s) { return bar_s + 8u * (S + s); };
+    auto empty = [&](int s) { return bar_s + 8u * (2 * S + s); };
+    const uint32_t acc_full = bar_s + 8u * (3 * S);
+    uint32_t* tmem_addr_word = reinterpret_cast<uint32_t*>(base + (bar_s - base_s) + 8 * (3 * S + 1));
     volatile uint32_t* abort_flag = tmem_addr_word + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // this CTA's unit: tile t, K range z of nz; pu = its partial tile (-1: the tile is whole)
+    // this CTA's unit: tile t, K range z of nz; pu = its partial tile (-1: the tile is whole).
+    // PAIR: units are pairs (cluster = blockIdx.x / 2, rank = the CTA's rank in it); tile t is a
+    // pair tile (n-tile t % nt, token tiles 2 * (t / nt) + rank), partial tile (2 * (t - full) +
+    // rank) * s + z.
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u, unit = PAIR ? blockIdx.x >> 1 : blockIdx.x;
+    const bool leader = rank == 0;  // (always, unpaired)
     uint32_t t, z, nz;
     int pu;
-    if (blockIdx.x < p.full) {
-        t = blockIdx.x;
+    if (unit < p.full) {
+        t = unit;
         z = 0;
         nz = 1;
         pu = -1;
     } else {
-        const uint32_t v = blockIdx.x - p.full;
+        const uint32_t v = unit - p.full;
         t = p.full + v / p.s;
         z = v % p.s;
         nz = p.s;
-        pu = (int)v;
+        pu = PAIR ? (int)((2 * (v / p.s) + rank) * p.s + z) : (int)v;
     }
-    const uint32_t n0 = (t % p.nt) * BN, m0 = (t / p.nt) * G_BM;
+    const uint32_t n0 = (t % p.nt) * BN, m0 = (PAIR ? 2 * (t / p.nt) + rank : t / p.nt) * G_BM;
     // this CTA's share of K: the 256-blocks [b0, b1) of range z, i.e. the 64-k stages
     // [kt0, kt0 + NKT) (at least one: the host never makes more ranges than blocks)
     const uint32_t b0 = (uint32_t)((uint64_t)z * p.nb / nz);
     const uint32_t b1 = (uint32_t)((uint64_t)(z + 1) * p.nb / nz);
     const uint32_t kt0 = b0 * (QK / G_BK);
     const uint32_t NKT = min(b1 * (QK / G_BK), (p.K + G_BK - 1) / G_BK) - kt0;
-    const bool upper = m0 + 128 < p.M;  // the tile's second 128-token half holds tokens
+    const bool upper = m0 + 128 < p.M;  // this CTA's second 128-token half holds tokens
+    // the second MMA (second halves) runs when the first token tile's second half holds tokens
+    // (PAIR: the even CTA's; the odd CTA then loads its second half too, zeros past M)
+    const bool upper_mma = (PAIR ? m0 - rank * G_BM : m0) + 128 < p.M;
 
     // decode table -> shared memory: per grid entry the four 16-bit prmt selectors packed in two
     // words, G_SEL_COPIES times (copy c of entry e at (e * G_SEL_COPIES + c) * 8)
@@ -305,26 +433,24 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
         reinterpret_cast<uint2*>(base + (sel_s - base_s))[i] = make_uint2(e[0] | (e[1] << 16), e[2] | (e[3] << 16));
     }
     if (threadIdx.x == 0) {
-        for (int s = 0; s < G_STAGES; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(full_a(s), 1);
-            mbar_init(full_b(s), G_DEC_WARPS);
+            // the decode warps (PAIR: both CTAs', plus the odd CTA's relay; only the even CTA's is used)
+            mbar_init(full_b(s), PAIR ? 2 * G_DEC_WARPS + 1 : G_DEC_WARPS);
             mbar_init(empty(s), 1);
         }
         mbar_init(acc_full, 1);
         *abort_flag = 0u;
         fence_barrier_init();
     }
-    if (warp == G_MMA_WARP) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         smem_u32(tmem_addr_word)),
-                     "r"(G_TMEM_COLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
+    if (warp == G_MMA_WARP) tmem_alloc<PAIR>(smem_u32(tmem_addr_word), G_TMEM_COLS);
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_barrier();  // the peer's barriers are initialised before anything reaches them
     tc_fence_after();
     const uint32_t tmem = *tmem_addr_word;
+    // the even CTA's `full_b` (shared::cluster addresses), where the odd CTA's arrivals go
+    const uint32_t full_b_lead0 = PAIR ? map_peer(full_b(0), 0u) : 0u;
 
     if (warp == G_TMA_WARP) {
         // ---------------- x producer ----------------
@@ -332,8 +458,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
             uint32_t issued = 0;
             bool aborted = false;
             for (uint32_t i = 0; i < NKT; ++i) {
-                const int s = i % G_STAGES;
-                if (i >= G_STAGES && !mbar_wait(empty(s), ((i / G_STAGES) - 1) & 1, p.err, 1u, p.wait_ns)) {
+                const int s = i % S;
+                if (i >= (uint32_t)S && !mbar_wait(empty(s), ((i / S) - 1) & 1, p.err, 1u, p.wait_ns)) {
                     *abort_flag = 1u;
                     aborted = true;
                     break;
@@ -342,43 +468,65 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
                     aborted = true;
                     break;
                 }
-                const uint32_t a_s = base_s + s * G_STAGE_BYTES;
+                const uint32_t a_s = base_s + s * SB;
                 const int kx = (int)((kt0 + i) * G_BK);
-                mbar_expect_tx(full_a(s), upper ? G_A_BYTES : G_A_HALF);
+                mbar_expect_tx(full_a(s), upper_mma ? G_A_BYTES : G_A_HALF);
                 tma_load_2d(a_s, &tmap_x, full_a(s), kx, (int)m0);
-                if (upper) tma_load_2d(a_s + G_A_HALF, &tmap_x, full_a(s), kx, (int)(m0 + 128));
+                if (upper_mma) tma_load_2d(a_s + G_A_HALF, &tmap_x, full_a(s), kx, (int)(m0 + 128));
                 ++issued;
             }
             // after an abort, the loads already issued (at most one per stage slot, each the last
             // use of its slot) land before the CTA's shared memory goes away (bounded as well)
             if (aborted)
-                for (uint32_t j = issued > G_STAGES ? issued - G_STAGES : 0u; j < issued; ++j)
-                    mbar_wait(full_a(j % G_STAGES), (j / G_STAGES) & 1u, p.err, 32u, p.wait_ns);
+                for (uint32_t j = issued > (uint32_t)S ? issued - S : 0u; j < issued; ++j)
+                    mbar_wait(full_a(j % S), (j / S) & 1u, p.err, 32u, p.wait_ns);
         }
     } else if (warp == G_MMA_WARP) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        if (lane == 0 && leader) {
+            // ---------------- MMA issuer ----------------
             bool ok = true;
             for (uint32_t i = 0; i < NKT && ok; ++i) {
-                const int s = i % G_STAGES;
-                const uint32_t ph = (i / G_STAGES) & 1;
+                const int s = i % S;
+                const uint32_t ph = (i / S) & 1;
                 ok = mbar_wait(full_a(s), ph, p.err, 2u, p.wait_ns) && mbar_wait(full_b(s), ph, p.err, 4u, p.wait_ns);
                 if (!ok || *abort_flag) {
                     *abort_flag = 1u;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a_s = base_s + s * G_STAGE_BYTES, b_s = a_s + G_A_BYTES;
+                const uint32_t a_s = base_s + s * SB, b_s = a_s + G_A_BYTES;
 #pragma unroll
                 for (int ks = 0; ks < G_BK / 16; ++ks) {
                     const uint64_t bd = sw128_desc(b_s + ks * 32);
                     const uint32_t acc = (i | ks) ? 1u : 0u;
-                    tc_mma(tmem, sw128_desc(a_s + ks * 32), bd, idesc_for<BN>(), acc);
-                    if (upper) tc_mma(tmem + 256, sw128_desc(a_s + G_A_HALF + ks * 32), bd, idesc_for<BN>(), acc);
+                    if (PAIR) {
+                        tc_mma_pair(tmem, sw128_desc(a_s + ks * 32), bd, idesc_for<BN, 256>(), acc);
+                        if (upper_mma)
+                            tc_mma_pair(tmem + 256, sw128_desc(a_s + G_A_HALF + ks * 32), bd, idesc_for<BN, 256>(),
+                                        acc);
+                    } else {
+                        tc_mma(tmem, sw128_desc(a_s + ks * 32), bd, idesc_for<BN>(), acc);
+                        if (upper_mma)
+                            tc_mma(tmem + 256, sw128_desc(a_s + G_A_HALF + ks * 32), bd, idesc_for<BN>(), acc);
+                    }
                 }
-                tc_commit(empty(s));  // the stage is free once these MMAs have read it
+                // the stage is free once these MMAs have read it (PAIR: in both CTAs)
+                if (PAIR) tc_commit_pair(empty(s));
+                else tc_commit(empty(s));
             }
-            tc_commit(acc_full);      // fires when every MMA issued above has completed
+            // fires when every MMA issued above has completed
+            if (PAIR) tc_commit_pair(acc_full);
+            else tc_commit(acc_full);
+        } else if (lane == 0 && PAIR) {
+            // ---------------- the odd CTA: relay "x landed" to the even CTA ----------------
+            for (uint32_t i = 0; i < NKT; ++i) {
+                const int s = i % S;
+                if (!mbar_wait(full_a(s), (i / S) & 1, p.err, 2u, p.wait_ns) || *abort_flag) {
+                    *abort_flag = 1u;
+                    break;
+                }
+                mbar_arrive_cluster(full_b_lead0 + 8u * s);
+            }
         }
     } else {
         // ---------------- weight decode (warps 0..15), then epilogue ----------------
@@ -386,9 +534,13 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
         // BN skip the decode (the MMA never reads those rows); a row past N decodes row N - 1
         // instead (it only reaches accumulator columns the epilogue skips), so the loop carries no
         // per-thread condition.
-        const uint32_t r = threadIdx.x & 255u, hh = threadIdx.x >> 8;
+        // PAIR: thread = (row r of this CTA's 128, sub-block hh, half `ghalf` of its four groups);
+        // the weight row is n0 + 128 * rank + r.
+        const uint32_t r = PAIR ? (threadIdx.x & 127u) : threadIdx.x & 255u;
+        const uint32_t hh = PAIR ? (threadIdx.x >> 8) & 1u : threadIdx.x >> 8;
+        const uint32_t ghalf = (threadIdx.x >> 7) & 1u;  // (PAIR only)
         const bool live = (r & ~31u) < (uint32_t)BN;  // warp-uniform: BN is a multiple of 32
-        const uint32_t row = min(n0 + r, p.N - 1u);
+        const uint32_t row = min(n0 + (PAIR ? 128u * rank : 0u) + r, p.N - 1u);
         const uint8_t* qrow = p.qs + (size_t)row * p.nb * QS_BYTES + hh * 8;
         const uint8_t* srow = p.sc + (size_t)row * p.nb * SC_BYTES;
         // this thread's 16-byte chunks of a stage: row r of the SW128 tile, chunk (hh*4 + t) ^ (r%8)
@@ -418,7 +570,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
                 dbits = dnext;
                 dnext = ld_d((kt >> 2) + 1);
             }
-            if (i >= G_STAGES) {
+            if (i >= (uint32_t)S) {
                 // a wait that runs out (only a broken pipeline) stops this warp; the MMA thread
                 // then runs out of its own waits and stops too
                 bool go = true;
@@ -429,16 +581,22 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
                     break;
                 }
             }
-            if (live) {
-                const float d = half_bits_to_float(dbits);
-                const uint32_t dst = brow + s * G_STAGE_BYTES;
+            const float d = half_bits_to_float(dbits);
+            const uint32_t dst = brow + s * SB;
+            if (PAIR) {
+                if (kt < kt_full) decode_half<false>(q, d, sel_l, dst, ghalf, 0, p.K);
+                else decode_half<true>(q, d, sel_l, dst, ghalf, kt * G_BK + hh * 32, p.K);
+            } else if (live) {
                 if (kt < kt_full) decode_sub<false>(q, d, sel_l, dst, 0, p.K);
                 else decode_sub<true>(q, d, sel_l, dst, kt * G_BK + hh * 32, p.K);
             }
             fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
             __syncwarp();
-            if (lane == 0 && i + 1 != p.stall) mbar_arrive(full_b(s));
-            if (++s == G_STAGES) {
+            if (lane == 0 && i + 1 != p.stall) {
+                if (PAIR) mbar_arrive_cluster(full_b_lead0 + 8u * s);  // (the even CTA's barrier)
+                else mbar_arrive(full_b(s));
+            }
+            if (++s == (uint32_t)S) {
                 s = 0;
                 ph ^= 1u;
             }
@@ -518,10 +676,10 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
 
     tc_fence_before();
     __syncthreads();
-    if (warp == G_MMA_WARP) {
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G_TMEM_COLS)
-                     : "memory");
-    }
+    // PAIR: neither CTA frees its TMEM (a pair allocation) or leaves while the other may still
+    // arrive on its barriers or have MMAs reading its shared memory
+    if (PAIR) cluster_barrier();
+    if (warp == G_MMA_WARP) tmem_dealloc<PAIR>(tmem, G_TMEM_COLS);
 }
 
 // x (f32 / f16) -> bf16, row-major [M, K] (round to nearest even).
@@ -534,17 +692,20 @@ __global__ void __launch_bounds__(256) to_bf16_kernel(const XT* __restrict__ x, 
 
 // The split tiles' outputs: out = the sum of each tile's K ranges, in range order (deterministic).
 // One thread per 4 columns of a partial tile row.
+// R: split tiles (PAIR: split pair tiles, 2R partial tiles, tile i = pair i / 2, rank i % 2).
 __global__ void __launch_bounds__(256) splitk_tile_sum_kernel(const float* __restrict__ part, float* __restrict__ out,
                                                               uint32_t M, uint32_t N, uint32_t nt, uint32_t full,
-                                                              uint32_t R, uint32_t s, uint32_t BN, uint32_t PR) {
+                                                              uint32_t R, uint32_t s, uint32_t BN, uint32_t PR,
+                                                              uint32_t pair) {
     const uint32_t q = BN / 4;  // column quads per row
-    const size_t total = (size_t)R * PR * q;
+    const size_t total = (size_t)(pair ? 2 * R : R) * PR * q;
     for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
         const uint32_t i = (uint32_t)(e / ((size_t)PR * q));
         const uint32_t rem = (uint32_t)(e % ((size_t)PR * q));
         const uint32_t row = rem / q, c4 = (rem % q) * 4;
-        const uint32_t t = full + i;
-        const uint32_t token = (t / nt) * G_BM + row, n = (t % nt) * BN + c4;
+        const uint32_t t = full + (pair ? i >> 1 : i);
+        const uint32_t mtile = pair ? 2 * (t / nt) + (i & 1u) : t / nt;
+        const uint32_t token = mtile * G_BM + row, n = (t % nt) * BN + c4;
         if (token >= M || n >= N) continue;
         const float4* src = reinterpret_cast<const float4*>(part + (((size_t)i * s) * PR + row) * BN + c4);
         float4 a = src[0];
@@ -583,6 +744,7 @@ EncodeTiledFn encode_fn() {
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 struct GemmPlan {
+    bool pair;            // 2-CTA clusters sharing each weight tile (units and R count pairs)
     uint32_t bn;          // weight rows per tile: 256 or 224
     uint32_t nt, tiles;   // tiles along N, all tiles
     uint32_t full, R, s;  // whole tiles; the split ones after them, and their K ranges
@@ -600,6 +762,28 @@ struct GemmPlan {
 GemmPlan gemm_plan(uint32_t m, uint32_t n, uint32_t k, int num_sms) {
     const uint64_t sms = num_sms > 0 ? (uint64_t)num_sms : 148u;
     const uint64_t mt = (m + G_BM - 1) / G_BM, nb = (k + QK - 1) / QK;
+    if (mt >= 2 && g_pair_enabled) {
+        // two token tiles per weight tile, one decode for both: units are pair tiles, a wave is
+        // sms / 2 of them; the split of the last wave as below
+        GemmPlan pl{};
+        pl.pair = true;
+        pl.bn = G_BN;
+        pl.nt = (n + G_BN - 1) / G_BN;
+        pl.tiles = (uint32_t)(pl.nt * ((mt + 1) / 2));
+        pl.PR = G_BM;
+        const uint64_t slots = std::max<uint64_t>(1, sms / 2), T = pl.tiles;
+        uint64_t R = T <= slots ? T : T - ((T + slots - 1) / slots - 1) * slots;
+        if (R == slots) R = 0;
+        uint64_t sp = R ? std::max<uint64_t>(1, std::min<uint64_t>(slots / R, nb / 2)) : 1;
+        if (sp <= 1) {
+            R = 0;
+            sp = 1;
+        }
+        pl.R = (uint32_t)R;
+        pl.s = (uint32_t)sp;
+        pl.full = (uint32_t)(T - R);
+        return pl;
+    }
     GemmPlan best{};
     double best_cost = 1e300;
     for (uint32_t bn : {(uint32_t)G_BN, 224u}) {
@@ -688,7 +872,7 @@ size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype, int 
     size_t ws = 256;  // (reserved)
     if (x_dtype != kDtypeBf16) ws += align256((size_t)m * k * 2);  // bf16 copy of x
     const GemmPlan pl = gemm_plan(m, n, k, num_sms);
-    if (pl.R) ws += align256((size_t)pl.R * pl.s * pl.PR * pl.bn * sizeof(float));  // partial tiles
+    if (pl.R) ws += align256((size_t)(pl.pair ? 2 : 1) * pl.R * pl.s * pl.PR * pl.bn * sizeof(float));  // partial tiles
     return ws;
 }
 
@@ -724,9 +908,11 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+        e = cudaFuncSetAttribute(gemm_kernel<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gemm_kernel<224>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+            e = cudaFuncSetAttribute(gemm_kernel<224, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set[dev] = true;
     }
@@ -763,17 +949,38 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     std::memset(&omap, 0, sizeof(omap));
     std::memset(&pmap, 0, sizeof(pmap));
     bool tma = p.vec && encode_out(&omap, out, n, m, 1);
-    if (tma && pl.R) tma = encode_out(&pmap, p.part, pl.bn, pl.PR, (cuuint64_t)pl.R * pl.s);
+    const uint32_t ptiles = (pl.pair ? 2u : 1u) * pl.R;  // partial tiles (each split s ways)
+    if (tma && pl.R) tma = encode_out(&pmap, p.part, pl.bn, pl.PR, (cuuint64_t)ptiles * pl.s);
     p.tma = tma ? 1u : 0u;
     const unsigned units = pl.full + pl.R * pl.s;
-    if (pl.bn == 224) gemm_kernel<224><<<units, G_THREADS, G_SMEM, stream>>>(map, omap, pmap, p);
-    else gemm_kernel<256><<<units, G_THREADS, G_SMEM, stream>>>(map, omap, pmap, p);
+    if (pl.pair) {
+        // one 2-CTA cluster per unit
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * units);
+        cfg.blockDim = dim3(G_THREADS);
+        cfg.dynamicSmemBytes = G_SMEM;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, gemm_kernel<256, true>, map, omap, pmap, p);
+        if (e != cudaSuccess) return e;
+    } else if (pl.bn == 224) {
+        gemm_kernel<224, false><<<units, G_THREADS, G_SMEM, stream>>>(map, omap, pmap, p);
+    } else {
+        gemm_kernel<256, false><<<units, G_THREADS, G_SMEM, stream>>>(map, omap, pmap, p);
+    }
     e = cudaGetLastError();
     if (e != cudaSuccess || pl.R == 0) return e;
-    const size_t quads = (size_t)pl.R * pl.PR * (pl.bn / 4);
+    const size_t quads = (size_t)ptiles * pl.PR * (pl.bn / 4);
     const int sms = num_sms > 0 ? num_sms : 148;
     const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((quads + 255) / 256, (size_t)sms * 8));
-    splitk_tile_sum_kernel<<<blocks, 256, 0, stream>>>(p.part, out, m, n, pl.nt, pl.full, pl.R, pl.s, pl.bn, pl.PR);
+    splitk_tile_sum_kernel<<<blocks, 256, 0, stream>>>(p.part, out, m, n, pl.nt, pl.full, pl.R, pl.s, pl.bn, pl.PR,
+                                                       pl.pair ? 1u : 0u);
     return cudaGetLastError();
 }
 
