@@ -154,8 +154,19 @@ int matmul_impl(const char* op, const void* x, int x_dtype, uint32_t m, const ui
         return fail(IQ2_ERR_INVALID_ARGUMENT, "%s: x/out not aligned to their element size", op);
     const int sms = num_sms_for_current_device();
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (variant != IQ2_VARIANT_IQ2_XXS) {  // the other formats: one generic kernel, no workspace
-        e = iq2::launch_variant_matmul(variant, x, x_dtype, m, weight_bytes, weight_scales, out_dim, in_dim, out, sms, s);
+    if (variant != IQ2_VARIANT_IQ2_XXS) {
+        // the other formats: the tensor-core GEMM for m > kGemvMaxM when the caller gives the
+        // workspace iq2_matmul_workspace_size asks for; else the f32 CUDA-core kernel (no workspace)
+        const bool gemm = m > iq2::kGemvMaxM &&
+                          iq2::gemm_path_ok(m, out_dim, in_dim, x, x_dtype, weight_bytes, weight_scales, out) &&
+                          workspace != nullptr &&
+                          workspace_bytes >= iq2::gemm_workspace_size(m, out_dim, in_dim, x_dtype, sms);
+        if (gemm)
+            e = iq2::launch_gemm(x, x_dtype, m, weight_bytes, weight_scales, out_dim, in_dim, out, workspace, sms, s,
+                                 variant);
+        else
+            e = iq2::launch_variant_matmul(variant, x, x_dtype, m, weight_bytes, weight_scales, out_dim, in_dim, out,
+                                           sms, s);
     } else if (m <= iq2::kGemvMaxM) {
         if (iq2::gemv_fast_path_ok(m, in_dim, weight_bytes, weight_scales)) {
             const size_t need = iq2::gemv_workspace_size(m, out_dim, in_dim, sms);
@@ -321,7 +332,8 @@ int iq2_testing_set_gemm_stall(uint64_t wait_limit_ns, uint32_t stall_stage) {
 
 size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, int x_dtype,
                                  int variant) {
-    if (variant != IQ2_VARIANT_IQ2_XXS) return 0;
+    if (variant < IQ2_VARIANT_IQ2_XXS || variant > IQ2_VARIANT_IQ3_S) return 0;
+    if (variant != IQ2_VARIANT_IQ2_XXS && m <= iq2::kGemvMaxM) return 0;  // (their decode kernel needs none)
     return workspace_for(m, out_dim, in_dim, x_dtype, num_sms_for_current_device());
 }
 
@@ -399,10 +411,10 @@ size_t iq2_matmul_with_activation_quant_workspace_size(uint32_t m, uint32_t out_
                                                       int x_dtype, int variant, int act_mode) {
     if (act_mode != IQ2_ACT_QUANT_W8A8) return iq2_matmul_workspace_size(m, out_dim, in_dim, x_dtype, variant);
     if (m == 0 || out_dim == 0 || in_dim == 0 || variant < IQ2_VARIANT_IQ2_XXS || variant > IQ2_VARIANT_IQ3_S) return 0;
+    // (the other formats: their GEMM's workspace after the int8-rounded x, which selects the
+    // tensor-core path for m > kGemvMaxM; the call itself only requires the x part)
     const size_t qdq = ((size_t)m * in_dim * sizeof(float) + 255) / 256 * 256 +
-                       (variant == IQ2_VARIANT_IQ2_XXS
-                            ? workspace_for(m, out_dim, in_dim, IQ2_DTYPE_F32, num_sms_for_current_device())
-                            : 0);
+                       iq2_matmul_workspace_size(m, out_dim, in_dim, IQ2_DTYPE_F32, variant);
     // the decode path (int8 activations into the GEMV) needs less; the larger of the two is asked
     // for so that either path can run with it
     const size_t gemv = (variant == IQ2_VARIANT_IQ2_XXS && m <= iq2::kGemvW8A8MaxM)

@@ -56,6 +56,13 @@ __device__ __forceinline__ uint2 ld_shared_v2_const(uint32_t addr) {
     return v;
 }
 
+// ld_shared_v4_const: 16 bytes of such a read-only table.
+__device__ __forceinline__ uint4 ld_shared_v4_const(uint32_t addr) {
+    uint4 v;
+    asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
 // ld_shared_v4: 16 bytes at addr + OFF, kept in program order with the other volatile asm
 // (the cp.async waits that make the data valid).
 template <int OFF>

@@ -31,6 +31,7 @@
 // No TMA multicast is used anywhere (this library also runs on multi-GPU jobs).
 #include "iq2xxs_common.cuh"
 #include "iq2xxs_codebook.h"
+#include "iq2_variant_grids.h"
 #include "iq2xxs_internal.h"
 
 #include <cuda.h>
@@ -38,6 +39,7 @@
 #include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 namespace iq2 {
 
@@ -357,6 +359,149 @@ __device__ __forceinline__ void decode_half(uint2 q, float d, uint32_t sel_l, ui
     }
 }
 
+// ---- the other formats (IQ2_XS, IQ2_S, IQ3_S) ----
+// Split-layout geometry per 256-weight block (weight bytes QB, scale bytes SB; reference
+// src/iq2_matmul.rs:15-29) and the decode table: E entries of ENT bytes, C interleaved copies
+// (E * ENT * C = the table's 32 KB), copy `lane % C` for each lane.
+template <int V>
+struct GFmt {
+    static constexpr uint32_t QB = V == 2 ? 72u : (V == 3 ? 104u : 64u);
+    static constexpr uint32_t SB = V == 0 ? 2u : (V == 3 ? 6u : 10u);
+    static constexpr uint32_t ENT = V == 3 ? 16u : 8u;
+    static constexpr uint32_t E = V == 0 ? 256u : (V == 2 ? 1024u : 512u);
+    static constexpr uint32_t C = (uint32_t)G_SEL_BYTES / (E * ENT);
+    static_assert(C >= 1 && (C & (C - 1)) == 0, "copies");
+};
+
+// Table entry of a {8, 25, 43} grid word (IQ2_XS, IQ2_S): per pair p of weights (2p, 2p+1) the
+// 16-bit prmt selector picking bf16(g * dl) out of {qlo, qhi} (magnitude code c: bytes 2c, 2c+1),
+// the same layout as IQ2XXS_BF16_SEL.
+__device__ __forceinline__ uint2 sel_from_grid8(uint64_t g) {
+    uint32_t w[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const uint32_t b0 = (uint32_t)(g >> (16 * p)) & 0xFFu, b1 = (uint32_t)(g >> (16 * p + 8)) & 0xFFu;
+        const uint32_t c0 = b0 == 8u ? 0u : (b0 == 25u ? 1u : 2u), c1 = b1 == 8u ? 0u : (b1 == 25u ? 1u : 2u);
+        w[p] = (2u * c0) | ((2u * c0 + 1u) << 4) | ((2u * c1) << 8) | ((2u * c1 + 1u) << 12);
+    }
+    return make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
+}
+
+// IQ3_S table entry of a grid word (four magnitudes v in {1, 3, ..., 15}, code k = (v - 1) / 2):
+// x = the prmt selectors of pairs (0,1) and (2,3) into {c0, c1} or {c2, c3} (code k & 3: bytes
+// 2(k & 3), 2(k & 3) + 1), y / z = the halves of pairs (0,1) / (2,3) that take the high set (k >= 4).
+__device__ __forceinline__ uint4 sel_from_grid3s(uint32_t g) {
+    uint32_t sel = 0, m[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t k = ((g >> (8 * j)) & 0xFFu) >> 1, kk = k & 3u;
+        sel |= ((2u * kk) | ((2u * kk + 1u) << 4)) << (8 * j);
+        if (k >= 4u) m[j >> 1] |= 0xFFFFu << (16 * (j & 1));
+    }
+    return make_uint4(sel, m[0], m[1], 0u);
+}
+
+// The raw bytes of one 32-weight sub-block ib of one row (qblk / sblk: the row's block), loaded
+// two stages ahead of their decode:
+//   IQ2_XS: x, y = the four u16 words (9-bit grid index | 7-bit sign index << 9); w = scale byte
+//   IQ2_S:  x = the four grid low bytes, y = the four sign bytes; w = qh byte | scale byte << 8
+//   IQ3_S:  x, y = the eight grid low bytes (two per 8 weights), z = the four sign bytes;
+//           w = qh byte | this sub-block's scale nibble << 8
+template <int V>
+__device__ __forceinline__ uint4 ld_raw(const uint8_t* qblk, const uint8_t* sblk, uint32_t ib) {
+    if (V == 1) {
+        const uint2 q = __ldg(reinterpret_cast<const uint2*>(qblk + ib * 8));
+        return make_uint4(q.x, q.y, 0u, (uint32_t)__ldg(sblk + 2 + ib));
+    } else if (V == 2) {
+        const uint32_t lo = __ldg(reinterpret_cast<const uint32_t*>(qblk + ib * 4));
+        const uint32_t sg = __ldg(reinterpret_cast<const uint32_t*>(qblk + 32 + ib * 4));
+        return make_uint4(lo, sg, 0u, (uint32_t)__ldg(qblk + 64 + ib) | ((uint32_t)__ldg(sblk + 2 + ib) << 8));
+    } else {
+        const uint2 lo = __ldg(reinterpret_cast<const uint2*>(qblk + ib * 8));
+        const uint32_t sg = __ldg(reinterpret_cast<const uint32_t*>(qblk + 72 + ib * 4));
+        const uint32_t nib = ((uint32_t)__ldg(sblk + 2 + ib / 2) >> (4 * (ib & 1))) & 15u;
+        return make_uint4(lo.x, lo.y, sg, (uint32_t)__ldg(qblk + 64 + ib) | (nib << 8));
+    }
+}
+
+// Groups t0 .. t0 + NG - 1 (8 weights each) of a sub-block of format V to bf16, stored as 16-byte
+// chunks at dst ^ (t << 4) like decode_sub. Each weight is bf16 of its exact value dl * g * sign
+// (dl * g has at most 22 significant bits): the candidate products are rounded once and `prmt`
+// picks them by grid code; an XOR applies the signs. TAIL: zero the weights at k >= K.
+template <int V, int NG, bool TAIL>
+__device__ __forceinline__ void decode_v(uint4 raw, float d, uint32_t sel_l, uint32_t dst, uint32_t t0,
+                                         uint32_t k_lo, uint32_t K) {
+    constexpr uint32_t STRIDE = GFmt<V>::C * GFmt<V>::ENT;  // bytes between table entries
+    uint32_t ca = 0, cb = 0, cc = 0, cdd = 0;  // the rounded candidates (IQ3_S: all four; else qlo, qhi)
+    uint32_t cur_nib = 0xFFFFFFFFu;
+#pragma unroll
+    for (int tt = 0; tt < NG; ++tt) {
+        const uint32_t t = t0 + tt;
+        uint32_t S;  // the 8 sign bits of the group (bit j: weight j negative)
+        uint4 w;
+        if (V == 3) {
+            if (tt == 0) {
+                const float dl = d * (float)(1u + 2u * (raw.w >> 8));  // d(1+2s), exact
+                ca = cvt_bf16x2(dl * 1.0f, dl * 3.0f);
+                cb = cvt_bf16x2(dl * 5.0f, dl * 7.0f);
+                cc = cvt_bf16x2(dl * 9.0f, dl * 11.0f);
+                cdd = cvt_bf16x2(dl * 13.0f, dl * 15.0f);
+            }
+            const uint32_t lo = ((t < 2 ? raw.x : raw.y) >> (16 * (t & 1))) & 0xFFFFu;
+            const uint32_t i1 = (lo & 0xFFu) | (((raw.w >> (2 * t)) & 1u) << 8);
+            const uint32_t i2 = (lo >> 8) | (((raw.w >> (2 * t + 1)) & 1u) << 8);
+            const uint4 e1 = ld_shared_v4_const(sel_l + i1 * STRIDE);
+            const uint4 e2 = ld_shared_v4_const(sel_l + i2 * STRIDE);
+            S = (raw.z >> (8 * t)) & 0xFFu;
+            auto pick = [&](uint32_t sel, uint32_t m) {
+                const uint32_t a = prmt(ca, cb, sel), b = prmt(cc, cdd, sel);
+                return (a & ~m) | (b & m);
+            };
+            w.x = pick(e1.x, e1.y);
+            w.y = pick(e1.x >> 16, e1.z);
+            w.z = pick(e2.x, e2.y);
+            w.w = pick(e2.x >> 16, e2.z);
+        } else {
+            uint32_t gi, nib;
+            if (V == 1) {
+                const uint32_t word = ((t < 2 ? raw.x : raw.y) >> (16 * (t & 1))) & 0xFFFFu;
+                gi = word & 0x1FFu;
+                const uint32_t si = word >> 9;
+                S = si | ((__popc(si) & 1u) << 7);  // ksigns: the 8th sign makes the parity even
+                nib = (raw.w >> (4 * (t >> 1))) & 15u;
+            } else {
+                gi = ((raw.x >> (8 * t)) & 0xFFu) | (((raw.w >> (2 * t)) & 3u) << 8);
+                S = (raw.y >> (8 * t)) & 0xFFu;
+                nib = (raw.w >> (8 + 4 * (t >> 1))) & 15u;
+            }
+            if (nib != cur_nib) {  // (uniform per pair of groups: the scale nibble covers 16 weights)
+                cur_nib = nib;
+                const float dl = d * (float)(2u * nib + 1u) * 0.125f;  // d(0.5+s)/4, exact
+                ca = cvt_bf16x2(dl * 8.0f, dl * 25.0f);
+                cb = cvt_bf16x2(dl * 43.0f, 0.0f);
+            }
+            const uint2 sel = ld_shared_v2_const(sel_l + gi * STRIDE);
+            w.x = prmt(ca, cb, sel.x);
+            w.y = prmt(ca, cb, sel.x >> 16);
+            w.z = prmt(ca, cb, sel.y);
+            w.w = prmt(ca, cb, sel.y >> 16);
+        }
+        w.x ^= (S * 0x40008000u) & 0x80008000u;
+        w.y ^= (S * 0x10002000u) & 0x80008000u;
+        w.z ^= (S * 0x04000800u) & 0x80008000u;
+        w.w ^= (S * 0x01000200u) & 0x80008000u;
+        if (TAIL && k_lo + t * 8 + 8 > K) {
+            const uint32_t k0 = k_lo + t * 8;
+            const uint32_t keep = k0 >= K ? 0u : K - k0;
+            w.x = keep >= 2 ? w.x : (keep == 1 ? (w.x & 0xFFFFu) : 0u);
+            w.y = keep >= 4 ? w.y : (keep == 3 ? (w.y & 0xFFFFu) : 0u);
+            w.z = keep >= 6 ? w.z : (keep == 5 ? (w.z & 0xFFFFu) : 0u);
+            w.w = keep >= 8 ? w.w : (keep == 7 ? (w.w & 0xFFFFu) : 0u);
+        }
+        st_shared_v4(dst ^ (t << 4), w);
+    }
+}
+
 // ---- the kernel ----
 // BN: weight rows per CTA (256, or 224 where that fills the last wave better); the stage
 // layout is always sized for 256 rows.
@@ -370,7 +515,9 @@ __device__ __forceinline__ void decode_half(uint2 q, float d, uint32_t sel_l, ui
 // has landed (each CTA's x loads complete on its own `full_a`, so that an aborted CTA can still
 // wait for its own loads). The even CTA's commits arrive on both CTAs' `empty` and `acc_full`. No
 // TMA multicast.
-template <int BN, bool PAIR>
+// V: the weight format (0 IQ2_XXS, 1 IQ2_XS, 2 IQ2_S, 3 IQ3_S); only the decode table and the
+// decode differ.
+template <int BN, bool PAIR, int V = 0>
 __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                             const __grid_constant__ CUtensorMap tmap_out,
                                                             const __grid_constant__ CUtensorMap tmap_part,
@@ -427,10 +574,17 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
     const bool upper_mma = (PAIR ? m0 - rank * G_BM : m0) + 128 < p.M;
 
     // decode table -> shared memory: per grid entry the four 16-bit prmt selectors packed in two
-    // words, G_SEL_COPIES times (copy c of entry e at (e * G_SEL_COPIES + c) * 8)
-    for (int i = threadIdx.x; i < 256 * G_SEL_COPIES; i += blockDim.x) {
-        const uint32_t* e = IQ2XXS_BF16_SEL[i / G_SEL_COPIES];
-        reinterpret_cast<uint2*>(base + (sel_s - base_s))[i] = make_uint2(e[0] | (e[1] << 16), e[2] | (e[3] << 16));
+    // words (IQ3_S: GFmt<3>'s 16-byte entries), C times (copy c of entry e at (e * C + c) * ENT)
+    for (int i = threadIdx.x; i < (int)(GFmt<V>::E * GFmt<V>::C); i += blockDim.x) {
+        const uint32_t e = (uint32_t)i / GFmt<V>::C;
+        if constexpr (V == 0) {
+            const uint32_t* w = IQ2XXS_BF16_SEL[e];
+            reinterpret_cast<uint2*>(base + (sel_s - base_s))[i] = make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
+        } else if constexpr (V == 3) {
+            reinterpret_cast<uint4*>(base + (sel_s - base_s))[i] = sel_from_grid3s(IQ3S_GRID[e]);
+        } else {
+            reinterpret_cast<uint2*>(base + (sel_s - base_s))[i] = sel_from_grid8(V == 1 ? IQ2XS_GRID[e] : IQ2S_GRID[e]);
+        }
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -541,29 +695,35 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
         const uint32_t ghalf = (threadIdx.x >> 7) & 1u;  // (PAIR only)
         const bool live = (r & ~31u) < (uint32_t)BN;  // warp-uniform: BN is a multiple of 32
         const uint32_t row = min(n0 + (PAIR ? 128u * rank : 0u) + r, p.N - 1u);
-        const uint8_t* qrow = p.qs + (size_t)row * p.nb * QS_BYTES + hh * 8;
-        const uint8_t* srow = p.sc + (size_t)row * p.nb * SC_BYTES;
+        // (IQ2_XXS: the row's sub-block hh of each stage; the others: the row's first block)
+        const uint8_t* qrow = p.qs + (size_t)row * p.nb * GFmt<V>::QB + (V == 0 ? hh * 8 : 0u);
+        const uint8_t* srow = p.sc + (size_t)row * p.nb * GFmt<V>::SB;
         // this thread's 16-byte chunks of a stage: row r of the SW128 tile, chunk (hh*4 + t) ^ (r%8)
         const uint32_t brow = base_s + G_A_BYTES + (r >> 3) * 1024u + (r & 7u) * 128u +
                               ((((hh * 4u) ^ (r & 7u))) << 4);
         const uint32_t kt_full = p.K / G_BK;  // stages below this one have no K tail
-        const uint32_t sel_l = sel_s + (lane & (G_SEL_COPIES - 1)) * 8u;  // this lane's table copy
+        const uint32_t sel_l = sel_s + (lane & (GFmt<V>::C - 1)) * GFmt<V>::ENT;  // this lane's table copy
         // loads run ahead of the decode (the sub-block two stages on, the block scale one block
         // on), clamped to this CTA's last stage and block
         const uint32_t kt_last = kt0 + NKT - 1u, b_last = b1 - 1u;
-        auto ld_q = [&](uint32_t kt) {
-            return __ldg(reinterpret_cast<const uint2*>(qrow + (size_t)min(kt, kt_last) * 16));
+        using Raw = typename std::conditional<V == 0, uint2, uint4>::type;
+        auto ld_q = [&](uint32_t kt) -> Raw {
+            const uint32_t kc = min(kt, kt_last);
+            if constexpr (V == 0) return __ldg(reinterpret_cast<const uint2*>(qrow + (size_t)kc * 16));
+            else
+                return ld_raw<V>(qrow + (size_t)(kc >> 2) * GFmt<V>::QB, srow + (size_t)(kc >> 2) * GFmt<V>::SB,
+                                 (kc & 3u) * 2u + hh);
         };
         auto ld_d = [&](uint32_t blk) {
-            const uint8_t* e = srow + (size_t)min(blk, b_last) * 2;
+            const uint8_t* e = srow + (size_t)min(blk, b_last) * GFmt<V>::SB;
             return (uint32_t)e[0] | ((uint32_t)e[1] << 8);
         };
-        uint2 q1 = ld_q(kt0), q2 = ld_q(kt0 + 1);
+        Raw q1 = ld_q(kt0), q2 = ld_q(kt0 + 1);
         uint32_t dbits = ld_d(b0), dnext = ld_d(b0 + 1);
         uint32_t s = 0, ph = 0;  // stage slot and the parity of its current use
         for (uint32_t i = 0; i < NKT; ++i) {
             const uint32_t kt = kt0 + i;
-            const uint2 q = q1;
+            const Raw q = q1;
             q1 = q2;
             q2 = ld_q(kt + 2);
             if ((kt & 3) == 0 && i > 0) {
@@ -583,7 +743,14 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
             }
             const float d = half_bits_to_float(dbits);
             const uint32_t dst = brow + s * SB;
-            if (PAIR) {
+            if constexpr (V != 0) {
+                constexpr int NG = PAIR ? 2 : 4;  // groups per thread
+                const uint32_t t0 = PAIR ? 2u * ghalf : 0u;
+                if (PAIR || live) {
+                    if (kt < kt_full) decode_v<V, NG, false>(q, d, sel_l, dst, t0, 0, p.K);
+                    else decode_v<V, NG, true>(q, d, sel_l, dst, t0, kt * G_BK + hh * 32, p.K);
+                }
+            } else if (PAIR) {
                 if (kt < kt_full) decode_half<false>(q, d, sel_l, dst, ghalf, 0, p.K);
                 else decode_half<true>(q, d, sel_l, dst, ghalf, kt * G_BK + hh * 32, p.K);
             } else if (live) {
@@ -876,8 +1043,46 @@ size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype, int 
     return ws;
 }
 
+namespace {
+// The three launch forms of format V: paired (one 2-CTA cluster per unit), or one CTA per unit
+// with 256- or 224-row tiles.
+template <int V>
+cudaError_t set_attributes_v() {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<256, false, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_kernel<224, false, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_kernel<256, true, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+    return e;
+}
+
+template <int V>
+cudaError_t launch_forms(const GemmPlan& pl, unsigned units, const CUtensorMap& map, const CUtensorMap& omap,
+                         const CUtensorMap& pmap, const GemmParams& p, cudaStream_t stream) {
+    if (pl.pair) {
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * units);
+        cfg.blockDim = dim3(G_THREADS);
+        cfg.dynamicSmemBytes = G_SMEM;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, gemm_kernel<256, true, V>, map, omap, pmap, p);
+    }
+    if (pl.bn == 224) gemm_kernel<224, false, V><<<units, G_THREADS, G_SMEM, stream>>>(map, omap, pmap, p);
+    else gemm_kernel<256, false, V><<<units, G_THREADS, G_SMEM, stream>>>(map, omap, pmap, p);
+    return cudaGetLastError();
+}
+}  // namespace
+
 cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc, uint32_t n,
-                        uint32_t k, float* out, void* workspace, int num_sms, cudaStream_t stream) {
+                        uint32_t k, float* out, void* workspace, int num_sms, cudaStream_t stream, int variant) {
+    if (variant < 0 || variant > 3) return cudaErrorInvalidValue;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     unsigned int* err = nullptr;
     cudaError_t e = status_word_for_current_device(&err);
@@ -908,11 +1113,10 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemm_kernel<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gemm_kernel<224, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gemm_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+        e = set_attributes_v<0>();
+        if (e == cudaSuccess) e = set_attributes_v<1>();
+        if (e == cudaSuccess) e = set_attributes_v<2>();
+        if (e == cudaSuccess) e = set_attributes_v<3>();
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set[dev] = true;
     }
@@ -953,28 +1157,13 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     if (tma && pl.R) tma = encode_out(&pmap, p.part, pl.bn, pl.PR, (cuuint64_t)ptiles * pl.s);
     p.tma = tma ? 1u : 0u;
     const unsigned units = pl.full + pl.R * pl.s;
-    if (pl.pair) {
-        // one 2-CTA cluster per unit
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(2 * units);
-        cfg.blockDim = dim3(G_THREADS);
-        cfg.dynamicSmemBytes = G_SMEM;
-        cfg.stream = stream;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, gemm_kernel<256, true>, map, omap, pmap, p);
-        if (e != cudaSuccess) return e;
-    } else if (pl.bn == 224) {
-        gemm_kernel<224, false><<<units, G_THREADS, G_SMEM, stream>>>(map, omap, pmap, p);
-    } else {
-        gemm_kernel<256, false><<<units, G_THREADS, G_SMEM, stream>>>(map, omap, pmap, p);
+    switch (variant) {
+        case 0: e = launch_forms<0>(pl, units, map, omap, pmap, p, stream); break;
+        case 1: e = launch_forms<1>(pl, units, map, omap, pmap, p, stream); break;
+        case 2: e = launch_forms<2>(pl, units, map, omap, pmap, p, stream); break;
+        default: e = launch_forms<3>(pl, units, map, omap, pmap, p, stream); break;
     }
-    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess || pl.R == 0) return e;
     const size_t quads = (size_t)ptiles * pl.PR * (pl.bn / 4);
     const int sms = num_sms > 0 ? num_sms : 148;

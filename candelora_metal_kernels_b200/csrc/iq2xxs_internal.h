@@ -71,13 +71,14 @@ cudaError_t launch_gemv_generic(const void* x, int x_dtype, uint32_t m, const ui
                                 const uint8_t* sc, uint32_t n, uint32_t k, float* out,
                                 int num_sms, cudaStream_t stream);
 
-// Tensor-core GEMM (iq2xxs_gemm.cu), m > 16.
+// Tensor-core GEMM (iq2xxs_gemm.cu), m > 16. variant: the weight format (IQ2_VARIANT_*: 0
+// IQ2_XXS, 1 IQ2_XS, 2 IQ2_S, 3 IQ3_S; the workspace size does not depend on it).
 bool gemm_path_ok(uint32_t m, uint32_t n, uint32_t k, const void* x, int x_dtype, const uint8_t* qs,
                   const uint8_t* sc, const float* out);
 size_t gemm_workspace_size(uint32_t m, uint32_t n, uint32_t k, int x_dtype, int num_sms);
 cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
                         uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,
-                        cudaStream_t stream);
+                        cudaStream_t stream, int variant = 0);
 
 // The prefill GEMM's per-device sticky status (iq2xxs_gemm.cu): synchronises the current device,
 // stores the status bits in *status and clears them; returns a cudaError_t.

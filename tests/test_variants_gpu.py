@@ -101,3 +101,61 @@ def test_variant_w8a8(oracle, variant):
                                            n, k, var, cfg).cpu().numpy()
     ref = oracle.matmul(oracle.rowwise_qdq_w8a8(x.numpy()), wb, ws, n, k, variant=variant)
     assert rel_l2(y, ref) <= 1e-4
+
+
+# ---- m > 32: the tcgen05 GEMM (weights decoded to bf16 in shared memory), selected when the call
+# ---- has the workspace iq2_matmul_workspace_size asks for
+GEMM_FP32_TOL = 1e-4    # against a plain fp32 matmul of the same bf16 operands
+GEMM_ORACLE_TOL = 2e-2  # against the oracle (the GEMM rounds x and the weights to bf16)
+
+
+def _cuda_core(x, wb, ws, n, k, var):
+    """The CUDA-core kernel: the C call with no workspace (the path a caller without one gets)."""
+    import ctypes
+    from candelora_metal_kernels_b200 import _lib
+    lib = _lib.load()
+    out = torch.empty(x.shape[0], n, dtype=torch.float32, device="cuda")
+    dt = {torch.float32: _lib.DTYPE_F32, torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16}[x.dtype]
+    rc = lib.iq2_matmul(ctypes.c_void_p(x.data_ptr()), dt, x.shape[0], ctypes.c_void_p(wb.data_ptr()), wb.numel(),
+                        ctypes.c_void_p(ws.data_ptr()), ws.numel(), n, k, int(var), ctypes.c_void_p(out.data_ptr()),
+                        None, 0, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _lib.check(rc)
+    return out
+
+
+@pytest.mark.parametrize("variant", list(VARIANTS))
+@pytest.mark.parametrize("m,n,k,xdt", [
+    (33, 72, 1000, torch.float32),     # one 256-token tile, ragged K, a part-filled weight tile
+    (300, 520, 4096, torch.bfloat16),  # paired CTAs, the odd one part-filled
+    (600, 256, 2304, torch.float16),   # two pairs, the last pair's odd CTA without tokens
+    (2048, 1024, 4096, torch.bfloat16),  # every pair tile split over K (fewer tiles than SMs)
+])
+def test_variant_gemm(oracle, variant, m, n, k, xdt):
+    var = VARIANTS[variant][0]
+    wb, ws = _blocks(variant, n, k, seed=m + n)
+    assert c.workspace_bytes(m, n, k, xdt, var) > 0  # (the size query routes these to the GEMM)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(m)).to(xdt).cuda()
+    wbd, wsd = torch.from_numpy(wb).cuda(), torch.from_numpy(ws).cuda()
+    y = c.iq2_matmul(x, wbd, wsd, n, k, var)
+    assert bool(torch.isfinite(y).all())
+    w = c.iq2_dequantize(wbd, wsd, n, k, var, dtype=torch.bfloat16).float()
+    exact = x.to(torch.bfloat16).float() @ w.T
+    assert rel_l2(y.double().cpu().numpy(), exact.double().cpu().numpy()) <= GEMM_FP32_TOL
+    cols = np.unique(np.concatenate([np.arange(4), np.random.default_rng(n).integers(0, n, 24), [n - 1]]))
+    ref = oracle.matmul(x.float().cpu().numpy(), wb, ws, n, k, cols=cols, variant=variant)
+    assert rel_l2(y.cpu().numpy()[:, cols], ref) <= GEMM_ORACLE_TOL
+    assert rel_l2(y.cpu().numpy(), _cuda_core(x, wbd, wsd, n, k, var).cpu().numpy()) <= GEMM_ORACLE_TOL
+
+
+@pytest.mark.parametrize("variant", list(VARIANTS))
+def test_variant_w8a8_gemm(oracle, variant):
+    """W8A8 at m > 32: the int8-rounded activations through the tensor-core GEMM."""
+    var = VARIANTS[variant][0]
+    n, k, m = 64, 1024, 48
+    wb, ws = _blocks(variant, n, k, seed=9)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(6))
+    cfg = c.ActivationQuantConfig(c.ActivationQuantMode.W8A8)
+    y = c.iq2_matmul_with_activation_quant(x.cuda(), torch.from_numpy(wb).cuda(), torch.from_numpy(ws).cuda(),
+                                           n, k, var, cfg).cpu().numpy()
+    ref = oracle.matmul(oracle.rowwise_qdq_w8a8(x.numpy()), wb, ws, n, k, variant=variant)
+    assert rel_l2(y, ref) <= GEMM_ORACLE_TOL
