@@ -694,6 +694,8 @@ def next_rows_bench(args, device, stream, peaks, peak_src):
     one GPU, inputs resident, HBM-bound, against measured HBM:
       w8a8      iq2_matmul_with_activation_quant (IQ2_XXS, W8A8) at M=1 and M=16; packed weight GB/s
       variants  iq2_xs_matmul / iq2_s_matmul / iq3_s_matmul at M=1, f32 x; packed weight GB/s
+      variants_prefill_tcgen05  the same at M=2048, bf16 x (the tcgen05 GEMM); TFLOP/s against the
+                measured bf16 burst
       dequant   iq2_dequantize to f16 (IQ2_XXS); GB/s of packed bytes read + f16 bytes written
       gguf      split_interleaved of ggml IQ2_XXS blocks; GB/s of block bytes read + written
     Matmuls rotate over distinct weights totalling > 260 MB (CUDA graph of back-to-back calls);
@@ -740,13 +742,39 @@ def next_rows_bench(args, device, stream, peaks, peak_src):
         gbs = wbytes / (ms * 1e-3) / 1e9
         return {"us": round(ms * 1e3, 2), "weight_gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4)}
 
+    def prefill_tflops(var, m=2048):
+        """The variant's tcgen05 GEMM at M=m (bf16 x), weights rotated over > 260 MB."""
+        bpb, spb = gguf.SPLIT[var]
+        wbytes = n * nb * (bpb + spb)
+        copies = max(2, int(260e6 // wbytes) + 1)
+        ws_list = [variant_weights(var) for _ in range(copies)]
+        x = synth.activations(m, k, seed=78, dtype=torch.bfloat16, device=device)
+        out = torch.empty(m, n, device=device)
+        wsp = torch.empty(max(1, c.workspace_bytes(m, n, k, torch.bfloat16, var)), dtype=torch.uint8, device=device)
+        for (wb, sc) in ws_list:
+            c.iq2_matmul(x, wb, sc, n, k, var, out=out, workspace=wsp)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 3
+        e0.record()
+        for _ in range(reps):
+            for (wb, sc) in ws_list:
+                c.iq2_matmul(x, wb, sc, n, k, var, out=out, workspace=wsp)
+        e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+        tf = 2.0 * m * n * k / (us * 1e-6) / 1e12
+        return {"m": m, "us": round(us, 1), "tflops": round(tf, 1),
+                "frac_bf16_burst": round(tf / peaks["bf16_tflops"], 4)}
+
     aq = c.ActivationQuantConfig(c.ActivationQuantMode.W8A8)
     w8a8 = {f"m{m}": matmul_gbs(lambda x, wb, sc, o, w: c.iq2_matmul_with_activation_quant(
         x, wb, sc, n, k, V.Iq2Xxs, aq, out=o, workspace=w), V.Iq2Xxs, m) for m in (1, 16)}
-    variants = {}
+    variants, variants_prefill = {}, {}
     for name, var in (("iq2_xs", V.Iq2Xs), ("iq2_s", V.Iq2S), ("iq3_s", V.Iq3S)):
         variants[name] = matmul_gbs(lambda x, wb, sc, o, w, var=var: c.iq2_matmul(
             x, wb, sc, n, k, var, out=o, workspace=w), var, 1)
+        variants_prefill[name] = prefill_tflops(var)
 
     def eager_ms(fn, reps=20):
         with torch.cuda.stream(stream):
@@ -782,7 +810,8 @@ def next_rows_bench(args, device, stream, peaks, peak_src):
           "frac_hbm": round(gbytes / (ms * 1e-3) / 1e9 / hbm, 4), "bytes": gbytes}
     del blocks
     return {"shape": "K=4096, N=14336 (Llama-3-8B gate/up)", "peak_hbm_gbs": hbm, "peak_source": peak_src,
-            "w8a8": w8a8, "variants": variants, "dequant_f16": dq, "gguf_split_interleaved": gg}
+            "w8a8": w8a8, "variants": variants, "variants_prefill_tcgen05": variants_prefill,
+            "dequant_f16": dq, "gguf_split_interleaved": gg}
 
 
 # ---------------------------------------------------------------------------------------- CPU
