@@ -102,6 +102,24 @@ template <typename XT, int NT, int LB = 4>
 __device__ __forceinline__ void limb_job(const XT* __restrict__ x, uint32_t M, uint32_t K, uint32_t m,
                                          uint32_t b, uint8_t* xb, float* colscale, int lane) {
     const int sbi = lane >> 2, t = lane & 3;
+    if (m >= M) {
+        // a padding token (warp-uniform): zero limbs and zero column scales, nothing to read
+        const size_t sb = (size_t)b * 8 + sbi;
+        if constexpr (LB == 16) {
+            const uint32_t ntile = m >> 3, col = m & 7u;
+            *reinterpret_cast<uint2*>(xb + ((sb * NT + ntile) * 32 + col * 4 + t) * 8) = make_uint2(0u, 0u);
+            *reinterpret_cast<uint2*>(xb + ((sb * NT + NT / 2 + ntile) * 32 + col * 4 + t) * 8) = make_uint2(0u, 0u);
+            if (lane < 2) colscale[(size_t)b * (NT * 8) + (lane == 0 ? ntile : NT / 2 + ntile) * 8 + col] = 0.0f;
+        } else {
+            constexpr uint32_t TPN = 8 / LB;
+            const uint32_t nt = m / TPN, colbase = (m % TPN) * LB;
+#pragma unroll
+            for (int l = 0; l < LB; ++l)
+                *reinterpret_cast<uint2*>(xb + ((sb * NT + nt) * 32 + (colbase + l) * 4 + t) * 8) = make_uint2(0u, 0u);
+            if (lane < LB) colscale[(size_t)b * (NT * 8) + nt * 8 + colbase + lane] = 0.0f;
+        }
+        return;
+    }
     const size_t k0 = (size_t)b * QK + sbi * 32 + t * 8;
     const XT* xr = x + (size_t)min(m, M - 1u) * K;
     float v[8];
@@ -157,16 +175,45 @@ __device__ __forceinline__ void limb_job(const XT* __restrict__ x, uint32_t M, u
 #pragma unroll
         for (int l = 0; l < LB; ++l) lo[l] = hi[l] = 0u;
         if (!bad && amax > 0.0f) {
+            if constexpr (LB == 4) {
+                // element i -> one word whose byte l is its signed limb l: |q| < 2^27 spread into
+                // four 7-bit bytes, negated bytewise for q < 0 ((0x80 - v) ^ 0x80 is -v mod 256 for
+                // every byte v <= 127, with no borrow between bytes); then a 4x4 byte transpose per
+                // half gives the words of limb l over elements 0..3 (lo) and 4..7 (hi)
+                uint32_t w[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int q = (int)rintf(fast ? v[i] * sc : ldexpf(v[i], B - E));
-                const uint32_t mag = (uint32_t)(q < 0 ? -q : q);
+                for (int i = 0; i < 8; ++i) {
+                    const int q = (int)rintf(fast ? v[i] * sc : ldexpf(v[i], B - E));
+                    const uint32_t mag = (uint32_t)(q < 0 ? -q : q);
+                    const uint32_t sp = (mag & 0x7Fu) | ((mag << 1) & 0x7F00u) | ((mag << 2) & 0x7F0000u) |
+                                        ((mag << 3) & 0x7F000000u);
+                    w[i] = q < 0 ? ((0x80808080u - sp) ^ 0x80808080u) : sp;
+                }
 #pragma unroll
-                for (int l = 0; l < LB; ++l) {
-                    const int limb = (l < LB - 1) ? (int)((mag >> (7 * l)) & 127u) : (int)(mag >> (7 * (LB - 1)));
-                    const uint32_t byte = (uint32_t)(uint8_t)(int8_t)(q < 0 ? -limb : limb);
-                    if (i < 4) lo[l] |= byte << (8 * i);
-                    else hi[l] |= byte << (8 * (i - 4));
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t* dst = h ? hi : lo;
+                    const uint32_t a0 = prmt(w[4 * h], w[4 * h + 1], 0x5140u);  // {e0.b0, e1.b0, e0.b1, e1.b1}
+                    const uint32_t a1 = prmt(w[4 * h], w[4 * h + 1], 0x7362u);  // {e0.b2, e1.b2, e0.b3, e1.b3}
+                    const uint32_t b0 = prmt(w[4 * h + 2], w[4 * h + 3], 0x5140u);
+                    const uint32_t b1 = prmt(w[4 * h + 2], w[4 * h + 3], 0x7362u);
+                    dst[0] = prmt(a0, b0, 0x5410u);
+                    dst[1] = prmt(a0, b0, 0x7632u);
+                    dst[2] = prmt(a1, b1, 0x5410u);
+                    dst[3] = prmt(a1, b1, 0x7632u);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int q = (int)rintf(fast ? v[i] * sc : ldexpf(v[i], B - E));
+                    const uint32_t mag = (uint32_t)(q < 0 ? -q : q);
+#pragma unroll
+                    for (int l = 0; l < LB; ++l) {
+                        const int limb =
+                            (l < LB - 1) ? (int)((mag >> (7 * l)) & 127u) : (int)(mag >> (7 * (LB - 1)));
+                        const uint32_t byte = (uint32_t)(uint8_t)(int8_t)(q < 0 ? -limb : limb);
+                        if (i < 4) lo[l] |= byte << (8 * i);
+                        else hi[l] |= byte << (8 * (i - 4));
+                    }
                 }
             }
         }

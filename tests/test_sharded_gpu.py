@@ -43,7 +43,7 @@ def _rank(rank: int, port: int, q):
         errs = {}
         shapes = [(4096, 4096), (1024, 14336), (14336, 4096)]
         full = [tuple(t.to(dev) for t in synth.iq2xxs_weights(n, k, seed=i)) for i, (n, k) in enumerate(shapes)]
-        for m in (1, 3):
+        for m in (1, 3, 300):  # (300: the tensor-core GEMM, paired CTAs, on each rank's slice)
             xs = [synth.activations(m, k, seed=20 + i, device=dev) for i, (n, k) in enumerate(shapes)]
             # one projection per call (m = 1: all-gathered straight into the output)
             for i, (n, k) in enumerate(shapes):
