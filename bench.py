@@ -873,9 +873,10 @@ def run_reference(args, rank: int, world: int):
 def run_case(args):
     """Only the dominant kernel on its roofline shape, `--steps` times after two warm calls: the
     command the profiler captures. gemv: 4096x14336 (K x N) at M=1, f32 x, two weight copies
-    (30 MB) in turn; gemm: M=2048 on the same projection, bf16 x; grouped: the benchmark step
-    (every projection of `--layers` layers in one iq2_matmul_grouped call, M=1); variant: the
-    IQ2_XS matmul on the gemv shape (random blocks, d ~U[1e-3, 1e-2]), M=1, f32 x."""
+    (30 MB) in turn; gemm: M=2048 (or `--m` M > 32) on the same projection, bf16 x; grouped: the
+    benchmark step (every projection of `--layers` layers in one iq2_matmul_grouped call, M=1);
+    variant: the IQ2_XS matmul on the gemv shape (random blocks, d ~U[1e-3, 1e-2]), M=1, f32 x, or
+    with `--m` M > 32 its tcgen05 GEMM at that M, bf16 x."""
     import candelora_metal_kernels_b200 as c
     from candelora_metal_kernels_b200 import synth
     torch.cuda.set_device(0)
@@ -894,7 +895,7 @@ def run_case(args):
                           "calls": args.steps, "us_per_call": round(e0.elapsed_time(e1) * 1e3 / args.steps, 2)}),
               flush=True)
         return
-    n, k = 14336, 4096
+    k, n = (int(v) for v in args.kn.split(","))
     if args.case == "variant":
         nb = k // 256
         g = torch.Generator(device="cuda")
@@ -904,21 +905,24 @@ def run_case(args):
         sc[:, :2] = (torch.rand(n * nb, device="cuda", generator=g) * 9e-3 + 1e-3).to(torch.float16).view(
             torch.uint8).view(-1, 2)
         sc = sc.reshape(-1)
-        x = synth.activations(1, k, seed=1, device="cuda")
-        out = torch.empty(1, n, device="cuda")
+        vm = args.m if args.m > 32 else 1  # (m > 32: the tcgen05 GEMM, bf16 x)
+        x = synth.activations(vm, k, seed=1, dtype=torch.bfloat16 if vm > 1 else torch.float32, device="cuda")
+        out = torch.empty(vm, n, device="cuda")
+        vws = torch.empty(max(1, c.workspace_bytes(vm, n, k, x.dtype, c.Iq2MatmulVariant.Iq2Xs)), dtype=torch.uint8,
+                          device="cuda")
         for _ in range(2):
-            c.iq2_matmul(x, wb, sc, n, k, c.Iq2MatmulVariant.Iq2Xs, out=out)
+            c.iq2_matmul(x, wb, sc, n, k, c.Iq2MatmulVariant.Iq2Xs, out=out, workspace=vws)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
-            c.iq2_matmul(x, wb, sc, n, k, c.Iq2MatmulVariant.Iq2Xs, out=out)
+            c.iq2_matmul(x, wb, sc, n, k, c.Iq2MatmulVariant.Iq2Xs, out=out, workspace=vws)
         e1.record()
         e1.synchronize()
-        print(json.dumps({"case": "variant", "m": 1, "k": k, "n": n, "calls": args.steps,
+        print(json.dumps({"case": "variant", "m": vm, "k": k, "n": n, "calls": args.steps,
                           "us_per_call": round(e0.elapsed_time(e1) * 1e3 / args.steps, 2)}), flush=True)
         return
-    m = 1 if args.case == "gemv" else 2048
+    m = 1 if args.case == "gemv" else (args.m if args.m > 32 else 2048)
     dtype = torch.float32 if args.case == "gemv" else torch.bfloat16
     ws_ = [tuple(t.cuda() for t in synth.iq2xxs_weights(n, k, seed=i)) for i in range(2)]
     x = synth.activations(m, k, seed=1, dtype=dtype, device="cuda")
@@ -957,6 +961,7 @@ def main():
     ap.add_argument("--gemm-reps", type=int, default=5)
     ap.add_argument("--case", choices=["gemv", "gemm", "grouped", "variant"], default=None,
                     help="run only the dominant kernel's shape (the profiler's small case) and exit")
+    ap.add_argument("--kn", default="4096,14336", help="--case gemv/gemm/variant: K,N of the projection")
     args = ap.parse_args()
     if args.case:
         run_case(args)
