@@ -362,14 +362,18 @@ __device__ __forceinline__ void decode_half(uint2 q, float d, uint32_t sel_l, ui
 // ---- the other formats (IQ2_XS, IQ2_S, IQ3_S) ----
 // Split-layout geometry per 256-weight block (weight bytes QB, scale bytes SB; reference
 // src/iq2_matmul.rs:15-29) and the decode table: E entries of ENT bytes, C interleaved copies
-// (E * ENT * C = the table's 32 KB), copy `lane % C` for each lane.
-template <int V>
+// (E * ENT * C = the table's TBL bytes), copy `lane % C` for each lane. The paired kernel of the
+// other formats has three 48 KB stages and a 64 KB table (16 / 8 / 8 copies: the lookups of a
+// half-warp bank-conflict less); everything else four paired or three unpaired stages and 32 KB.
+template <int V, bool PAIR = false>
 struct GFmt {
+    static constexpr uint32_t TBL = (PAIR && V != 0) ? 2u * (uint32_t)G_SEL_BYTES : (uint32_t)G_SEL_BYTES;
+    static constexpr int STAGES = PAIR ? (V == 0 ? G_STAGES_PAIR : 3) : G_STAGES;
     static constexpr uint32_t QB = V == 2 ? 72u : (V == 3 ? 104u : 64u);
     static constexpr uint32_t SB = V == 0 ? 2u : (V == 3 ? 6u : 10u);
     static constexpr uint32_t ENT = V == 3 ? 16u : 8u;
     static constexpr uint32_t E = V == 0 ? 256u : (V == 2 ? 1024u : 512u);
-    static constexpr uint32_t C = (uint32_t)G_SEL_BYTES / (E * ENT);
+    static constexpr uint32_t C = TBL / (E * ENT);
     static_assert(C >= 1 && (C & (C - 1)) == 0, "copies");
 };
 
@@ -428,10 +432,10 @@ __device__ __forceinline__ uint4 ld_raw(const uint8_t* qblk, const uint8_t* sblk
 // chunks at dst ^ (t << 4) like decode_sub. Each weight is bf16 of its exact value dl * g * sign
 // (dl * g has at most 22 significant bits): the candidate products are rounded once and `prmt`
 // picks them by grid code; an XOR applies the signs. TAIL: zero the weights at k >= K.
-template <int V, int NG, bool TAIL>
+template <int V, int NG, bool TAIL, bool PAIR>
 __device__ __forceinline__ void decode_v(uint4 raw, float d, uint32_t sel_l, uint32_t dst, uint32_t t0,
                                          uint32_t k_lo, uint32_t K) {
-    constexpr uint32_t STRIDE = GFmt<V>::C * GFmt<V>::ENT;  // bytes between table entries
+    constexpr uint32_t STRIDE = GFmt<V, PAIR>::C * GFmt<V, PAIR>::ENT;  // bytes between table entries
     uint32_t ca = 0, cb = 0, cc = 0, cdd = 0;  // the rounded candidates (IQ3_S: all four; else qlo, qhi)
     uint32_t cur_nib = 0xFFFFFFFFu;
 #pragma unroll
@@ -524,14 +528,16 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
                                                             const GemmParams p) {
     static_assert(BN % 32 == 0 && BN <= G_BN, "BN");
     static_assert(!PAIR || BN == G_BN, "paired CTAs split a 256-row tile");
-    constexpr int S = PAIR ? G_STAGES_PAIR : G_STAGES;                 // stages in the ring
+    using F = GFmt<V, PAIR>;
+    constexpr int S = F::STAGES;                                        // stages in the ring
     constexpr uint32_t SB = PAIR ? G_STAGE_BYTES_PAIR : G_STAGE_BYTES;  // bytes per stage
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_s = smem_u32(smem_raw);
     const uint32_t base_s = (raw_s + 1023u) & ~1023u;  // SW128 tiles need 1024-byte alignment
     uint8_t* base = smem_raw + (base_s - raw_s);
     const uint32_t sel_s = base_s + S * SB;
-    const uint32_t bar_s = sel_s + G_SEL_BYTES;
+    const uint32_t bar_s = sel_s + F::TBL;
+    static_assert(1024 + S * SB + F::TBL + 256 <= (uint32_t)G_SMEM, "shared memory");
     // barriers: full_a[S], full_b[S], empty[S], acc_full; then the TMEM address word; abort flag
     auto full_a = [&](int s) { return bar_s + 8u * s; };
     auto full_b = [&](int s) { return bar_s + 8u * (S + s); };
@@ -575,8 +581,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
 
     // decode table -> shared memory: per grid entry the four 16-bit prmt selectors packed in two
     // words (IQ3_S: GFmt<3>'s 16-byte entries), C times (copy c of entry e at (e * C + c) * ENT)
-    for (int i = threadIdx.x; i < (int)(GFmt<V>::E * GFmt<V>::C); i += blockDim.x) {
-        const uint32_t e = (uint32_t)i / GFmt<V>::C;
+    for (int i = threadIdx.x; i < (int)(F::E * F::C); i += blockDim.x) {
+        const uint32_t e = (uint32_t)i / F::C;
         if constexpr (V == 0) {
             const uint32_t* w = IQ2XXS_BF16_SEL[e];
             reinterpret_cast<uint2*>(base + (sel_s - base_s))[i] = make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
@@ -702,7 +708,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
         const uint32_t brow = base_s + G_A_BYTES + (r >> 3) * 1024u + (r & 7u) * 128u +
                               ((((hh * 4u) ^ (r & 7u))) << 4);
         const uint32_t kt_full = p.K / G_BK;  // stages below this one have no K tail
-        const uint32_t sel_l = sel_s + (lane & (GFmt<V>::C - 1)) * GFmt<V>::ENT;  // this lane's table copy
+        const uint32_t sel_l = sel_s + (lane & (F::C - 1)) * F::ENT;  // this lane's table copy
         // loads run ahead of the decode (the sub-block two stages on, the block scale one block
         // on), clamped to this CTA's last stage and block
         const uint32_t kt_last = kt0 + NKT - 1u, b_last = b1 - 1u;
@@ -747,8 +753,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
                 constexpr int NG = PAIR ? 2 : 4;  // groups per thread
                 const uint32_t t0 = PAIR ? 2u * ghalf : 0u;
                 if (PAIR || live) {
-                    if (kt < kt_full) decode_v<V, NG, false>(q, d, sel_l, dst, t0, 0, p.K);
-                    else decode_v<V, NG, true>(q, d, sel_l, dst, t0, kt * G_BK + hh * 32, p.K);
+                    if (kt < kt_full) decode_v<V, NG, false, PAIR>(q, d, sel_l, dst, t0, 0, p.K);
+                    else decode_v<V, NG, true, PAIR>(q, d, sel_l, dst, t0, kt * G_BK + hh * 32, p.K);
                 }
             } else if (PAIR) {
                 if (kt < kt_full) decode_half<false>(q, d, sel_l, dst, ghalf, 0, p.K);
