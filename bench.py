@@ -13,7 +13,9 @@ from L2). Synthetic data.
   per_call = the same step as 224 reference-shaped iq2_xxs_matmul calls
   e2e      = the same step through the public API (the one grouped call) with every projection's x
              copied host->device from pinned memory and every output device->host inside the timed
-             region; e2e.per_call: the same with the 224 reference-shaped calls
+             region, pipelined as a serving loop runs it (copy streams, two buffer sets: step k's
+             copies overlap steps k-1 / k+1's compute); e2e.per_call: the same with the 224
+             reference-shaped calls
   roofline: the dominant kernel of the timed region (the step's one grouped GEMV launch; its
             duration bounded by the step time) against measured HBM, with ncu DRAM traffic;
             roofline.single_call: the decode GEMV of one 4096x14336 gate/up projection timed alone
@@ -107,13 +109,14 @@ class ClockSampler:
 
 # ---------------------------------------------------------------------------------------- ours
 class Workload:
-    """Device-resident weights, inputs, outputs and workspaces of one step, optionally sharded."""
+    """Device-resident weights, inputs, outputs and workspaces of one step, optionally sharded.
+    The x and output buffers come in sets (add_buffer_set): the pipelined end-to-end run alternates
+    two, so that one step's copies overlap another step's compute."""
 
     def __init__(self, m: int, layers: int, rank: int, world: int, device: torch.device, comm=None):
         from candelora_metal_kernels_b200 import grouped_workspace_bytes, synth, workspace_bytes
         from candelora_metal_kernels_b200.sharded import sharded_workspace_bytes
         self.m, self.device, self.rank, self.world, self.comm = m, device, rank, world, comm
-        self.calls = []  # (x_view, qs, sc, n, k, out_view, ws, name): qs/sc = this rank's row slice
         self.weight_bytes = 0        # whole-job packed bytes per step
         x_elems = out_elems = 0
         specs = []
@@ -123,48 +126,64 @@ class Workload:
                 x_elems += m * k
                 out_elems += m * n  # every rank ends with the full outputs
                 self.weight_bytes += synth.packed_bytes(n, k)
+        self.x_elems, self.out_elems = x_elems, out_elems
         self.fused = comm is not None and comm.has_symmetric and m <= 16
-        self.x_dev = torch.empty(x_elems, dtype=torch.float32, device=device)
-        self.out_dev = (comm.symmetric_empty(out_elems) if comm is not None and comm.has_symmetric
-                        else torch.empty(out_elems, dtype=torch.float32, device=device))
         self.x_host = torch.empty(x_elems, dtype=torch.float32, pin_memory=True)
         self.out_host = torch.empty(out_elems, dtype=torch.float32, pin_memory=True)
         ws_cache = {}
+        self.specs = []  # (qs, sc, n, k, x_off, out_off, ws, name): qs/sc = this rank's row slice
         for (layer, pi, name, k, n, n_loc, xo, oo) in specs:
             seed = layer * 16 + pi
             qs, sc = synth.iq2xxs_weights(n, k, seed, device=device, row_begin=rank * n_loc,
                                           row_end=(rank + 1) * n_loc)
             x = synth.activations(m, k, seed=10_000 + seed)
             self.x_host[xo:xo + m * k].copy_(x.reshape(-1))
-            xv = self.x_dev[xo:xo + m * k].view(m, k)
             key = (n, k)
             if key not in ws_cache:  # one workspace per shape is enough: calls are stream-ordered
                 need = (workspace_bytes(m, n, k, torch.float32) if world == 1
-                        else sharded_workspace_bytes(comm, [(xv, qs, sc, n, k)]))
+                        else sharded_workspace_bytes(comm, [(torch.empty(m, k, device=device), qs, sc, n, k)]))
                 ws_cache[key] = torch.empty(need, dtype=torch.uint8, device=device)
-            self.calls.append((xv, qs, sc, n, k, self.out_dev[oo:oo + m * n].view(m, n), ws_cache[key], name))
-        self.x_dev.copy_(self.x_host)
-        self.problems = [(x, qs, sc, n, k, out) for (x, qs, sc, n, k, out, _, _) in self.calls]
+            self.specs.append((qs, sc, n, k, xo, oo, ws_cache[key], name))
+        self.sets = []
+        self.add_buffer_set()
+        self.x_dev, self.out_dev = self.sets[0]["x"], self.sets[0]["out"]
+        self.calls, self.problems = self.sets[0]["calls"], self.sets[0]["problems"]
         need = (grouped_workspace_bytes(self.problems) if world == 1
                 else sharded_workspace_bytes(comm, self.problems))
         self.grouped_ws = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
 
-    def step(self, grouped: bool = False):
-        """One step: every projection through the per-projection call (iq2_xxs_matmul, the
-        reference-shaped call; column-sharded with one all-gather per call on N > 1 GPUs), or all
-        of them through one grouped call (one all-gather per step on N > 1 GPUs)."""
+    def add_buffer_set(self):
+        """Another x buffer and output buffer (outputs in the symmetric region when there is one),
+        with the step's calls bound to them; returns its index."""
+        comm, m = self.comm, self.m
+        x_dev = torch.empty(self.x_elems, dtype=torch.float32, device=self.device)
+        out_dev = (comm.symmetric_empty(self.out_elems) if comm is not None and comm.has_symmetric
+                   else torch.empty(self.out_elems, dtype=torch.float32, device=self.device))
+        x_dev.copy_(self.x_host)
+        calls = []  # (x_view, qs, sc, n, k, out_view, ws, name)
+        for (qs, sc, n, k, xo, oo, ws, name) in self.specs:
+            calls.append((x_dev[xo:xo + m * k].view(m, k), qs, sc, n, k, out_dev[oo:oo + m * n].view(m, n), ws, name))
+        problems = [(x, qs, sc, n, k, out) for (x, qs, sc, n, k, out, _, _) in calls]
+        self.sets.append({"x": x_dev, "out": out_dev, "calls": calls, "problems": problems})
+        return len(self.sets) - 1
+
+    def step(self, grouped: bool = False, b: int = 0):
+        """One step on buffer set b: every projection through the per-projection call
+        (iq2_xxs_matmul, the reference-shaped call; column-sharded with one all-gather per call on
+        N > 1 GPUs), or all of them through one grouped call (one all-gather per step on N > 1 GPUs)."""
         from candelora_metal_kernels_b200 import iq2_matmul_grouped, iq2_xxs_matmul
         from candelora_metal_kernels_b200.sharded import iq2_matmul_grouped_sharded, iq2_matmul_sharded
+        calls, problems = self.sets[b]["calls"], self.sets[b]["problems"]
         if self.world == 1:
             if grouped:
-                iq2_matmul_grouped(self.problems, workspace=self.grouped_ws)
+                iq2_matmul_grouped(problems, workspace=self.grouped_ws)
             else:
-                for (x, qs, sc, n, k, out, ws, _) in self.calls:
+                for (x, qs, sc, n, k, out, ws, _) in calls:
                     iq2_xxs_matmul(x, qs, sc, n, k, out=out, workspace=ws)
         elif grouped:
-            iq2_matmul_grouped_sharded(self.comm, self.problems, workspace=self.grouped_ws)
+            iq2_matmul_grouped_sharded(self.comm, problems, workspace=self.grouped_ws)
         else:
-            for (x, qs, sc, n, k, out, ws, _) in self.calls:
+            for (x, qs, sc, n, k, out, ws, _) in calls:
                 iq2_matmul_sharded(self.comm, x, qs, sc, n, k, out=out, workspace=ws)
 
     def launches_per_step(self, grouped: bool = False) -> int:
@@ -209,7 +228,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         comm = Iq2Comm()  # the library's NCCL communicator; the NCCL process group carries its id
         if args.exchange == "fused":  # outputs here: the GEMV stores them into every rank
             step_out = args.m * args.layers * sum(n for (_, _, n) in synth.LLAMA3_8B_PROJECTIONS) * 4
-            comm.alloc_symmetric(step_out + (32 << 20))  # + the configuration 3/4 decode outputs
+            # two output sets (the pipelined end-to-end run) + the configuration 3/4 decode outputs
+            comm.alloc_symmetric(2 * step_out + (32 << 20))
     wl = Workload(args.m, args.layers, rank, world, device, comm)
     stream = torch.cuda.Stream(device)
     torch.cuda.synchronize()
@@ -278,35 +298,80 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     # ---- end to end: host x -> device, the step through the public API, outputs -> host; the
     # ---- same step as `value` (one grouped call) and, beside it, as 224 reference-shaped calls
-    def e2e_run(g) -> float:
-        def e2e_step():
-            wl.x_dev.copy_(wl.x_host, non_blocking=True)
-            g.replay()
-            wl.out_host.copy_(wl.out_dev, non_blocking=True)
+    # Pipelined as a serving loop runs it: step k's upload and download go on two copy streams and
+    # overlap other steps' compute, with two x and output buffers (graph b = k % 2 is the step on
+    # buffer set b). Every step's copies are inside the timed region: the uploads start after the
+    # start event and the end event follows the last download.
+    wl.add_buffer_set()
+    cin, cout = torch.cuda.Stream(device), torch.cuda.Stream(device)
+
+    def capture(grouped: bool, b: int):
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                wl.step(grouped=grouped, b=b)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            wl.step(grouped=grouped, b=b)
+        return g
+
+    ggraph1 = capture(True, 1)
+    graph1 = capture(False, 1)
+
+    def e2e_run(graphs) -> float:
+        def run(nsteps, start_ev):
+            comp, down = [None, None], [None, None]
+            for k in range(nsteps):
+                b = k % 2
+                bs = wl.sets[b]
+                with torch.cuda.stream(cin):
+                    cin.wait_event(start_ev)
+                    if comp[b] is not None:
+                        cin.wait_event(comp[b])  # the compute that last read this x buffer
+                    bs["x"].copy_(wl.x_host, non_blocking=True)
+                    up = torch.cuda.Event()
+                    up.record(cin)
+                with torch.cuda.stream(stream):
+                    stream.wait_event(up)
+                    if down[b] is not None:
+                        stream.wait_event(down[b])  # the download that last read this output buffer
+                    graphs[b].replay()
+                    comp[b] = torch.cuda.Event()
+                    comp[b].record(stream)
+                with torch.cuda.stream(cout):
+                    cout.wait_event(comp[b])
+                    wl.out_host.copy_(bs["out"], non_blocking=True)
+                    down[b] = torch.cuda.Event()
+                    down[b].record(cout)
+            for ev in down:
+                if ev is not None:
+                    stream.wait_event(ev)
 
         with torch.cuda.stream(stream):
-            for _ in range(3):
-                e2e_step()
+            w0 = torch.cuda.Event()
+            w0.record(stream)
+        run(4, w0)
         stream.synchronize()
         if dist:
             torch.distributed.barrier()
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             s0.record(stream)
-            for _ in range(args.steps):
-                e2e_step()
+        run(args.steps, s0)
+        with torch.cuda.stream(stream):
             s1.record(stream)
         s1.synchronize()
+        torch.cuda.synchronize()
         return max_over_ranks(s0.elapsed_time(s1))
 
-    e2e_ms = e2e_run(ggraph)
+    e2e_ms = e2e_run([ggraph, ggraph1])
     e2e_value = wl.weight_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
-    e2e_pc_ms = e2e_run(graph)
+    e2e_pc_ms = e2e_run([graph, graph1])
     e2e_per_call = {"value": round(wl.weight_bytes / (e2e_pc_ms / args.steps * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_pc_ms / args.steps, 4),
                     "path": ("pinned host x -> device, 224 reference-shaped iq2_matmul calls"
                              + (" (column-sharded, " + _exchange_words(wl, "each") + ")" if dist else "")
-                             + ", outputs -> pinned host")}
+                             + ", outputs -> pinned host; pipelined: copy streams, two buffer sets")}
 
     # ---- roofline of the dominant kernel: 4096x14336 decode GEMV alone, 64 matrices in rotation
     peaks, peak_src = _peaks()
@@ -346,7 +411,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 "single_call": single}
         del g2
 
-    del graph, ggraph
+    del graph, ggraph, graph1, ggraph1
     models = None
     if not args.no_models:
         models = {"forward": forward_bench(args, wl, device, stream, comm, dist),
@@ -378,7 +443,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                     "path": ("pinned host x -> device, the step's 224 projections through one "
                              + ("iq2_matmul_grouped call" if not dist else
                                 "iq2_matmul_grouped_sharded call (" + _exchange_words(wl, "per step") + ")")
-                             + ", outputs -> pinned host"),
+                             + ", outputs -> pinned host; pipelined: each step's upload and download on "
+                               "copy streams overlap the neighbouring steps' compute (two x / output buffer sets)"),
                     "per_call": e2e_per_call},
             "gpu_launches": wl.launches_per_step(True) * args.steps,
             "per_call": per_call,
