@@ -40,6 +40,7 @@
 //     GEMV only builds its constant table and prefetches its first weights into L2.
 #include "iq2xxs_common.cuh"
 #include "iq2xxs_codebook.h"
+#include "iq2_variant_grids.h"
 #include "iq2xxs_internal.h"
 
 #include <cstring>
@@ -53,6 +54,8 @@ namespace {
 constexpr int GEMV_WARPS = 16;            // per CTA; a cluster (2 CTAs) has 32
 constexpr int CLUSTER = 2;
 constexpr int LUT_BYTES = 256 * 256;      // 256 rows x (32 lanes grid selectors | 32 lanes sign)
+// IQ2_XS: 512 grid rows x 32 lanes (64 KB), then 128 sign rows x 32 lanes
+constexpr int LUT_BYTES_XS = 512 * 128 + 128 * 128;
 constexpr int MAX_PROBLEMS = 256;         // per grouped launch
 constexpr int MAX_CLUSTERS = 96;          // >= SMs / 2 of the device (74 on B200)
 constexpr int SMEM_LIMIT = 227 * 1024;
@@ -61,22 +64,30 @@ constexpr int SMEM_LIMIT = 227 * 1024;
 // 16: the 16-bit split (5 <= m <= 32; tiles [0, NT/2) hold eight tokens' signed high bytes,
 // tiles [NT/2, NT) the same tokens' unsigned low bytes); 1: the int8 activations of the W8A8
 // mode, eight tokens per n8 tile.
-template <int NT, int LB = 4>
+// FMT: the weight format, 0 IQ2_XXS, 1 IQ2_XS (its 512-entry grid needs an 80 KB table, its
+// scales a 16-byte word per row and stage).
+template <int NT, int LB = 4, int FMT = 0>
 struct GemvShape {
     static constexpr bool SPLIT = LB == 16;
+    static constexpr int LUT = FMT == 1 ? LUT_BYTES_XS : LUT_BYTES;
     static constexpr int T = ((NT <= 2 && LB != 1) || (NT == 1 && LB == 1)) ? 2 : 1;  // 16-row mma tiles per warp
     static constexpr int ROWS = 16 * T;                // rows of a tile
     static constexpr int TPN = SPLIT ? 8 : 8 / LB;     // tokens per n8 tile (SPLIT: per high-byte tile)
     static constexpr int TOK = SPLIT ? 4 * NT : TPN * NT;  // tokens incl. the zero padding
     static constexpr int STAGE_QS = ROWS * 64;         // one block of qs per row
-    static constexpr int STAGE_BYTES = STAGE_QS + ROWS * 4;  // + the aligned scale word per row
+    // + per row the aligned scale word (IQ2_XS: the 12 aligned bytes holding d and the 8 scale bytes)
+    static constexpr int STAGE_BYTES = STAGE_QS + ROWS * (FMT == 1 ? 16 : 4);
     // fewer stages where the partials (TOK x ROWS per warp slot) are large
-    static constexpr int NSTAGES = T == 2 ? 3 : ((LB == 4 || (LB == 1 && NT <= 2) || (SPLIT && NT <= 4)) ? 6 : 4);
-    static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;  // per warp
+    static constexpr int NSTAGES0 = T == 2 ? 3 : ((LB == 4 || (LB == 1 && NT <= 2) || (SPLIT && NT <= 4)) ? 6 : 4);
     static constexpr int PART_BYTES = GEMV_WARPS * 2 * TOK * ROWS * 4;  // [warp][first|last][token][row]
+    // IQ2_XS: as many as fit beside its larger table (2..5)
+    static constexpr int NS_FIT = (SMEM_LIMIT - LUT - PART_BYTES) / ((GEMV_WARPS + 1) * STAGE_BYTES);
+    static constexpr int NSTAGES = FMT == 1 ? (NS_FIT < NSTAGES0 ? NS_FIT : NSTAGES0) : NSTAGES0;
+    static_assert(NSTAGES >= 2, "stages");
+    static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;  // per warp
     // The table sits at the first 64 KB-aligned shared address of the block's window and the
     // warps' rings fill the space around it; whatever the window's base, this suffices:
-    static constexpr int SMEM = LUT_BYTES + (GEMV_WARPS + 1) * RING_BYTES + PART_BYTES;
+    static constexpr int SMEM = LUT + (GEMV_WARPS + 1) * RING_BYTES + PART_BYTES;
 };
 
 int nt_for(uint32_t m) { return m <= 2 ? 1 : (m <= 8 ? 2 : (m <= 16 ? 4 : 8)); }
@@ -400,6 +411,9 @@ struct DecodeK {
     uint32_t gsel;  // prmt selector {gsrc.b0, aux_g.byte t, gsrc.b2, gsrc.b3}
     uint32_t rot;   // rotate that brings sign index t (bits 7t..7t+6) to bits 8..14
     uint32_t soff;  // base | 128 | lane*4
+    // IQ2_XS: prmt selector taking this lane's u16 word t of a sub-block to bits 0..15, and the
+    // grid / sign tables' bases | lane*4 (both 64 KB-aligned, rows of 128 bytes)
+    uint32_t xsel, gbase, sbase;
 };
 
 // Four signed int8 weights of one 8-weight group (sub-block word {aux_g, aux_s}) for this
@@ -411,6 +425,96 @@ __device__ __forceinline__ void decode_group(const DecodeK& k, uint32_t aux_g, u
     const uint32_t sel = ld_shared_const(ga) | ld_shared_const(sa);
     lo = prmt(KPOS, KNEG, sel);
     hi = prmt(KPOS, KNEG, sel >> 16);
+}
+
+// IQ2_XS: four signed int8 weights of one 8-weight group for this lane's word t of the sub-block
+// {lo32 = words 0, 1; hi32 = words 2, 3} (grid index bits 0..8, sign index bits 9..15).
+__device__ __forceinline__ void decode_group_xs(const DecodeK& k, uint32_t lo32, uint32_t hi32, uint32_t& lo,
+                                                uint32_t& hi) {
+    const uint32_t word = prmt(lo32, hi32, k.xsel);  // (bits 16..31: don't care)
+    const uint32_t ga = ((word << 7) & 0xFF80u) | k.gbase;
+    const uint32_t sa = ((word >> 2) & 0x3F80u) | k.sbase;
+    const uint32_t sel = ld_shared_const(ga) | ld_shared_const(sa);
+    lo = prmt(KPOS, KNEG, sel);
+    hi = prmt(KPOS, KNEG, sel >> 16);
+}
+
+__device__ __forceinline__ uint32_t ld_shared_u8_volatile(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+// IQ2_XS stage: as stage_compute, but the scale changes every 16 weights (groups 0-1: the low
+// nibble of the sub-block's scale byte, groups 2-3: the high one). Lane t holds group t's weights,
+// i.e. MMA k-chunks 4t.. and 16+4t.., so two MMAs whose x fragments are zero on lanes t >= 2
+// (resp. t < 2) give the two halves' sums, each scaled by its 2s+1. sc_s: this stage's scale
+// bytes of row g (row r at + (r - g) * 16).
+template <int NT, int T, bool PARTIAL, bool SPLIT>
+__device__ __forceinline__ void stage_compute_xs(const DecodeK& dk, uint32_t st_s, const uint8_t* xbp, uint32_t s_lo,
+                                                 uint32_t s_hi, uint32_t rowbase, uint32_t swz, uint32_t sc_s,
+                                                 bool low_lane, int (&I)[T][NT][4]) {
+#pragma unroll
+    for (int pair = 0; pair < 4; ++pair) {
+        const uint32_t a0 = st_s + rowbase + (((uint32_t)pair ^ swz) << 4);
+        uint4 qw[T][2];
+        qw[0][0] = ld_shared_v4<0>(a0);
+        qw[0][1] = ld_shared_v4<512>(a0);
+        if (T == 2) {
+            qw[T - 1][0] = ld_shared_v4<1024>(a0);
+            qw[T - 1][1] = ld_shared_v4<1536>(a0);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t sb = pair * 2 + h;
+            uint32_t bfa[NT][2], bfb[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                uint2 v = __ldg(reinterpret_cast<const uint2*>(xbp + (sb * NT + nt) * 256));
+                if (PARTIAL && (sb < s_lo || sb >= s_hi)) v = make_uint2(0u, 0u);
+                bfa[nt][0] = low_lane ? v.x : 0u;
+                bfa[nt][1] = low_lane ? v.y : 0u;
+                bfb[nt][0] = low_lane ? 0u : v.x;
+                bfb[nt][1] = low_lane ? 0u : v.y;
+            }
+#pragma unroll
+            for (int tt = 0; tt < T; ++tt) {
+                const uint32_t l0 = h ? qw[tt][0].z : qw[tt][0].x, h0 = h ? qw[tt][0].w : qw[tt][0].y;
+                const uint32_t l1 = h ? qw[tt][1].z : qw[tt][1].x, h1 = h ? qw[tt][1].w : qw[tt][1].y;
+                uint32_t w0, w1, w2, w3;
+                decode_group_xs(dk, l0, h0, w0, w2);
+                decode_group_xs(dk, l1, h1, w1, w3);
+                const uint32_t b0 = ld_shared_u8_volatile(sc_s + (uint32_t)tt * 256u + sb);
+                const uint32_t b1 = ld_shared_u8_volatile(sc_s + (uint32_t)tt * 256u + 128u + sb);
+                const int ca0 = (int)(((b0 & 15u) << 1) | 1u), cb0 = (int)(((b0 >> 4) << 1) | 1u);
+                const int ca1 = (int)(((b1 & 15u) << 1) | 1u), cb1 = (int)(((b1 >> 4) << 1) | 1u);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    int d1[4], d2[4];
+                    if (SPLIT && nt >= NT / 2) {
+                        mma_s8u8_16832(d1, w0, w1, w2, w3, bfa[nt][0], bfa[nt][1]);
+                        mma_s8u8_16832(d2, w0, w1, w2, w3, bfb[nt][0], bfb[nt][1]);
+                    } else {
+                        mma_s8_16832(d1, w0, w1, w2, w3, bfa[nt][0], bfa[nt][1]);
+                        mma_s8_16832(d2, w0, w1, w2, w3, bfb[nt][0], bfb[nt][1]);
+                    }
+                    const int v0 = ca0 * d1[0] + cb0 * d2[0], v1 = ca0 * d1[1] + cb0 * d2[1];
+                    const int v2 = ca1 * d1[2] + cb1 * d2[2], v3 = ca1 * d1[3] + cb1 * d2[3];
+                    if (sb == 0) {
+                        I[tt][nt][0] = v0;
+                        I[tt][nt][1] = v1;
+                        I[tt][nt][2] = v2;
+                        I[tt][nt][3] = v3;
+                    } else {
+                        I[tt][nt][0] += v0;
+                        I[tt][nt][1] += v1;
+                        I[tt][nt][2] += v2;
+                        I[tt][nt][3] += v3;
+                    }
+                }
+            }
+        }
+    }
 }
 
 // One stage (a block of ROWS rows) of the decode: s32 sums per 256-block in I. The first
@@ -479,9 +583,11 @@ __device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, 
 // whose f32/f16/bf16 x this kernel turns into limbs itself (kernel-side layout in shared memory).
 // P2P: every output is stored at the same offset of every rank's symmetric region (the
 // column-sharded call's all-gather done by the epilogue), ordered by the header words.
-template <int NT, int CAP, int XDT, bool P2P = false, int LB = 4>
+template <int NT, int CAP, int XDT, bool P2P = false, int LB = 4, int FMT = 0>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvLaunch<CAP> L) {
-    using S_ = GemvShape<NT, LB>;
+    using S_ = GemvShape<NT, LB, FMT>;
+    static_assert(FMT == 0 || (!P2P && (LB == 4 || LB == 16)), "IQ2_XS: the plain decode GEMV only");
+    constexpr uint32_t SC_B = FMT == 1 ? 10u : (uint32_t)SC_BYTES;  // scale bytes per block
     constexpr bool FUSED = XDT >= 0;
     constexpr int T = S_::T, ROWS = S_::ROWS, TOK = S_::TOK, STAGE_QS = S_::STAGE_QS;
     constexpr int STAGE_BYTES = S_::STAGE_BYTES, NSTAGES = S_::NSTAGES, RING_BYTES = S_::RING_BYTES;
@@ -500,10 +606,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     const uint32_t gap_warps = min(gap / RING_BYTES, (uint32_t)GEMV_WARPS);
     const uint32_t ring_off = (uint32_t)warp < gap_warps
                                   ? (uint32_t)warp * RING_BYTES
-                                  : gap + LUT_BYTES + ((uint32_t)warp - gap_warps) * RING_BYTES;
+                                  : gap + S_::LUT + ((uint32_t)warp - gap_warps) * RING_BYTES;
     uint8_t* ring = smem + ring_off;
     const uint32_t ring_s = base_s + ring_off;
-    const uint32_t part_off = gap + LUT_BYTES + (GEMV_WARPS - gap_warps) * RING_BYTES;
+    const uint32_t part_off = gap + S_::LUT + (GEMV_WARPS - gap_warps) * RING_BYTES;
     float* part = reinterpret_cast<float*>(smem + part_off);
     const uint32_t part_s = base_s + part_off;
     const uint32_t xs_off = part_off + S_::PART_BYTES;
@@ -548,8 +654,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         i_full = row0 + ROWS <= P.N;
         i_rstep = P.nb * (uint32_t)QS_BYTES * 8u;
         iq = P.qs + ((size_t)(row0 + g) * P.nb + ic.blk) * QS_BYTES + t * 16;
-        isp = P.sc + ((size_t)(row0 + lane) * P.nb + ic.blk) * SC_BYTES;
-        i_scend = P.sc + (size_t)P.N * P.nb * SC_BYTES;
+        isp = P.sc + ((size_t)(row0 + lane) * P.nb + ic.blk) * SC_B;
+        i_scend = P.sc + (size_t)P.N * P.nb * SC_B;
     };
     if (LEAN && ic.tb < tb1) iss_tile();
     int islot = 0;
@@ -564,11 +670,21 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 for (int c = 0; c < ROWS * 4 / 32; ++c)
                     cp_async_16(st_s + c * 512 + lane_off, iq + (size_t)((uint32_t)c * i_rstep), 16u);
                 if (lane < ROWS) {
-                    // the 4-byte aligned word holding this row's d (the buffer is 4-byte aligned);
-                    // at the end of the buffer only the bytes that exist are read
+                    // the 4-byte aligned word holding this row's d (the buffer is 4-byte aligned;
+                    // IQ2_XS: the three words holding d and the 8 scale bytes); at the end of the
+                    // buffer only the bytes that exist are read
                     const uint8_t* ea = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(isp) & ~(uintptr_t)3);
                     const size_t rem = (size_t)(i_scend - ea);
-                    cp_async_4(st_s + STAGE_QS + lane * 4, ea, rem < 4 ? (uint32_t)rem : 4u);
+                    if constexpr (FMT == 1) {
+#pragma unroll
+                        for (uint32_t w = 0; w < 3; ++w) {
+                            const size_t r4 = rem > 4 * w ? rem - 4 * w : 0;
+                            cp_async_4(st_s + STAGE_QS + lane * 16 + 4 * w, r4 ? ea + 4 * w : ea,
+                                       r4 < 4 ? (uint32_t)r4 : 4u);
+                        }
+                    } else {
+                        cp_async_4(st_s + STAGE_QS + lane * 4, ea, rem < 4 ? (uint32_t)rem : 4u);
+                    }
                 }
             } else {
                 const GemvProblem& P = L.prob[ic.p];
@@ -590,15 +706,24 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 if (lane < ROWS) {
                     const uint32_t row = row0 + lane;
                     const bool ok = row < P.N;
-                    const size_t e = ((size_t)row * P.nb + ic.blk) * SC_BYTES;
-                    const size_t ea = e & ~(size_t)3, total = (size_t)P.N * P.nb * SC_BYTES;
-                    const uint32_t nbytes = ok ? (uint32_t)min((size_t)4, total - ea) : 0u;
-                    cp_async_4(st_s + STAGE_QS + lane * 4, P.sc + (ok ? ea : 0), nbytes);
+                    const size_t e = ((size_t)row * P.nb + ic.blk) * SC_B;
+                    const size_t ea = e & ~(size_t)3, total = (size_t)P.N * P.nb * SC_B;
+                    if constexpr (FMT == 1) {
+#pragma unroll
+                        for (uint32_t w = 0; w < 3; ++w) {
+                            const size_t at = ea + 4 * w;
+                            const uint32_t nbytes = ok && at < total ? (uint32_t)min((size_t)4, total - at) : 0u;
+                            cp_async_4(st_s + STAGE_QS + lane * 16 + 4 * w, P.sc + (nbytes ? at : 0), nbytes);
+                        }
+                    } else {
+                        const uint32_t nbytes = ok ? (uint32_t)min((size_t)4, total - ea) : 0u;
+                        cp_async_4(st_s + STAGE_QS + lane * 4, P.sc + (ok ? ea : 0), nbytes);
+                    }
                 }
             }
             ++ic.tb;
             iq += QS_BYTES;
-            isp += SC_BYTES;
+            isp += SC_B;
             if (++ic.blk == i_nb) {
                 ic.blk = 0;
                 if (++ic.rg == i_tiles) {
@@ -621,7 +746,34 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
 
     // ---- the decode table, built from the 1.5 KB compact copy: row e = 32 copies (one per lane)
     // ---- of the grid selector of code e, then (e < 128) 32 copies of the sign selector of index e
-    {
+    if constexpr (FMT == 1) {
+        // IQ2_XS: row e < 512 = 32 copies of the grid selector of grid entry e (nibble j: the
+        // magnitude code of weight j), then row 512 + e (e < 128) = 32 copies of the sign selector
+        // of sign index e (IQ2_XS uses IQ2_XXS's sign table)
+        constexpr int PER_THREAD = LUT_BYTES_XS / 16 / (GEMV_WARPS * 32);
+        uint32_t v[PER_THREAD];
+#pragma unroll
+        for (int i = 0; i < PER_THREAD; ++i) {
+            const int row = (threadIdx.x + i * GEMV_WARPS * 32) >> 3;  // 8 x 16 bytes per row
+            if (row < 512) {
+                const uint64_t gw = IQ2XS_GRID[row];
+                uint32_t sel = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t b = (uint32_t)(gw >> (8 * j)) & 0xFFu;
+                    sel |= (b == 8u ? 0u : (b == 25u ? 1u : 2u)) << (4 * j);
+                }
+                v[i] = sel;
+            } else {
+                v[i] = __ldg(IQ2XXS_SEL_COMPACT + 256 + (row - 512));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < PER_THREAD; ++i) {
+            const int c = threadIdx.x + i * GEMV_WARPS * 32;
+            *reinterpret_cast<uint4*>(smem + gap + c * 16) = make_uint4(v[i], v[i], v[i], v[i]);
+        }
+    } else {
         constexpr int PER_THREAD = LUT_BYTES / 16 / (GEMV_WARPS * 32);
         uint32_t v[PER_THREAD];  // all loads first: one latency, not one per store
 #pragma unroll
@@ -724,6 +876,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     dk.gsel = 0x7604u | ((uint32_t)t << 4);
     dk.rot = (7u * t + 24u) & 31u;
     dk.soff = lut_s | 128u | ((uint32_t)lane * 4u);
+    dk.xsel = (2u * t) | ((2u * t + 1u) << 4) | ((2u * t) << 8) | ((2u * t + 1u) << 12);
+    dk.gbase = lut_s | ((uint32_t)lane * 4u);
+    dk.sbase = (lut_s + 65536u) | ((uint32_t)lane * 4u);
     const uint32_t swz = (uint32_t)((g >> 1) & 3);  // rows g, g+8, g+16, g+24 share it
     const uint32_t rowbase = (uint32_t)g * 64u;     // rows tt*16+g (+8): rowbase + tt*1024 (+512)
 
@@ -764,10 +919,20 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         int I[T][NT][4];
         const uint8_t* xbp = FUSED ? nullptr : c_xb + (size_t)(cc.blk * (8u * NT * 256u));
         const uint32_t xsp = xs_s + cc.blk * 8 * NT * 256 + lane * 8;
-        if (s_lo == 0 && s_hi == 8)
+        if constexpr (FMT == 1) {
+            // the row's 12 scale bytes start at its 16-byte slot; d is at byte 2 * parity, the
+            // sub-block scale bytes after it (the parity of row * nb + blk, as for the d word)
+            const uint32_t so = (((cc.blk & 1u) ^ c_dpar) ? 4u : 2u);
+            const uint32_t sc_s = st_s + STAGE_QS + (uint32_t)g * 16u + so;
+            if (s_lo == 0 && s_hi == 8)
+                stage_compute_xs<NT, T, false, S_::SPLIT>(dk, st_s, xbp, s_lo, s_hi, rowbase, swz, sc_s, t < 2, I);
+            else
+                stage_compute_xs<NT, T, true, S_::SPLIT>(dk, st_s, xbp, s_lo, s_hi, rowbase, swz, sc_s, t < 2, I);
+        } else if (s_lo == 0 && s_hi == 8) {
             stage_compute<NT, T, false, FUSED, S_::SPLIT>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
-        else
+        } else {
             stage_compute<NT, T, true, FUSED, S_::SPLIT>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
+        }
 
         // Block epilogue: s32 -> f32 with d (per row) and the limb scale (per column).
         {
@@ -782,8 +947,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
 #pragma unroll
             for (int tt = 0; tt < T; ++tt) {
                 const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
-                const uint32_t w0 = ld_shared_u32_volatile(st_s + STAGE_QS + r0 * 4);
-                const uint32_t w1 = ld_shared_u32_volatile(st_s + STAGE_QS + r1 * 4);
+                constexpr uint32_t SLOT = FMT == 1 ? 16u : 4u;  // scale bytes per row in the stage
+                const uint32_t w0 = ld_shared_u32_volatile(st_s + STAGE_QS + r0 * SLOT);
+                const uint32_t w1 = ld_shared_u32_volatile(st_s + STAGE_QS + r1 * SLOT);
                 const float d0 = half_bits_to_float(prmt(w0, 0u, dsel));
                 const float d1 = half_bits_to_float(prmt(w1, 0u, dsel));
 #pragma unroll
@@ -1023,12 +1189,20 @@ struct GroupPlan {
     size_t smem;
 };
 
-template <int NT, int LB = 4>
+template <int NT, int LB = 4, int FMT = 0>
 size_t smem_for(bool fused, uint32_t nb) {
-    return GemvShape<NT, LB>::SMEM + (fused ? xs_bytes(nb, NT) + cs_bytes(nb, NT) : 0);
+    return GemvShape<NT, LB, FMT>::SMEM + (fused ? xs_bytes(nb, NT) + cs_bytes(nb, NT) : 0);
 }
 
-size_t smem_for_nt(int nt, int limbs, bool fused, uint32_t nb) {
+size_t smem_for_nt(int nt, int limbs, bool fused, uint32_t nb, int fmt = 0) {
+    if (fmt == 1) {  // IQ2_XS: x limbs always from the prep kernel
+        switch (nt) {
+            case 1: return smem_for<1, 4, 1>(false, nb);
+            case 2: return limbs == 4 ? smem_for<2, 4, 1>(false, nb) : smem_for<2, 16, 1>(false, nb);
+            case 4: return smem_for<4, 16, 1>(false, nb);
+            default: return smem_for<8, 16, 1>(false, nb);
+        }
+    }
     if (limbs == 1) {
         switch (nt) {
             case 1: return smem_for<1, 1>(fused, nb);
@@ -1078,7 +1252,9 @@ int max_active_clusters(int num_sms) {
 
 // max_cl: clusters the device can run at once (0 when only the workspace size is wanted).
 // w8a8: the activations as the W8A8 mode's int8 (one limb, m <= 32).
-GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int max_cl, bool w8a8 = false) {
+// fmt: the weight format (0 IQ2_XXS, 1 IQ2_XS; IQ2_XS never makes its x limbs in the GEMV).
+GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int max_cl, bool w8a8 = false,
+                     int fmt = 0) {
     GroupPlan pl;
     pl.nt = w8a8 ? nt_w8a8(m) : nt_for(m);
     pl.rows = w8a8 ? (pl.nt == 1 ? 32 : 16) : rows_for(m);
@@ -1101,8 +1277,9 @@ GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, i
         pl.x_of.push_back(xi);
     }
     // one projection whose limbs fit in shared memory: the GEMV makes them itself
-    pl.fused = !w8a8 && count == 1 && pl.nt <= 2 && smem_for_nt(pl.nt, pl.limbs, true, pl.nb[0]) <= (size_t)SMEM_LIMIT;
-    pl.smem = smem_for_nt(pl.nt, pl.limbs, pl.fused, count ? pl.nb[0] : 0);
+    pl.fused = fmt == 0 && !w8a8 && count == 1 && pl.nt <= 2 &&
+               smem_for_nt(pl.nt, pl.limbs, true, pl.nb[0]) <= (size_t)SMEM_LIMIT;
+    pl.smem = smem_for_nt(pl.nt, pl.limbs, pl.fused, count ? pl.nb[0] : 0, fmt);
     // clusters: whole tiles, about equal numbers of tile-blocks each
     uint64_t cl = (uint64_t)(max_cl > 0 ? max_cl : 1);
     if (cl > MAX_CLUSTERS) cl = MAX_CLUSTERS;
@@ -1145,14 +1322,14 @@ GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, i
     return pl;
 }
 
-template <int NT, int CAP, int XDT, bool P2P, int LB>
+template <int NT, int CAP, int XDT, bool P2P, int LB, int FMT = 0>
 cudaError_t launch_gemv_kernel(const GemvLaunch<CAP>& L, const GroupPlan& pl, cudaStream_t stream) {
     static bool attr_set[64] = {};  // per device; an idempotent attribute, so a race is benign
     int dev = 0;
     cudaGetDevice(&dev);
     cudaError_t e;
     if (dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemv_kernel<NT, CAP, XDT, P2P, LB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(gemv_kernel<NT, CAP, XDT, P2P, LB, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  SMEM_LIMIT);
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set[dev] = true;
@@ -1171,16 +1348,21 @@ cudaError_t launch_gemv_kernel(const GemvLaunch<CAP>& L, const GroupPlan& pl, cu
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<NT, CAP, XDT, P2P, LB>, L);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<NT, CAP, XDT, P2P, LB, FMT>, L);
 }
 
-template <int NT, int CAP, int XDT, int LB = 4>
+template <int NT, int CAP, int XDT, int LB = 4, int FMT = 0>
 cudaError_t launch_gemv_kernel_p(const GemvLaunch<CAP>& L, const GroupPlan& pl, bool p2p, cudaStream_t stream) {
-    return p2p ? launch_gemv_kernel<NT, CAP, XDT, true, LB>(L, pl, stream)
-               : launch_gemv_kernel<NT, CAP, XDT, false, LB>(L, pl, stream);
+    if constexpr (FMT == 1) {
+        (void)p2p;  // (the sharded calls are IQ2_XXS only)
+        return launch_gemv_kernel<NT, CAP, XDT, false, LB, 1>(L, pl, stream);
+    } else {
+        return p2p ? launch_gemv_kernel<NT, CAP, XDT, true, LB>(L, pl, stream)
+                   : launch_gemv_kernel<NT, CAP, XDT, false, LB>(L, pl, stream);
+    }
 }
 
-template <int NT, int CAP, int LB = 4>
+template <int NT, int CAP, int LB = 4, int FMT = 0>
 cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint32_t m, int x_dtype,
                              uint8_t* ws, const GroupPlan& pl, cudaStream_t stream, const GemvPeers* peers) {
     cudaError_t e;
@@ -1252,8 +1434,8 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
     }
     const bool p2p = peers != nullptr;
     if (p2p) L.peers = *peers;
-    if (!pl.fused) e = launch_gemv_kernel_p<NT, CAP, -1, LB>(L, pl, p2p, stream);
-    else if constexpr (NT <= 2 && CAP == 1 && (LB == 4 || LB == 16)) {
+    if (!pl.fused) e = launch_gemv_kernel_p<NT, CAP, -1, LB, FMT>(L, pl, p2p, stream);
+    else if constexpr (FMT == 0 && NT <= 2 && CAP == 1 && (LB == 4 || LB == 16)) {
         switch (x_dtype) {
             case 0: e = launch_gemv_kernel_p<NT, CAP, 0, LB>(L, pl, p2p, stream); break;
             case 1: e = launch_gemv_kernel_p<NT, CAP, 1, LB>(L, pl, p2p, stream); break;
@@ -1341,6 +1523,26 @@ cudaError_t launch_gemv(const void* x, int x_dtype, uint32_t m, const uint8_t* q
                         cudaStream_t stream) {
     GemvProblemHost p{x, qs, sc, n, k, out};
     return launch_gemv_group(&p, 1, m, x_dtype, workspace, num_sms, stream);
+}
+
+size_t gemv_xs_workspace_size(uint32_t m, uint32_t n, uint32_t k) {
+    GemvProblemHost p{nullptr, nullptr, nullptr, n, k, nullptr};
+    return plan_group(&p, 1, m, 0, false, 1).total;
+}
+
+cudaError_t launch_gemv_xs(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
+                           uint32_t n, uint32_t k, float* out, void* workspace, int num_sms, cudaStream_t stream) {
+    GemvProblemHost p{x, qs, sc, n, k, out};
+    const GroupPlan pl = plan_group(&p, 1, m, max_active_clusters(num_sms), false, 1);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    switch (pl.nt) {
+        case 1: return launch_group_cap<1, 1, 4, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
+        case 2:
+            return pl.limbs == 4 ? launch_group_cap<2, 1, 4, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr)
+                                 : launch_group_cap<2, 1, 16, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
+        case 4: return launch_group_cap<4, 1, 16, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
+        default: return launch_group_cap<8, 1, 16, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
+    }
 }
 
 cudaError_t launch_gemv_generic(const void* x, int x_dtype, uint32_t m, const uint8_t* qs,
