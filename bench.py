@@ -941,10 +941,10 @@ def run_case(args):
     command the profiler captures. gemv: 4096x14336 (K x N) at M=1, f32 x, two weight copies
     (30 MB) in turn; gemm: M=2048 (or `--m` M > 32) on the same projection, bf16 x; grouped: the
     benchmark step (every projection of `--layers` layers in one iq2_matmul_grouped call, M=1);
-    variant: the IQ2_XS matmul on the gemv shape (random blocks, d ~U[1e-3, 1e-2]), M=1, f32 x, or
-    with `--m` M > 32 its tcgen05 GEMM at that M, bf16 x."""
+    variant: the `--variant` format's matmul on the gemv shape (random blocks, d ~U[1e-3, 1e-2]) at
+    `--m` M <= 32 with f32 x (the decode kernel), or M > 32 with bf16 x (the tcgen05 GEMM)."""
     import candelora_metal_kernels_b200 as c
-    from candelora_metal_kernels_b200 import synth
+    from candelora_metal_kernels_b200 import gguf, synth
     torch.cuda.set_device(0)
     if args.case == "grouped":
         wl = Workload(1, args.layers, 0, 1, torch.device("cuda", 0))
@@ -963,29 +963,31 @@ def run_case(args):
         return
     k, n = (int(v) for v in args.kn.split(","))
     if args.case == "variant":
+        var = {"iq2_xs": c.Iq2MatmulVariant.Iq2Xs, "iq2_s": c.Iq2MatmulVariant.Iq2S,
+               "iq3_s": c.Iq2MatmulVariant.Iq3S}[args.variant]
+        bpb, spb = gguf.SPLIT[var]
         nb = k // 256
         g = torch.Generator(device="cuda")
         g.manual_seed(1)
-        wb = torch.randint(0, 256, (n * nb * 64,), dtype=torch.uint8, device="cuda", generator=g)
-        sc = torch.randint(0, 256, (n * nb, 10), dtype=torch.uint8, device="cuda", generator=g)
+        wb = torch.randint(0, 256, (n * nb * bpb,), dtype=torch.uint8, device="cuda", generator=g)
+        sc = torch.randint(0, 256, (n * nb, spb), dtype=torch.uint8, device="cuda", generator=g)
         sc[:, :2] = (torch.rand(n * nb, device="cuda", generator=g) * 9e-3 + 1e-3).to(torch.float16).view(
             torch.uint8).view(-1, 2)
         sc = sc.reshape(-1)
-        vm = args.m if args.m > 32 else 1  # (m > 32: the tcgen05 GEMM, bf16 x)
-        x = synth.activations(vm, k, seed=1, dtype=torch.bfloat16 if vm > 1 else torch.float32, device="cuda")
+        vm = args.m  # (m > 32: the tcgen05 GEMM, bf16 x; else the decode kernel, f32 x)
+        x = synth.activations(vm, k, seed=1, dtype=torch.bfloat16 if vm > 32 else torch.float32, device="cuda")
         out = torch.empty(vm, n, device="cuda")
-        vws = torch.empty(max(1, c.workspace_bytes(vm, n, k, x.dtype, c.Iq2MatmulVariant.Iq2Xs)), dtype=torch.uint8,
-                          device="cuda")
+        vws = torch.empty(max(1, c.workspace_bytes(vm, n, k, x.dtype, var)), dtype=torch.uint8, device="cuda")
         for _ in range(2):
-            c.iq2_matmul(x, wb, sc, n, k, c.Iq2MatmulVariant.Iq2Xs, out=out, workspace=vws)
+            c.iq2_matmul(x, wb, sc, n, k, var, out=out, workspace=vws)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
-            c.iq2_matmul(x, wb, sc, n, k, c.Iq2MatmulVariant.Iq2Xs, out=out, workspace=vws)
+            c.iq2_matmul(x, wb, sc, n, k, var, out=out, workspace=vws)
         e1.record()
         e1.synchronize()
-        print(json.dumps({"case": "variant", "m": vm, "k": k, "n": n, "calls": args.steps,
+        print(json.dumps({"case": "variant", "variant": args.variant, "m": vm, "k": k, "n": n, "calls": args.steps,
                           "us_per_call": round(e0.elapsed_time(e1) * 1e3 / args.steps, 2)}), flush=True)
         return
     m = 1 if args.case == "gemv" else (args.m if args.m > 32 else 2048)
@@ -1028,6 +1030,8 @@ def main():
     ap.add_argument("--case", choices=["gemv", "gemm", "grouped", "variant"], default=None,
                     help="run only the dominant kernel's shape (the profiler's small case) and exit")
     ap.add_argument("--kn", default="4096,14336", help="--case gemv/gemm/variant: K,N of the projection")
+    ap.add_argument("--variant", choices=["iq2_xs", "iq2_s", "iq3_s"], default="iq2_xs",
+                    help="--case variant: the weight format")
     args = ap.parse_args()
     if args.case:
         run_case(args)

@@ -56,6 +56,8 @@ constexpr int CLUSTER = 2;
 constexpr int LUT_BYTES = 256 * 256;      // 256 rows x (32 lanes grid selectors | 32 lanes sign)
 // IQ2_XS: 512 grid rows x 32 lanes (64 KB), then 128 sign rows x 32 lanes
 constexpr int LUT_BYTES_XS = 512 * 128 + 128 * 128;
+// IQ2_S: 1024 grid rows x 16 lane copies (64 KB), then 256 sign rows x 16 lane copies
+constexpr int LUT_BYTES_S = 1024 * 64 + 256 * 64;
 constexpr int MAX_PROBLEMS = 256;         // per grouped launch
 constexpr int MAX_CLUSTERS = 96;          // >= SMs / 2 of the device (74 on B200)
 constexpr int SMEM_LIMIT = 227 * 1024;
@@ -65,24 +67,29 @@ constexpr int SMEM_LIMIT = 227 * 1024;
 // tiles [NT/2, NT) the same tokens' unsigned low bytes); 1: the int8 activations of the W8A8
 // mode, eight tokens per n8 tile.
 // FMT: the weight format, 0 IQ2_XXS, 1 IQ2_XS (its 512-entry grid needs an 80 KB table, its
-// scales a 16-byte word per row and stage).
+// scales a 16-byte slot per row and stage), 2 IQ2_S (1024-entry grid and its 256-entry sign table
+// at 16 copies, 80 KB; per row and stage the 16-byte aligned 80-byte window around the row's
+// 72-byte block, then a 12-byte scale slot).
 template <int NT, int LB = 4, int FMT = 0>
 struct GemvShape {
     static constexpr bool SPLIT = LB == 16;
-    static constexpr int LUT = FMT == 1 ? LUT_BYTES_XS : LUT_BYTES;
+    static constexpr int LUT = FMT == 2 ? LUT_BYTES_S : (FMT == 1 ? LUT_BYTES_XS : LUT_BYTES);
+    static constexpr int SLOT = FMT == 0 ? 4 : (FMT == 1 ? 16 : 12);  // per row: the scales
+    static constexpr int QROW = FMT == 2 ? 80 : 64;                    // per row: the packed bytes
     static constexpr int T = ((NT <= 2 && LB != 1) || (NT == 1 && LB == 1)) ? 2 : 1;  // 16-row mma tiles per warp
     static constexpr int ROWS = 16 * T;                // rows of a tile
     static constexpr int TPN = SPLIT ? 8 : 8 / LB;     // tokens per n8 tile (SPLIT: per high-byte tile)
     static constexpr int TOK = SPLIT ? 4 * NT : TPN * NT;  // tokens incl. the zero padding
-    static constexpr int STAGE_QS = ROWS * 64;         // one block of qs per row
-    // + per row the aligned scale word (IQ2_XS: the 12 aligned bytes holding d and the 8 scale bytes)
-    static constexpr int STAGE_BYTES = STAGE_QS + ROWS * (FMT == 1 ? 16 : 4);
+    static constexpr int STAGE_QS = ROWS * QROW;       // one block of qs per row
+    // + per row the aligned scale word (IQ2_XS, IQ2_S: the 12 aligned bytes holding d and the 8
+    // scale bytes)
+    static constexpr int STAGE_BYTES = STAGE_QS + ROWS * SLOT;
     // fewer stages where the partials (TOK x ROWS per warp slot) are large
     static constexpr int NSTAGES0 = T == 2 ? 3 : ((LB == 4 || (LB == 1 && NT <= 2) || (SPLIT && NT <= 4)) ? 6 : 4);
     static constexpr int PART_BYTES = GEMV_WARPS * 2 * TOK * ROWS * 4;  // [warp][first|last][token][row]
-    // IQ2_XS: as many as fit beside its larger table (2..5)
+    // IQ2_XS, IQ2_S: as many as fit beside the larger table (2..5)
     static constexpr int NS_FIT = (SMEM_LIMIT - LUT - PART_BYTES) / ((GEMV_WARPS + 1) * STAGE_BYTES);
-    static constexpr int NSTAGES = FMT == 1 ? (NS_FIT < NSTAGES0 ? NS_FIT : NSTAGES0) : NSTAGES0;
+    static constexpr int NSTAGES = FMT != 0 ? (NS_FIT < NSTAGES0 ? NS_FIT : NSTAGES0) : NSTAGES0;
     static_assert(NSTAGES >= 2, "stages");
     static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;  // per warp
     // The table sits at the first 64 KB-aligned shared address of the block's window and the
@@ -349,6 +356,10 @@ struct GemvLaunch {
     uint32_t K, clusters;
     uint32_t cl_tb[MAX_CLUSTERS + 1];       // cluster c owns tile-blocks [cl_tb[c], cl_tb[c+1]) (whole tiles)
     uint16_t cl_p[MAX_CLUSTERS];            // problem of the cluster's first tile
+    // 2, as a value the compiler cannot see: the decode forms each weight scale 2s+1 as one
+    // multiply-add on the FMA pipe instead of a shift and an OR on the integer ALU pipe that
+    // bounds the kernel (3 % on the grouped M=1 launch)
+    uint32_t two;
     GemvPeers peers;                        // peer-memory outputs (P2P launches only)
 };
 
@@ -412,8 +423,14 @@ struct DecodeK {
     uint32_t rot;   // rotate that brings sign index t (bits 7t..7t+6) to bits 8..14
     uint32_t soff;  // base | 128 | lane*4
     // IQ2_XS: prmt selector taking this lane's u16 word t of a sub-block to bits 0..15, and the
-    // grid / sign tables' bases | lane*4 (both 64 KB-aligned, rows of 128 bytes)
+    // grid / sign tables' bases | lane*4 (both 64 KB-aligned, rows of 128 bytes).
+    // IQ2_S: xsel = {byte t, 0, 0, 0}; sbase = sign table | (lane % 16) * 4 (rows of 64 bytes);
+    // gsel2 = {qa.b0, low byte t, qa.b2, qa.b3} for the grid address word (+1: qa.b1); qsh the
+    // shift taking qh bits 2t, 2t+1 of every byte to bits 6, 7; qfill = (lane % 16) * 4 in
+    // every byte; lutw the table base (its bytes 2, 3)
     uint32_t xsel, gbase, sbase;
+    uint32_t gsel2, qsh, qfill, lutw;
+    uint32_t two;  // GemvLaunch::two
 };
 
 // Four signed int8 weights of one 8-weight group (sub-block word {aux_g, aux_s}) for this
@@ -439,30 +456,81 @@ __device__ __forceinline__ void decode_group_xs(const DecodeK& k, uint32_t lo32,
     hi = prmt(KPOS, KNEG, sel >> 16);
 }
 
+// IQ2_S: four signed int8 weights of one 8-weight group for this lane's group t of a sub-block
+// (lows: its 4 grid low bytes, signs: its 4 sign bytes). The grid row of entry low | qh2 << 8
+// sits at low * 256 + qh2 * 64 of the table, so its address is one permute of the low byte
+// and qa = {(qh2 of sub-blocks 2j, 2j+1) << 6 | (lane % 16) * 4, same, table base bytes 2, 3};
+// h picks the sub-block (qa.b0 or qa.b1; a constant after unrolling).
+__device__ __forceinline__ void decode_group_s(const DecodeK& k, uint32_t lows, uint32_t signs, uint32_t qa,
+                                               uint32_t h, uint32_t& lo, uint32_t& hi) {
+    const uint32_t ga = prmt(lows, qa, k.gsel2 + h);
+    const uint32_t sa = prmt(signs, 0u, k.xsel) * 64u + k.sbase;
+    const uint32_t sel = ld_shared_const(ga) | ld_shared_const(sa);
+    lo = prmt(KPOS, KNEG, sel);
+    hi = prmt(KPOS, KNEG, sel >> 16);
+}
+
 __device__ __forceinline__ uint32_t ld_shared_u8_volatile(uint32_t addr) {
     uint32_t v;
     asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(addr));
     return v;
 }
 
-// IQ2_XS stage: as stage_compute, but the scale changes every 16 weights (groups 0-1: the low
-// nibble of the sub-block's scale byte, groups 2-3: the high one). Lane t holds group t's weights,
-// i.e. MMA k-chunks 4t.. and 16+4t.., so two MMAs whose x fragments are zero on lanes t >= 2
-// (resp. t < 2) give the two halves' sums, each scaled by its 2s+1. sc_s: this stage's scale
-// bytes of row g (row r at + (r - g) * 16).
-template <int NT, int T, bool PARTIAL, bool SPLIT>
+// IQ2_XS / IQ2_S stage: as stage_compute, but the scale changes every 16 weights (groups 0-1:
+// the low nibble of the sub-block's scale byte, groups 2-3: the high one). Lane t holds group t's
+// weights, i.e. MMA k-chunks 4t.. and 16+4t.., so two MMAs whose x fragments are zero on lanes
+// t >= 2 (resp. t < 2) give the two halves' sums, each scaled by its 2s+1. slot_s: this stage's
+// slot of row g (row r at + (r - g) * SLOT); so: the offset of the first scale byte in it.
+// IQ2_S: rowbase is row g's block in the stage (its 80-byte window + 0 or 8; row r at
+// + (r - g) * 80): grid low bytes of sub-block sb at + 4 sb, sign bytes at + 32 + 4 sb, qh at + 64.
+template <int NT, int T, bool PARTIAL, bool SPLIT, int FMT, int SLOT>
 __device__ __forceinline__ void stage_compute_xs(const DecodeK& dk, uint32_t st_s, const uint8_t* xbp, uint32_t s_lo,
-                                                 uint32_t s_hi, uint32_t rowbase, uint32_t swz, uint32_t sc_s,
-                                                 bool low_lane, int (&I)[T][NT][4]) {
+                                                 uint32_t s_hi, uint32_t rowbase, uint32_t swz, uint32_t slot_s,
+                                                 uint32_t so, bool low_lane, int (&I)[T][NT][4]) {
+    const uint32_t sc_s = slot_s + so;
+    // IQ2_S: per row (tt, half) the qh words of sub-blocks 0-3 / 4-7, this lane's two bits of
+    // every byte at bits 6, 7 and (lane % 16) * 4 below them
+    uint32_t qx[T][2], qy[T][2];
+    if constexpr (FMT == 2) {
+#pragma unroll
+        for (int tt = 0; tt < T; ++tt)
+#pragma unroll
+            for (int hr = 0; hr < 2; ++hr) {
+                const uint2 q = ld_shared_v2_volatile(st_s + rowbase + (uint32_t)((tt * 16 + hr * 8) * 80) + 64u);
+                qx[tt][hr] = ((q.x << dk.qsh) & 0xC0C0C0C0u) | dk.qfill;
+                qy[tt][hr] = ((q.y << dk.qsh) & 0xC0C0C0C0u) | dk.qfill;
+            }
+    }
 #pragma unroll
     for (int pair = 0; pair < 4; ++pair) {
-        const uint32_t a0 = st_s + rowbase + (((uint32_t)pair ^ swz) << 4);
+        // qw[tt][half]: IQ2_XS: the 16-byte chunk of sub-blocks 2 pair, 2 pair + 1; IQ2_S: their
+        // {lows, lows, signs, signs}
         uint4 qw[T][2];
-        qw[0][0] = ld_shared_v4<0>(a0);
-        qw[0][1] = ld_shared_v4<512>(a0);
-        if (T == 2) {
-            qw[T - 1][0] = ld_shared_v4<1024>(a0);
-            qw[T - 1][1] = ld_shared_v4<1536>(a0);
+        if constexpr (FMT == 2) {
+#pragma unroll
+            for (int tt = 0; tt < T; ++tt)
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const uint32_t ra = st_s + rowbase + (uint32_t)((tt * 16 + hr * 8) * 80 + 8 * pair);
+                    const uint2 l = ld_shared_v2_volatile(ra), sg = ld_shared_v2_volatile(ra + 32u);
+                    qw[tt][hr] = make_uint4(l.x, l.y, sg.x, sg.y);
+                }
+        } else {
+            const uint32_t a0 = st_s + rowbase + (((uint32_t)pair ^ swz) << 4);
+            qw[0][0] = ld_shared_v4<0>(a0);
+            qw[0][1] = ld_shared_v4<512>(a0);
+            if (T == 2) {
+                qw[T - 1][0] = ld_shared_v4<1024>(a0);
+                qw[T - 1][1] = ld_shared_v4<1536>(a0);
+            }
+        }
+        uint32_t qa[T][2];  // IQ2_S: the grid address words of this pair's sub-blocks
+        if constexpr (FMT == 2) {
+#pragma unroll
+            for (int tt = 0; tt < T; ++tt)
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr)
+                    qa[tt][hr] = prmt(pair < 2 ? qx[tt][hr] : qy[tt][hr], dk.lutw, (pair & 1) ? 0x7632u : 0x7610u);
         }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -479,15 +547,22 @@ __device__ __forceinline__ void stage_compute_xs(const DecodeK& dk, uint32_t st_
             }
 #pragma unroll
             for (int tt = 0; tt < T; ++tt) {
-                const uint32_t l0 = h ? qw[tt][0].z : qw[tt][0].x, h0 = h ? qw[tt][0].w : qw[tt][0].y;
-                const uint32_t l1 = h ? qw[tt][1].z : qw[tt][1].x, h1 = h ? qw[tt][1].w : qw[tt][1].y;
                 uint32_t w0, w1, w2, w3;
-                decode_group_xs(dk, l0, h0, w0, w2);
-                decode_group_xs(dk, l1, h1, w1, w3);
-                const uint32_t b0 = ld_shared_u8_volatile(sc_s + (uint32_t)tt * 256u + sb);
-                const uint32_t b1 = ld_shared_u8_volatile(sc_s + (uint32_t)tt * 256u + 128u + sb);
-                const int ca0 = (int)(((b0 & 15u) << 1) | 1u), cb0 = (int)(((b0 >> 4) << 1) | 1u);
-                const int ca1 = (int)(((b1 & 15u) << 1) | 1u), cb1 = (int)(((b1 >> 4) << 1) | 1u);
+                if constexpr (FMT == 2) {
+                    const uint32_t l0 = h ? qw[tt][0].y : qw[tt][0].x, s0 = h ? qw[tt][0].w : qw[tt][0].z;
+                    const uint32_t l1 = h ? qw[tt][1].y : qw[tt][1].x, s1 = h ? qw[tt][1].w : qw[tt][1].z;
+                    decode_group_s(dk, l0, s0, qa[tt][0], (uint32_t)h, w0, w2);
+                    decode_group_s(dk, l1, s1, qa[tt][1], (uint32_t)h, w1, w3);
+                } else {
+                    const uint32_t l0 = h ? qw[tt][0].z : qw[tt][0].x, h0 = h ? qw[tt][0].w : qw[tt][0].y;
+                    const uint32_t l1 = h ? qw[tt][1].z : qw[tt][1].x, h1 = h ? qw[tt][1].w : qw[tt][1].y;
+                    decode_group_xs(dk, l0, h0, w0, w2);
+                    decode_group_xs(dk, l1, h1, w1, w3);
+                }
+                const uint32_t b0 = ld_shared_u8_volatile(sc_s + (uint32_t)(tt * 16 * SLOT) + sb);
+                const uint32_t b1 = ld_shared_u8_volatile(sc_s + (uint32_t)((tt * 16 + 8) * SLOT) + sb);
+                const int ca0 = (int)((b0 & 15u) * dk.two + 1u), cb0 = (int)((b0 >> 4) * dk.two + 1u);
+                const int ca1 = (int)((b1 & 15u) * dk.two + 1u), cb1 = (int)((b1 >> 4) * dk.two + 1u);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     int d1[4], d2[4];
@@ -556,7 +631,7 @@ __device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, 
                 uint32_t w0, w1, w2, w3;
                 decode_group(dk, g0, s0, w0, w2);
                 decode_group(dk, g1, s1, w1, w3);
-                const int c0 = (int)((s0 >> 27) | 1u), c1 = (int)((s1 >> 27) | 1u);
+                const int c0 = (int)((s0 >> 28) * dk.two + 1u), c1 = (int)((s1 >> 28) * dk.two + 1u);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     int d[4];
@@ -586,8 +661,10 @@ __device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, 
 template <int NT, int CAP, int XDT, bool P2P = false, int LB = 4, int FMT = 0>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvLaunch<CAP> L) {
     using S_ = GemvShape<NT, LB, FMT>;
-    static_assert(FMT == 0 || (!P2P && (LB == 4 || LB == 16)), "IQ2_XS: the plain decode GEMV only");
-    constexpr uint32_t SC_B = FMT == 1 ? 10u : (uint32_t)SC_BYTES;  // scale bytes per block
+    static_assert(FMT == 0 || (!P2P && (LB == 4 || LB == 16)), "IQ2_XS, IQ2_S: the plain decode GEMV only");
+    constexpr uint32_t SC_B = FMT != 0 ? 10u : (uint32_t)SC_BYTES;  // scale bytes per block
+    constexpr uint32_t QB = FMT == 2 ? 72u : (uint32_t)QS_BYTES;   // packed bytes per block
+    constexpr uint32_t SLOT = (uint32_t)S_::SLOT;
     constexpr bool FUSED = XDT >= 0;
     constexpr int T = S_::T, ROWS = S_::ROWS, TOK = S_::TOK, STAGE_QS = S_::STAGE_QS;
     constexpr int STAGE_BYTES = S_::STAGE_BYTES, NSTAGES = S_::NSTAGES, RING_BYTES = S_::RING_BYTES;
@@ -631,7 +708,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
 
     // ---- issue side: cp.async stages of one tile-block each, NSTAGES ahead ----
     // State of the issue cursor: this lane's 16-byte chunk t of row g (iq; rows g+8c at
-    // iq + c*i_rstep) and the scale of row `lane` (isp). With up to four n8 tiles it is set up
+    // iq + c*i_rstep; IQ2_S: the block of row lane % ROWS) and the scale of row `lane` (isp). With up to four n8 tiles it is set up
     // once per tile (iss_tile) and advanced by one block per stage, so that a stage costs no
     // 64-bit index arithmetic (+4..7 % at m <= 8); the eight-tile kernels have no registers to
     // keep it across the loop and recompute it per stage.
@@ -652,8 +729,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         i_nb = P.nb;
         i_tiles = P.tiles;
         i_full = row0 + ROWS <= P.N;
-        i_rstep = P.nb * (uint32_t)QS_BYTES * 8u;
-        iq = P.qs + ((size_t)(row0 + g) * P.nb + ic.blk) * QS_BYTES + t * 16;
+        i_rstep = P.nb * QB * 8u;
+        // (IQ2_S: the block of row lane % ROWS)
+        iq = FMT == 2 ? P.qs + ((size_t)(row0 + ((uint32_t)lane & (ROWS - 1))) * P.nb + ic.blk) * QB
+                      : P.qs + ((size_t)(row0 + g) * P.nb + ic.blk) * QB + t * 16;
         isp = P.sc + ((size_t)(row0 + lane) * P.nb + ic.blk) * SC_B;
         i_scend = P.sc + (size_t)P.N * P.nb * SC_B;
     };
@@ -666,20 +745,36 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
             if (ic.tb >= tbf_lo && ic.tb < tbf_hi && i_full) {
                 // the common case: every sub-block and every row of the stage is needed; chunk t
                 // of row r = 8c + g goes to chunk t ^ ((r >> 1) & 3) of the row's 64 bytes
+                if constexpr (FMT == 2) {
+                    // the 16-byte aligned 80-byte window around the row's 72-byte block (which
+                    // starts at byte 0 or 8 of it) in five 16-byte copies; the last one reads
+                    // only bytes of the block
+                    const uint32_t odd = (uint32_t)reinterpret_cast<uintptr_t>(iq) & 8u;
+                    const uint8_t* win = iq - odd;
+                    const uint32_t r = (uint32_t)lane & (ROWS - 1);
 #pragma unroll
-                for (int c = 0; c < ROWS * 4 / 32; ++c)
-                    cp_async_16(st_s + c * 512 + lane_off, iq + (size_t)((uint32_t)c * i_rstep), 16u);
+                    for (int i = 0; i < (ROWS * 5 + 31) / 32; ++i) {
+                        const uint32_t idx = (uint32_t)lane + 32u * i;
+                        if ((ROWS * 5) % 32 != 0 && idx >= (uint32_t)(ROWS * 5)) break;
+                        const uint32_t ch = idx / ROWS;
+                        cp_async_16(st_s + r * 80 + ch * 16, win + ch * 16, (ch == 4 && !odd) ? 8u : 16u);
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < ROWS * 4 / 32; ++c)
+                        cp_async_16(st_s + c * 512 + lane_off, iq + (size_t)((uint32_t)c * i_rstep), 16u);
+                }
                 if (lane < ROWS) {
                     // the 4-byte aligned word holding this row's d (the buffer is 4-byte aligned;
                     // IQ2_XS: the three words holding d and the 8 scale bytes); at the end of the
                     // buffer only the bytes that exist are read
                     const uint8_t* ea = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(isp) & ~(uintptr_t)3);
                     const size_t rem = (size_t)(i_scend - ea);
-                    if constexpr (FMT == 1) {
+                    if constexpr (FMT != 0) {
 #pragma unroll
                         for (uint32_t w = 0; w < 3; ++w) {
                             const size_t r4 = rem > 4 * w ? rem - 4 * w : 0;
-                            cp_async_4(st_s + STAGE_QS + lane * 16 + 4 * w, r4 ? ea + 4 * w : ea,
+                            cp_async_4(st_s + STAGE_QS + lane * SLOT + 4 * w, r4 ? ea + 4 * w : ea,
                                        r4 < 4 ? (uint32_t)r4 : 4u);
                         }
                     } else {
@@ -692,28 +787,45 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 const uint32_t s_lo = ic.tb * 8 < a ? a - ic.tb * 8 : 0u;        // first sub-block needed
                 const uint32_t s_hi = min(8u, b - ic.tb * 8);                     // one past the last
                 const uint32_t ch_lo = s_lo >> 1, ch_hi = (s_hi + 1) >> 1;        // 16-byte chunks needed
-                const uint8_t* qrow = P.qs + ((size_t)row0 * P.nb + ic.blk) * QS_BYTES;
-                const size_t row_bytes = (size_t)P.nb * QS_BYTES;
+                const uint8_t* qrow = P.qs + ((size_t)row0 * P.nb + ic.blk) * QB;
+                const size_t row_bytes = (size_t)P.nb * QB;
+                if constexpr (FMT == 2) {
+                    // rows that exist: their whole window, as in the common case; others: zeros
+                    const uint32_t r = (uint32_t)lane & (ROWS - 1);
+                    const bool ok = row0 + r < P.N;
+                    const uint8_t* blkp = ok ? qrow + (size_t)r * row_bytes : P.qs;
+                    const uint32_t odd = (uint32_t)reinterpret_cast<uintptr_t>(blkp) & 8u;
+                    const uint8_t* win = blkp - odd;
 #pragma unroll
-                for (int c = 0; c < ROWS * 4 / 32; ++c) {
-                    const int idx = c * 32 + lane;
-                    const int r = idx >> 2, ch = idx & 3;
-                    const bool ok = row0 + r < P.N && (uint32_t)ch >= ch_lo && (uint32_t)ch < ch_hi;
-                    const uint8_t* src = ok ? qrow + (size_t)r * row_bytes + ch * 16 : P.qs;
-                    // swizzle: chunk ch of row r goes to chunk ch ^ ((r >> 1) & 3)
-                    cp_async_16(st_s + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4), src, ok ? 16u : 0u);
+                    for (int i = 0; i < (ROWS * 5 + 31) / 32; ++i) {
+                        const uint32_t idx = (uint32_t)lane + 32u * i;
+                        if ((ROWS * 5) % 32 != 0 && idx >= (uint32_t)(ROWS * 5)) break;
+                        const uint32_t ch = idx / ROWS;
+                        cp_async_16(st_s + r * 80 + ch * 16, ok ? win + ch * 16 : P.qs,
+                                    ok ? ((ch == 4 && !odd) ? 8u : 16u) : 0u);
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < ROWS * 4 / 32; ++c) {
+                        const int idx = c * 32 + lane;
+                        const int r = idx >> 2, ch = idx & 3;
+                        const bool ok = row0 + r < P.N && (uint32_t)ch >= ch_lo && (uint32_t)ch < ch_hi;
+                        const uint8_t* src = ok ? qrow + (size_t)r * row_bytes + ch * 16 : P.qs;
+                        // swizzle: chunk ch of row r goes to chunk ch ^ ((r >> 1) & 3)
+                        cp_async_16(st_s + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4), src, ok ? 16u : 0u);
+                    }
                 }
                 if (lane < ROWS) {
                     const uint32_t row = row0 + lane;
                     const bool ok = row < P.N;
                     const size_t e = ((size_t)row * P.nb + ic.blk) * SC_B;
                     const size_t ea = e & ~(size_t)3, total = (size_t)P.N * P.nb * SC_B;
-                    if constexpr (FMT == 1) {
+                    if constexpr (FMT != 0) {
 #pragma unroll
                         for (uint32_t w = 0; w < 3; ++w) {
                             const size_t at = ea + 4 * w;
                             const uint32_t nbytes = ok && at < total ? (uint32_t)min((size_t)4, total - at) : 0u;
-                            cp_async_4(st_s + STAGE_QS + lane * 16 + 4 * w, P.sc + (nbytes ? at : 0), nbytes);
+                            cp_async_4(st_s + STAGE_QS + lane * SLOT + 4 * w, P.sc + (nbytes ? at : 0), nbytes);
                         }
                     } else {
                         const uint32_t nbytes = ok ? (uint32_t)min((size_t)4, total - ea) : 0u;
@@ -722,7 +834,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 }
             }
             ++ic.tb;
-            iq += QS_BYTES;
+            iq += QB;
             isp += SC_B;
             if (++ic.blk == i_nb) {
                 ic.blk = 0;
@@ -746,7 +858,37 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
 
     // ---- the decode table, built from the 1.5 KB compact copy: row e = 32 copies (one per lane)
     // ---- of the grid selector of code e, then (e < 128) 32 copies of the sign selector of index e
-    if constexpr (FMT == 1) {
+    if constexpr (FMT == 2) {
+        // IQ2_S: 64-byte rows of 16 copies: row 4 * low + qh2 (< 1024) = the grid selector of
+        // grid entry low | qh2 << 8 (nibble j: the magnitude code of weight j); then sign row s =
+        // the sign selector of sign byte s (nibble j: 4 when bit j is set)
+        constexpr int PER_THREAD = LUT_BYTES_S / 16 / (GEMV_WARPS * 32);
+        static_assert(LUT_BYTES_S % (16 * GEMV_WARPS * 32) == 0, "table chunks per thread");
+        uint32_t v[PER_THREAD];
+#pragma unroll
+        for (int i = 0; i < PER_THREAD; ++i) {
+            const int c = threadIdx.x + i * GEMV_WARPS * 32;
+            const int row = c >> 2;
+            uint32_t sel = 0;
+            if (row < 1024) {
+                const uint64_t gw = IQ2S_GRID[(row >> 2) | ((row & 3) << 8)];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t b = (uint32_t)(gw >> (8 * j)) & 0xFFu;
+                    sel |= (b == 8u ? 0u : (b == 25u ? 1u : 2u)) << (4 * j);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) sel |= (((uint32_t)(row - 1024) >> j) & 1u) << (4 * j + 2);
+            }
+            v[i] = sel;
+        }
+#pragma unroll
+        for (int i = 0; i < PER_THREAD; ++i) {
+            const int c = threadIdx.x + i * GEMV_WARPS * 32;
+            *reinterpret_cast<uint4*>(smem + gap + c * 16) = make_uint4(v[i], v[i], v[i], v[i]);
+        }
+    } else if constexpr (FMT == 1) {
         // IQ2_XS: row e < 512 = 32 copies of the grid selector of grid entry e (nibble j: the
         // magnitude code of weight j), then row 512 + e (e < 128) = 32 copies of the sign selector
         // of sign index e (IQ2_XS uses IQ2_XXS's sign table)
@@ -872,6 +1014,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     __syncthreads();  // the table (and the fused limbs) are complete
 
     DecodeK dk;
+    dk.two = L.two;
     dk.gsrc = (lut_s & 0xFFFF0000u) | ((uint32_t)lane * 4u);
     dk.gsel = 0x7604u | ((uint32_t)t << 4);
     dk.rot = (7u * t + 24u) & 31u;
@@ -879,6 +1022,15 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
     dk.xsel = (2u * t) | ((2u * t + 1u) << 4) | ((2u * t) << 8) | ((2u * t + 1u) << 12);
     dk.gbase = lut_s | ((uint32_t)lane * 4u);
     dk.sbase = (lut_s + 65536u) | ((uint32_t)lane * 4u);
+    if constexpr (FMT == 2) {
+        const uint32_t l16 = ((uint32_t)lane & 15u) * 4u;
+        dk.xsel = (uint32_t)t | 0x4440u;
+        dk.sbase = (lut_s + 65536u) | l16;
+        dk.gsel2 = 4u | ((uint32_t)t << 4) | 0x7600u;
+        dk.qsh = 6u - 2u * (uint32_t)t;
+        dk.qfill = l16 * 0x01010101u;
+        dk.lutw = lut_s;
+    }
     const uint32_t swz = (uint32_t)((g >> 1) & 3);  // rows g, g+8, g+16, g+24 share it
     const uint32_t rowbase = (uint32_t)g * 64u;     // rows tt*16+g (+8): rowbase + tt*1024 (+512)
 
@@ -919,15 +1071,20 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         int I[T][NT][4];
         const uint8_t* xbp = FUSED ? nullptr : c_xb + (size_t)(cc.blk * (8u * NT * 256u));
         const uint32_t xsp = xs_s + cc.blk * 8 * NT * 256 + lane * 8;
-        if constexpr (FMT == 1) {
-            // the row's 12 scale bytes start at its 16-byte slot; d is at byte 2 * parity, the
-            // sub-block scale bytes after it (the parity of row * nb + blk, as for the d word)
-            const uint32_t so = (((cc.blk & 1u) ^ c_dpar) ? 4u : 2u);
-            const uint32_t sc_s = st_s + STAGE_QS + (uint32_t)g * 16u + so;
+        if constexpr (FMT != 0) {
+            // the row's 12 scale bytes start at its slot; d is at byte 2 * parity, the sub-block
+            // scale bytes after it (the parity of row * nb + blk, as for the d word)
+            // (IQ2_S: the row's block sits at byte 8 * parity of its window)
+            const uint32_t odd = (cc.blk & 1u) ^ c_dpar;
+            const uint32_t so = odd ? 4u : 2u;
+            const uint32_t slot_s = st_s + STAGE_QS + (uint32_t)g * SLOT;
+            const uint32_t rb = FMT == 2 ? (uint32_t)g * 80u + odd * 8u : rowbase;
             if (s_lo == 0 && s_hi == 8)
-                stage_compute_xs<NT, T, false, S_::SPLIT>(dk, st_s, xbp, s_lo, s_hi, rowbase, swz, sc_s, t < 2, I);
+                stage_compute_xs<NT, T, false, S_::SPLIT, FMT, SLOT>(dk, st_s, xbp, s_lo, s_hi, rb, swz, slot_s, so,
+                                                                     t < 2, I);
             else
-                stage_compute_xs<NT, T, true, S_::SPLIT>(dk, st_s, xbp, s_lo, s_hi, rowbase, swz, sc_s, t < 2, I);
+                stage_compute_xs<NT, T, true, S_::SPLIT, FMT, SLOT>(dk, st_s, xbp, s_lo, s_hi, rb, swz, slot_s, so,
+                                                                    t < 2, I);
         } else if (s_lo == 0 && s_hi == 8) {
             stage_compute<NT, T, false, FUSED, S_::SPLIT>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
         } else {
@@ -947,7 +1104,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
 #pragma unroll
             for (int tt = 0; tt < T; ++tt) {
                 const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
-                constexpr uint32_t SLOT = FMT == 1 ? 16u : 4u;  // scale bytes per row in the stage
                 const uint32_t w0 = ld_shared_u32_volatile(st_s + STAGE_QS + r0 * SLOT);
                 const uint32_t w1 = ld_shared_u32_volatile(st_s + STAGE_QS + r1 * SLOT);
                 const float d0 = half_bits_to_float(prmt(w0, 0u, dsel));
@@ -1194,15 +1350,19 @@ size_t smem_for(bool fused, uint32_t nb) {
     return GemvShape<NT, LB, FMT>::SMEM + (fused ? xs_bytes(nb, NT) + cs_bytes(nb, NT) : 0);
 }
 
-size_t smem_for_nt(int nt, int limbs, bool fused, uint32_t nb, int fmt = 0) {
-    if (fmt == 1) {  // IQ2_XS: x limbs always from the prep kernel
-        switch (nt) {
-            case 1: return smem_for<1, 4, 1>(false, nb);
-            case 2: return limbs == 4 ? smem_for<2, 4, 1>(false, nb) : smem_for<2, 16, 1>(false, nb);
-            case 4: return smem_for<4, 16, 1>(false, nb);
-            default: return smem_for<8, 16, 1>(false, nb);
-        }
+template <int FMT>
+size_t smem_for_variant(int nt, int limbs, uint32_t nb) {
+    switch (nt) {  // x limbs always from the prep kernel
+        case 1: return smem_for<1, 4, FMT>(false, nb);
+        case 2: return limbs == 4 ? smem_for<2, 4, FMT>(false, nb) : smem_for<2, 16, FMT>(false, nb);
+        case 4: return smem_for<4, 16, FMT>(false, nb);
+        default: return smem_for<8, 16, FMT>(false, nb);
     }
+}
+
+size_t smem_for_nt(int nt, int limbs, bool fused, uint32_t nb, int fmt = 0) {
+    if (fmt == 1) return smem_for_variant<1>(nt, limbs, nb);  // IQ2_XS
+    if (fmt == 2) return smem_for_variant<2>(nt, limbs, nb);  // IQ2_S
     if (limbs == 1) {
         switch (nt) {
             case 1: return smem_for<1, 1>(fused, nb);
@@ -1252,7 +1412,7 @@ int max_active_clusters(int num_sms) {
 
 // max_cl: clusters the device can run at once (0 when only the workspace size is wanted).
 // w8a8: the activations as the W8A8 mode's int8 (one limb, m <= 32).
-// fmt: the weight format (0 IQ2_XXS, 1 IQ2_XS; IQ2_XS never makes its x limbs in the GEMV).
+// fmt: the weight format (0 IQ2_XXS, 1 IQ2_XS, 2 IQ2_S; only IQ2_XXS makes its x limbs in the GEMV).
 GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int max_cl, bool w8a8 = false,
                      int fmt = 0) {
     GroupPlan pl;
@@ -1353,9 +1513,9 @@ cudaError_t launch_gemv_kernel(const GemvLaunch<CAP>& L, const GroupPlan& pl, cu
 
 template <int NT, int CAP, int XDT, int LB = 4, int FMT = 0>
 cudaError_t launch_gemv_kernel_p(const GemvLaunch<CAP>& L, const GroupPlan& pl, bool p2p, cudaStream_t stream) {
-    if constexpr (FMT == 1) {
+    if constexpr (FMT != 0) {
         (void)p2p;  // (the sharded calls are IQ2_XXS only)
-        return launch_gemv_kernel<NT, CAP, XDT, false, LB, 1>(L, pl, stream);
+        return launch_gemv_kernel<NT, CAP, XDT, false, LB, FMT>(L, pl, stream);
     } else {
         return p2p ? launch_gemv_kernel<NT, CAP, XDT, true, LB>(L, pl, stream)
                    : launch_gemv_kernel<NT, CAP, XDT, false, LB>(L, pl, stream);
@@ -1417,6 +1577,7 @@ cudaError_t launch_group_cap(const GemvProblemHost* probs, uint32_t count, uint3
     L.x = probs[0].x;
     L.K = probs[0].k;
     L.clusters = pl.clusters;
+    L.two = 2u;
     for (uint32_t c = 0; c <= pl.clusters; ++c) L.cl_tb[c] = pl.cl_tb[c];
     for (uint32_t c = 0; c < pl.clusters; ++c) L.cl_p[c] = pl.cl_p[c];
     for (uint32_t i = 0; i < count; ++i) {
@@ -1525,24 +1686,38 @@ cudaError_t launch_gemv(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     return launch_gemv_group(&p, 1, m, x_dtype, workspace, num_sms, stream);
 }
 
-size_t gemv_xs_workspace_size(uint32_t m, uint32_t n, uint32_t k) {
+bool gemv_variant_ok(int variant) { return variant == 1 || variant == 2; }
+
+size_t gemv_variant_workspace_size(int variant, uint32_t m, uint32_t n, uint32_t k) {
+    if (!gemv_variant_ok(variant)) return 0;
     GemvProblemHost p{nullptr, nullptr, nullptr, n, k, nullptr};
-    return plan_group(&p, 1, m, 0, false, 1).total;
+    return plan_group(&p, 1, m, 0, false, variant).total;
 }
 
-cudaError_t launch_gemv_xs(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
-                           uint32_t n, uint32_t k, float* out, void* workspace, int num_sms, cudaStream_t stream) {
-    GemvProblemHost p{x, qs, sc, n, k, out};
-    const GroupPlan pl = plan_group(&p, 1, m, max_active_clusters(num_sms), false, 1);
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
+namespace {
+template <int FMT>
+cudaError_t launch_gemv_fmt(const GemvProblemHost& p, uint32_t m, int x_dtype, uint8_t* ws, const GroupPlan& pl,
+                            cudaStream_t stream) {
     switch (pl.nt) {
-        case 1: return launch_group_cap<1, 1, 4, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
+        case 1: return launch_group_cap<1, 1, 4, FMT>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
         case 2:
-            return pl.limbs == 4 ? launch_group_cap<2, 1, 4, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr)
-                                 : launch_group_cap<2, 1, 16, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
-        case 4: return launch_group_cap<4, 1, 16, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
-        default: return launch_group_cap<8, 1, 16, 1>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
+            return pl.limbs == 4 ? launch_group_cap<2, 1, 4, FMT>(&p, 1, m, x_dtype, ws, pl, stream, nullptr)
+                                 : launch_group_cap<2, 1, 16, FMT>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
+        case 4: return launch_group_cap<4, 1, 16, FMT>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
+        default: return launch_group_cap<8, 1, 16, FMT>(&p, 1, m, x_dtype, ws, pl, stream, nullptr);
     }
+}
+}  // namespace
+
+cudaError_t launch_gemv_variant(int variant, const void* x, int x_dtype, uint32_t m, const uint8_t* qs,
+                                const uint8_t* sc, uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,
+                                cudaStream_t stream) {
+    if (!gemv_variant_ok(variant)) return cudaErrorInvalidValue;
+    GemvProblemHost p{x, qs, sc, n, k, out};
+    const GroupPlan pl = plan_group(&p, 1, m, max_active_clusters(num_sms), false, variant);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    return variant == 1 ? launch_gemv_fmt<1>(p, m, x_dtype, ws, pl, stream)
+                        : launch_gemv_fmt<2>(p, m, x_dtype, ws, pl, stream);
 }
 
 cudaError_t launch_gemv_generic(const void* x, int x_dtype, uint32_t m, const uint8_t* qs,

@@ -161,18 +161,19 @@ def test_variant_w8a8_gemm(oracle, variant):
     assert rel_l2(y, ref) <= GEMM_ORACLE_TOL
 
 
+@pytest.mark.parametrize("variant", ["iq2_xs", "iq2_s"])
 @pytest.mark.parametrize("m", [1, 3, 8, 16, 32])
-def test_iq2xs_decode_gemv(oracle, m):
-    """IQ2_XS at m <= 32 on the IQ2_XXS decode GEMV (int8 tensor-core decode; two MMAs per
-    sub-block, one per 16-weight scale), selected when the call has the workspace the size query
-    reports: against the oracle and the CUDA-core kernel (no workspace), f32 x, ragged K."""
-    var = VARIANTS["iq2_xs"][0]
+def test_variant_decode_gemv(oracle, variant, m):
+    """IQ2_XS and IQ2_S at m <= 32 on the IQ2_XXS decode GEMV (int8 tensor-core decode; two MMAs
+    per sub-block, one per 16-weight scale), selected when the call has the workspace the size
+    query reports: against the oracle and the CUDA-core kernel (no workspace), f32 x, ragged K."""
+    var = VARIANTS[variant][0]
     n, k = 1000, 4096 + 256 + 96
-    wb, ws = _blocks("iq2_xs", n, k, seed=40 + m)
+    wb, ws = _blocks(variant, n, k, seed=40 + m)
     assert c.workspace_bytes(m, n, k, torch.float32, var) > 0
     x = torch.randn(m, k, generator=torch.Generator().manual_seed(50 + m)).cuda()
     wbd, wsd = torch.from_numpy(wb).cuda(), torch.from_numpy(ws).cuda()
     y = c.iq2_matmul(x, wbd, wsd, n, k, var)
-    ref = oracle.matmul(x.cpu().numpy(), wb, ws, n, k, variant="iq2_xs")
+    ref = oracle.matmul(x.cpu().numpy(), wb, ws, n, k, variant=variant)
     assert rel_l2(y.cpu().numpy(), ref) <= 1e-4
     assert rel_l2(y.cpu().numpy(), _cuda_core(x, wbd, wsd, n, k, var).cpu().numpy()) <= 1e-4
