@@ -547,6 +547,10 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
     volatile uint32_t* abort_flag = tmem_addr_word + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // The split tiles' sum kernel (launched as a programmatic dependent) may be scheduled now: it
+    // waits for this grid to complete before it reads anything. (Kernels of this library that
+    // read before their own wait only read weights, which this kernel never writes.)
+    pdl_launch_dependents();
     // this CTA's unit: tile t, K range z of nz; pu = its partial tile (-1: the tile is whole).
     // PAIR: units are pairs (cluster = blockIdx.x / 2, rank = the CTA's rank in it); tile t is a
     // pair tile (n-tile t % nt, token tiles 2 * (t / nt) + rank), partial tile (2 * (t - full) +
@@ -864,12 +868,15 @@ __global__ void __launch_bounds__(256) to_bf16_kernel(const XT* __restrict__ x, 
 }
 
 // The split tiles' outputs: out = the sum of each tile's K ranges, in range order (deterministic).
-// One thread per 4 columns of a partial tile row.
+// One thread per 4 columns of a partial tile row; the ranges' loads are issued four at a time.
 // R: split tiles (PAIR: split pair tiles, 2R partial tiles, tile i = pair i / 2, rank i % 2).
+// Launched as a programmatic dependent of the GEMM: its blocks may become resident while the GEMM
+// runs and wait here until it has completed and its partial tiles are visible.
 __global__ void __launch_bounds__(256) splitk_tile_sum_kernel(const float* __restrict__ part, float* __restrict__ out,
                                                               uint32_t M, uint32_t N, uint32_t nt, uint32_t full,
                                                               uint32_t R, uint32_t s, uint32_t BN, uint32_t PR,
                                                               uint32_t pair) {
+    pdl_wait();
     const uint32_t q = BN / 4;  // column quads per row
     const size_t total = (size_t)(pair ? 2 * R : R) * PR * q;
     for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
@@ -881,13 +888,21 @@ __global__ void __launch_bounds__(256) splitk_tile_sum_kernel(const float* __res
         const uint32_t token = mtile * G_BM + row, n = (t % nt) * BN + c4;
         if (token >= M || n >= N) continue;
         const float4* src = reinterpret_cast<const float4*>(part + (((size_t)i * s) * PR + row) * BN + c4);
+        const size_t zs = (size_t)PR * BN / 4;  // float4s between ranges
         float4 a = src[0];
-        for (uint32_t z = 1; z < s; ++z) {
-            const float4 b = src[(size_t)z * PR * BN / 4];
-            a.x += b.x;
-            a.y += b.y;
-            a.z += b.z;
-            a.w += b.w;
+        for (uint32_t z0 = 1; z0 < s; z0 += 4) {
+            float4 b[4];
+#pragma unroll
+            for (uint32_t j = 0; j < 4; ++j)
+                if (z0 + j < s) b[j] = src[(z0 + j) * zs];
+#pragma unroll
+            for (uint32_t j = 0; j < 4; ++j)
+                if (z0 + j < s) {
+                    a.x += b[j].x;
+                    a.y += b[j].y;
+                    a.z += b[j].z;
+                    a.w += b[j].w;
+                }
         }
         float* o = out + (size_t)token * N + n;
         o[0] = a.x;
@@ -1174,8 +1189,19 @@ cudaError_t launch_gemm(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     const size_t quads = (size_t)ptiles * pl.PR * (pl.bn / 4);
     const int sms = num_sms > 0 ? num_sms : 148;
     const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((quads + 255) / 256, (size_t)sms * 8));
-    splitk_tile_sum_kernel<<<blocks, 256, 0, stream>>>(p.part, out, m, n, pl.nt, pl.full, pl.R, pl.s, pl.bn, pl.PR,
-                                                       pl.pair ? 1u : 0u);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, splitk_tile_sum_kernel, static_cast<const float*>(p.part), out, m, n, pl.nt,
+                           pl.full, pl.R, pl.s, pl.bn, pl.PR, pl.pair ? 1u : 0u);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
