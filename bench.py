@@ -64,21 +64,56 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 100 ms while active."""
+    """SM clocks and throttle reasons of one GPU, sampled every 10 ms while active: through NVML (the
+    device opened before the timed region starts, found by the CUDA device's UUID), else nvidia-smi
+    every 100 ms (which takes about a second to produce its first sample)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.file = None
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.proc = self.file = self.thread = None
+        self.nvml = None
+        self.rows = []  # (sm_mhz, sm_max_mhz, [reason names])
+        self.stop = False
+
+    def _open_nvml(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            bits = (pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                    pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap)
+            smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            return pynvml, h, bits, smax
+        except Exception:
+            return None
+
+    def _sample_nvml(self):
+        pynvml, h, bits, smax = self.nvml
+        while not self.stop:
+            try:
+                sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((sm, smax, [n for n, bit in zip(self.NAMES, bits) if r & bit]))
+            except Exception:
+                pass
+            time.sleep(0.01)
 
     def __enter__(self):
+        import threading
+        self.nvml = self._open_nvml()
+        if self.nvml is not None:
+            self.thread = threading.Thread(target=self._sample_nvml, daemon=True)
+            self.thread.start()
+            return self
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device.index}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=self.file, stderr=subprocess.DEVNULL)
         except FileNotFoundError:
@@ -86,6 +121,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
+        self.stop = True
+        if self.thread is not None:
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -94,17 +132,21 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        self.file.flush()
-        rows = [r.split(",") for r in Path(self.file.name).read_text().strip().splitlines() if r.count(",") >= 8]
-        os.unlink(self.file.name)
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        smax = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": reasons, "samples": len(rows)}
+        if self.nvml is None:
+            if self.proc is None:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+            self.file.flush()
+            for r in [r.split(",") for r in Path(self.file.name).read_text().strip().splitlines() if r.count(",") >= 8]:
+                sm, smax = r[1].strip(), r[2].strip()
+                if sm.replace(".", "").isdigit() and smax.replace(".", "").isdigit():
+                    self.rows.append((float(sm), float(smax),
+                                      [n for i, n in enumerate(self.NAMES) if r[5 + i].strip().lower() == "active"]))
+            os.unlink(self.file.name)
+        rows = self.rows
+        return {"sm_mhz": statistics.median(r[0] for r in rows) if rows else None,
+                "sm_max_mhz": max(r[1] for r in rows) if rows else None,
+                "reasons": sorted({n for r in rows for n in r[2]}), "samples": len(rows),
+                "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------------------- ours
@@ -266,7 +308,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if dist:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(device.index) as clocks:
+    with ClockSampler(device) as clocks:
         ms = _time_graph(ggraph, args.steps, stream)
         # keep sampling a little longer when the timed region is shorter than a sample period
         # (every rank replays the same number of times: the step holds collectives)
@@ -460,7 +502,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             line["next_rows"] = next_rows_bench(args, device, stream, peaks, peak_src)
         if not args.no_config01 and world == 1:
             line.update(config01_bench(args, device, stream, peaks, peak_src))
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(args)
     return line
 
