@@ -9,6 +9,12 @@
 // into each projection's [m, N] output. A single projection at m = 1 is all-gathered straight
 // into its output (rank-major slices of one row are already the row).
 //
+// Pipelined exchange (m above the decode GEMV's range, the tensor-core GEMM): the call is cut into
+// chunks (each projection, split along m into parts of at most ~256 MB of gathered output), each
+// chunk's slice is computed on the caller's stream, and its all-gather and scatter run on two
+// side streams while the next chunk computes, so that the exchange (the larger part at 4-8
+// ranks: the f32 outputs cross NVLink) overlaps the GEMMs.
+//
 // Fused exchange: when every output lies in the communicator's symmetric region (allocated by
 // iq2_comm_symmetric_alloc: one device allocation per rank, mapped into every other rank's process
 // with CUDA IPC) and m <= 32, the decode GEMV stores each output value straight into all ranks'
@@ -35,6 +41,11 @@ struct iq2_comm_s {
     uint8_t* symm = nullptr;     // this rank's symmetric region (header + user area)
     size_t symm_bytes = 0;       // user area bytes
     void* peer[iq2::kMaxRanks] = {};  // the other ranks' regions mapped here (IPC); peer[rank] = symm
+    // The pipelined exchange (m above the decode GEMV's range): a stream for the all-gathers, one for
+    // the scatters, and events that fork them from and join them to the caller's stream; created on
+    // the first such call.
+    cudaStream_t xs[2] = {};
+    cudaEvent_t ev[2 * 64 + 2] = {};
 };
 
 namespace iq2 {
@@ -156,6 +167,50 @@ std::vector<iq2_matmul_problem> local_problems(const iq2_matmul_problem* probs, 
     return loc;
 }
 
+
+// Pipelined exchange: chunk c is rows [m0, m0 + mlen) of projection i; its slice sits at `off`
+// (elements) of the packed buffer and, gathered, at world * off ([rank][mlen][n_loc]).
+struct Chunk {
+    uint32_t i, m0, mlen;
+    uint64_t off;
+};
+constexpr uint32_t kMaxChunks = 64;
+constexpr uint64_t kChunkGatherBytes = 256ull << 20;
+
+bool use_pipeline(uint32_t m, uint32_t count, int world) { return world > 1 && m > kGemvMaxM && count <= kMaxChunks; }
+
+std::vector<Chunk> plan_chunks(const iq2_matmul_problem* probs, uint32_t count, uint32_t m, int world) {
+    std::vector<Chunk> ch;
+    uint64_t off = 0;
+    // parts per projection: at most ~kChunkGatherBytes gathered, a multiple of 256 rows (the GEMM's
+    // token tile) each, at most kMaxChunks in all
+    const uint32_t budget = std::max<uint32_t>(1, kMaxChunks / std::max<uint32_t>(1, count));
+    for (uint32_t i = 0; i < count; ++i) {
+        const uint64_t bytes = (uint64_t)m * probs[i].out_dim * sizeof(float);
+        uint32_t parts = (uint32_t)std::min<uint64_t>((bytes + kChunkGatherBytes - 1) / kChunkGatherBytes, budget);
+        uint32_t mlen = (m + parts - 1) / parts;
+        mlen = std::min(m, (mlen + 255) / 256 * 256);
+        const uint32_t n_loc = probs[i].out_dim / (uint32_t)world;
+        for (uint32_t m0 = 0; m0 < m; m0 += mlen) {
+            const uint32_t len = std::min(mlen, m - m0);
+            ch.push_back({i, m0, len, off});
+            off += (uint64_t)len * n_loc;
+        }
+    }
+    return ch;
+}
+
+// The chunk's local problem: its x rows, this rank's weight slice, its packed output.
+iq2_matmul_problem chunk_problem(const iq2_matmul_problem& p, const Chunk& c, int x_dtype, int world,
+                                 float* packed) {
+    iq2_matmul_problem q = p;
+    const size_t esize = x_dtype == IQ2_DTYPE_F32 ? 4 : 2;
+    q.x = static_cast<const uint8_t*>(p.x) + (size_t)c.m0 * p.in_dim * esize;
+    q.out_dim = p.out_dim / (uint32_t)world;
+    q.out = packed ? packed + c.off : nullptr;
+    return q;
+}
+
 }  // namespace
 
 // The fused-exchange path is taken when every output lies in the symmetric region and m <= 32.
@@ -221,6 +276,88 @@ int sharded_peer(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t coun
     const cudaError_t e = launch_gemv_group(loc.data(), count, m, x_dtype, workspace, sms,
                                             reinterpret_cast<cudaStream_t>(stream), &pe);
     if (e != cudaSuccess) return peer_local_failure(comm, stream, capi_cuda_fail(op, e));
+    return capi_ok();
+}
+
+namespace {
+
+// Side streams and events of the pipelined exchange, created once per communicator.
+int pipeline_resources(iq2_comm_t comm, const char* op) {
+    if (comm->xs[0] != nullptr) return IQ2_OK;
+    int lo = 0, hi = 0;
+    cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    for (cudaStream_t& x : comm->xs) {
+        // the exchange's kernels first: the GEMMs fill every SM, and a late all-gather stalls the chain
+        const cudaError_t e = cudaStreamCreateWithPriority(&x, cudaStreamNonBlocking, hi);
+        if (e != cudaSuccess) return capi_cuda_fail(op, e);
+    }
+    for (cudaEvent_t& ev : comm->ev) {
+        const cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        if (e != cudaSuccess) return capi_cuda_fail(op, e);
+    }
+    return IQ2_OK;
+}
+
+}  // namespace
+
+// The pipelined exchange (see the top of this file). Chunk c: its slice on the caller's stream,
+// then on xs[0] (after the slice) its all-gather, then on xs[1] (after the gather) its scatter;
+// at the end the caller's stream waits for both side streams. Works under stream capture (the side
+// streams fork from and join the caller's stream through events).
+int sharded_pipelined(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t count, uint32_t m, int x_dtype,
+                      uint8_t* ws, size_t ws_bytes, iq2_stream_t stream) {
+    const char* op = "iq2_matmul_grouped_sharded";
+    int rc = pipeline_resources(comm, op);
+    if (rc != IQ2_OK) return rc;
+    const int world = comm->world;
+    const ShardPlan pl = plan_shards(probs, count, m, world);
+    const std::vector<Chunk> chunks = plan_chunks(probs, count, m, world);
+    float* packed = reinterpret_cast<float*>(ws);
+    float* gathered = reinterpret_cast<float*>(ws + pl.packed_bytes);
+    const size_t inner_off = pl.packed_bytes + align256(pl.per_rank * world * sizeof(float));
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream), g = comm->xs[0], sc = comm->xs[1];
+    cudaEvent_t* ev_slice = comm->ev;              // [kMaxChunks]
+    cudaEvent_t* ev_gath = comm->ev + kMaxChunks;  // [kMaxChunks]
+    cudaEvent_t ev_g_end = comm->ev[2 * kMaxChunks], ev_s_end = comm->ev[2 * kMaxChunks + 1];
+    cudaError_t e = cudaSuccess;
+    for (size_t ci = 0; ci < chunks.size(); ++ci) {
+        const Chunk& c = chunks[ci];
+        const iq2_matmul_problem q = chunk_problem(probs[c.i], c, x_dtype, world, packed);
+        // 1. this rank's slice of the chunk (validated like iq2_matmul)
+        rc = iq2_matmul_grouped(&q, 1, c.mlen, x_dtype, ws + inner_off, ws_bytes - inner_off, stream);
+        if (rc != IQ2_OK) return rc;
+        // 2. every rank's slices of it, rank-major, while the next chunk computes
+        if ((e = cudaEventRecord(ev_slice[ci], s)) != cudaSuccess ||
+            (e = cudaStreamWaitEvent(g, ev_slice[ci], 0)) != cudaSuccess)
+            return capi_cuda_fail(op, e);
+        const uint64_t count_c = (uint64_t)c.mlen * q.out_dim;
+        const ncclResult_t r = nccl_settle(
+            comm->nccl,
+            ncclAllGather(packed + c.off, gathered + (uint64_t)world * c.off, count_c, ncclFloat, comm->nccl, g),
+            comm->timeout_ms);
+        if (r != ncclSuccess) return comm_failed(comm, op, "ncclAllGather", r);
+        // 3. its rows of the projection's [m, out_dim] output
+        if ((e = cudaEventRecord(ev_gath[ci], g)) != cudaSuccess ||
+            (e = cudaStreamWaitEvent(sc, ev_gath[ci], 0)) != cudaSuccess)
+            return capi_cuda_fail(op, e);
+        ScatterLaunch L;
+        std::memset(&L, 0, sizeof(L));
+        L.gathered = gathered + (uint64_t)world * c.off;
+        L.per_rank = count_c;
+        L.world = (uint32_t)world;
+        L.m = c.mlen;
+        L.item[0].out = probs[c.i].out + (size_t)c.m0 * probs[c.i].out_dim;
+        L.item[0].off = 0;
+        L.item[0].n_loc = q.out_dim;
+        const unsigned bx = (unsigned)std::min<uint64_t>(((uint64_t)c.mlen * probs[c.i].out_dim + 255) / 256, 1024);
+        scatter_slices_kernel<<<dim3(bx, 1), 256, 0, sc>>>(L);
+        if ((e = cudaGetLastError()) != cudaSuccess) return capi_cuda_fail(op, e);
+    }
+    // the caller's stream goes on once every chunk is gathered and scattered
+    if ((e = cudaEventRecord(ev_g_end, g)) != cudaSuccess || (e = cudaEventRecord(ev_s_end, sc)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(s, ev_g_end, 0)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(s, ev_s_end, 0)) != cudaSuccess)
+        return capi_cuda_fail(op, e);
     return capi_ok();
 }
 
@@ -320,6 +457,10 @@ int iq2_comm_destroy(iq2_comm_t comm) {
     }
     // after an abort a peer may still hold this rank's region mapped: it is then left allocated
     if (comm->symm != nullptr && r == ncclSuccess) release_symmetric(comm);
+    for (cudaStream_t x : comm->xs)
+        if (x != nullptr) cudaStreamDestroy(x);
+    for (cudaEvent_t e : comm->ev)
+        if (e != nullptr) cudaEventDestroy(e);
     delete comm;
     return rc == IQ2_OK ? iq2::capi_ok() : rc;
 }
@@ -435,6 +576,15 @@ size_t iq2_matmul_grouped_sharded_workspace_size(const iq2_matmul_problem* probl
                                                  int x_dtype, int world) {
     if (problems == nullptr || count == 0 || m == 0 || world < 1) return 0;
     const iq2::ShardPlan pl = iq2::plan_shards(problems, count, m, world);
+    if (iq2::use_pipeline(m, count, world)) {
+        // the chunks' GEMMs run one after another on the caller's stream and share the scratch
+        size_t inner = 0;
+        for (const iq2::Chunk& c : iq2::plan_chunks(problems, count, m, world)) {
+            const iq2_matmul_problem q = iq2::chunk_problem(problems[c.i], c, x_dtype, world, nullptr);
+            inner = std::max(inner, iq2_matmul_grouped_workspace_size(&q, 1, c.mlen, x_dtype));
+        }
+        return pl.packed_bytes + iq2::align256(pl.per_rank * world * sizeof(float)) + inner;
+    }
     std::vector<iq2_matmul_problem> loc = iq2::local_problems(problems, count, m, world, pl, nullptr);
     return pl.inner_off + iq2_matmul_grouped_workspace_size(loc.data(), count, m, x_dtype);
 }
@@ -469,6 +619,8 @@ int iq2_matmul_grouped_sharded(iq2_comm_t comm, const iq2_matmul_problem* proble
         return capi_fail(IQ2_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, got %zu", op, need,
                          workspace ? workspace_bytes : (size_t)0);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
+    if (iq2::use_pipeline(m, count, comm->world))
+        return iq2::sharded_pipelined(comm, problems, count, m, x_dtype, ws, workspace_bytes, stream);
     float* packed = reinterpret_cast<float*>(ws);
     std::vector<iq2_matmul_problem> loc = iq2::local_problems(problems, count, m, comm->world, pl, packed);
     // 1. this rank's slices (the grouped call validates every slice like iq2_matmul does)

@@ -56,6 +56,35 @@ def _rank(rank: int, port: int, q):
             ys = iq2_matmul_grouped_sharded(comm, probs)
             for i, (n, k) in enumerate(shapes):
                 errs[f"grouped m={m} {n}x{k}"] = rel(ys[i], c.iq2_xxs_matmul(xs[i], full[i][0], full[i][1], n, k))
+        # m > 32 exchanges chunk by chunk while the next chunk computes: a projection whose gathered
+        # output exceeds one chunk is split along m (4608 x 14336 f32 = 264 MB: chunks of 2304)
+        m = 4608
+        n, k = shapes[2]
+        xb = synth.activations(m, k, seed=40, dtype=torch.bfloat16, device=dev)
+        pb = [(xb, *shard_rows(full[2][0], full[2][1], n, k, rank, WORLD), n, k)]
+        errs[f"grouped m={m} {n}x{k} (split along m)"] = rel(iq2_matmul_grouped_sharded(comm, pb)[0],
+                                                            c.iq2_xxs_matmul(xb, full[2][0], full[2][1], n, k))
+        # ... and under CUDA-graph capture (the side streams fork from and join the capturing stream)
+        m = 300
+        xs = [synth.activations(m, k, seed=50 + i, device=dev) for i, (n, k) in enumerate(shapes)]
+        outs = [torch.empty(m, n, device=dev) for (n, k) in shapes]
+        probs = [(xs[i], *shard_rows(full[i][0], full[i][1], n, k, rank, WORLD), n, k, outs[i])
+                 for i, (n, k) in enumerate(shapes)]
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            iq2_matmul_grouped_sharded(comm, probs)
+        st.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            iq2_matmul_grouped_sharded(comm, probs)
+        for i in range(len(outs)):
+            outs[i].zero_()
+        with torch.cuda.stream(st):
+            g.replay()
+        st.synchronize()
+        for i, (n, k) in enumerate(shapes):
+            errs[f"graph m={m} {n}x{k}"] = rel(outs[i], c.iq2_xxs_matmul(xs[i], full[i][0], full[i][1], n, k))
+        del g
         torch.cuda.synchronize()
         comm.close()
         dist.destroy_process_group()
