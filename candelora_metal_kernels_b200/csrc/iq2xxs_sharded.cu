@@ -118,15 +118,26 @@ struct ScatterLaunch {
     ScatterItem item[SCATTER_CAP];
 };
 
-// blockIdx.y = projection; threads over its m * N outputs (coalesced writes).
+// blockIdx.y = projection; each block copies whole segments (rank r's n_loc columns of one row,
+// contiguous in both the gathered slices and the output), 16 bytes per thread and step where the
+// columns per rank are a multiple of 4 and the output is 16-byte aligned: a memory-bound copy with
+// no per-element index arithmetic, so that it takes little from GEMMs running beside it.
 __global__ void __launch_bounds__(256) scatter_slices_kernel(const __grid_constant__ ScatterLaunch L) {
     const ScatterItem& it = L.item[blockIdx.y];
-    const uint64_t n = (uint64_t)it.n_loc * L.world, total = n * L.m;
-    for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
-         e += (uint64_t)gridDim.x * blockDim.x) {
-        const uint64_t row = e / n, col = e % n;
-        const uint64_t r = col / it.n_loc, j = col % it.n_loc;
-        it.out[e] = L.gathered[r * L.per_rank + it.off + row * it.n_loc + j];
+    const uint32_t nl = it.n_loc, segs = L.m * L.world;
+    const uint64_t n = (uint64_t)nl * L.world;
+    const bool vec = nl % 4 == 0 && L.per_rank % 4 == 0 && it.off % 4 == 0 &&
+                     (reinterpret_cast<uintptr_t>(it.out) & 15u) == 0 && (reinterpret_cast<uintptr_t>(L.gathered) & 15u) == 0;
+    for (uint32_t sg = blockIdx.x; sg < segs; sg += gridDim.x) {
+        const uint32_t row = sg / L.world, r = sg % L.world;
+        const float* src = L.gathered + r * L.per_rank + it.off + (uint64_t)row * nl;
+        float* dst = it.out + row * n + (uint64_t)r * nl;
+        if (vec) {
+            for (uint32_t j = threadIdx.x * 4u; j < nl; j += blockDim.x * 4u)
+                *reinterpret_cast<float4*>(dst + j) = __ldcs(reinterpret_cast<const float4*>(src + j));
+        } else {
+            for (uint32_t j = threadIdx.x; j < nl; j += blockDim.x) dst[j] = src[j];
+        }
     }
 }
 
@@ -286,9 +297,10 @@ int pipeline_resources(iq2_comm_t comm, const char* op) {
     if (comm->xs[0] != nullptr) return IQ2_OK;
     int lo = 0, hi = 0;
     cudaDeviceGetStreamPriorityRange(&lo, &hi);
-    for (cudaStream_t& x : comm->xs) {
-        // the exchange's kernels first: the GEMMs fill every SM, and a late all-gather stalls the chain
-        const cudaError_t e = cudaStreamCreateWithPriority(&x, cudaStreamNonBlocking, hi);
+    for (int i = 0; i < 2; ++i) {
+        // the all-gathers first (the GEMMs fill every SM, and a late all-gather stalls the chain);
+        // the scatters at the GEMMs' priority
+        const cudaError_t e = cudaStreamCreateWithPriority(&comm->xs[i], cudaStreamNonBlocking, i == 0 ? hi : lo);
         if (e != cudaSuccess) return capi_cuda_fail(op, e);
     }
     for (cudaEvent_t& ev : comm->ev) {
@@ -349,7 +361,7 @@ int sharded_pipelined(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t
         L.item[0].out = probs[c.i].out + (size_t)c.m0 * probs[c.i].out_dim;
         L.item[0].off = 0;
         L.item[0].n_loc = q.out_dim;
-        const unsigned bx = (unsigned)std::min<uint64_t>(((uint64_t)c.mlen * probs[c.i].out_dim + 255) / 256, 1024);
+        const unsigned bx = (unsigned)std::min<uint64_t>((uint64_t)c.mlen * world, 1184);
         scatter_slices_kernel<<<dim3(bx, 1), 256, 0, sc>>>(L);
         if ((e = cudaGetLastError()) != cudaSuccess) return capi_cuda_fail(op, e);
     }
@@ -643,14 +655,12 @@ int iq2_matmul_grouped_sharded(iq2_comm_t comm, const iq2_matmul_problem* proble
     L.per_rank = pl.per_rank;
     L.world = (uint32_t)comm->world;
     L.m = m;
-    uint64_t longest = 0;
     for (uint32_t i = 0; i < count; ++i) {
         L.item[i].out = problems[i].out;
         L.item[i].off = pl.off[i];
         L.item[i].n_loc = problems[i].out_dim / (uint32_t)comm->world;
-        longest = std::max<uint64_t>(longest, (uint64_t)m * problems[i].out_dim);
     }
-    const unsigned bx = (unsigned)std::min<uint64_t>((longest + 255) / 256, 1024);
+    const unsigned bx = (unsigned)std::min<uint64_t>((uint64_t)m * comm->world, 1184);
     iq2::scatter_slices_kernel<<<dim3(bx, count), 256, 0, s>>>(L);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return iq2::capi_cuda_fail(op, e);
