@@ -102,3 +102,24 @@ def test_w8a8_workspace_query_needs_no_device(lib):
     w8 = lib.iq2_matmul_with_activation_quant_workspace_size(3, 4096, 4096, 0, 0, 1)
     assert w8 >= off + 3 * 4096 * 4
     assert lib.iq2_matmul_with_activation_quant_workspace_size(3, 4096, 4096, 0, 0, 0) == off
+
+
+def test_sharded_workspace_query_covers_the_exchange_buffers(lib):
+    """A sharded call's scratch is sized without a device: this rank's packed output slices, every
+    rank's gathered slices, and the largest GEMM scratch of its projections (for m > 32 the chunks of
+    the pipelined exchange run one after another and share it; f32 x adds the chunk's bf16 copy)."""
+    shapes = [(28672, 8192), (28672, 8192), (8192, 28672)]  # configuration 3: gate, up, down (N, K)
+    arr = (_lib.Iq2MatmulProblem * len(shapes))()
+    for i, (n, k) in enumerate(shapes):
+        arr[i].out_dim, arr[i].in_dim = n, k
+    f32, bf16 = 0, 2
+    for world in (2, 8):
+        for m in (1, 3, 300, 2048):
+            slices = sum(m * (n // world) for n, _ in shapes) * 4
+            need = lib.iq2_matmul_grouped_sharded_workspace_size(arr, len(shapes), m, bf16, world)
+            assert need >= slices * (world + 1)
+            if m > 32:
+                need_f32 = lib.iq2_matmul_grouped_sharded_workspace_size(arr, len(shapes), m, f32, world)
+                assert need_f32 >= slices * (world + 1) + m * 28672 * 2  # down's x rows as bf16
+    assert lib.iq2_matmul_grouped_sharded_workspace_size(arr, len(shapes), 0, bf16, 2) == 0
+    assert lib.iq2_matmul_grouped_sharded_workspace_size(arr, 0, 2048, bf16, 2) == 0
