@@ -332,12 +332,38 @@ int sharded_pipelined(iq2_comm_t comm, const iq2_matmul_problem* probs, uint32_t
     cudaEvent_t* ev_gath = comm->ev + kMaxChunks;  // [kMaxChunks]
     cudaEvent_t ev_g_end = comm->ev[2 * kMaxChunks], ev_s_end = comm->ev[2 * kMaxChunks + 1];
     cudaError_t e = cudaSuccess;
+    // On a failure after the first fork the side streams may still hold this call's gathers and
+    // scatters: the caller's stream waits for them all the same, so that nothing it runs next
+    // overwrites buffers they still read.
+    auto join = [&]() {
+        cudaEventRecord(ev_g_end, g);
+        cudaEventRecord(ev_s_end, sc);
+        cudaStreamWaitEvent(s, ev_g_end, 0);
+        cudaStreamWaitEvent(s, ev_s_end, 0);
+    };
+    // every chunk's problem passes the argument checks before anything is launched (as in the
+    // single grouped call): the first chunk of each projection is checked without a launch
+    for (uint32_t i = 0; i < count; ++i) {
+        const Chunk* first = nullptr;
+        for (const Chunk& c : chunks)
+            if (c.i == i) {
+                first = &c;
+                break;
+            }
+        const iq2_matmul_problem q = chunk_problem(probs[i], *first, x_dtype, world, packed);
+        rc = capi_validate_matmul(op, q.x, x_dtype, first->mlen, q.weight_bytes, q.weight_bytes_len, q.weight_scales,
+                                  q.weight_scales_len, q.out_dim, q.in_dim, q.out, IQ2_VARIANT_IQ2_XXS);
+        if (rc != IQ2_OK) return rc;
+    }
     for (size_t ci = 0; ci < chunks.size(); ++ci) {
         const Chunk& c = chunks[ci];
         const iq2_matmul_problem q = chunk_problem(probs[c.i], c, x_dtype, world, packed);
         // 1. this rank's slice of the chunk (validated like iq2_matmul)
         rc = iq2_matmul_grouped(&q, 1, c.mlen, x_dtype, ws + inner_off, ws_bytes - inner_off, stream);
-        if (rc != IQ2_OK) return rc;
+        if (rc != IQ2_OK) {
+            if (ci > 0) join();
+            return rc;
+        }
         // 2. every rank's slices of it, rank-major, while the next chunk computes
         if ((e = cudaEventRecord(ev_slice[ci], s)) != cudaSuccess ||
             (e = cudaStreamWaitEvent(g, ev_slice[ci], 0)) != cudaSuccess)
