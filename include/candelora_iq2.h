@@ -254,8 +254,12 @@ size_t iq2_matmul_grouped_sharded_workspace_size(const iq2_matmul_problem* probl
 /* Up to 256 projections: their slices through one grouped call, one ncclAllGather of all of them
  * on `stream`, one scatter kernel into the outputs (or, with every output in the symmetric
  * region and m <= 32, the fused exchange above; its weight slices must then be 16-byte (bytes)
- * and 4-byte (scales) aligned on every rank). Stream-ordered, collective: every rank makes the
- * same call with the same shapes. */
+ * and 4-byte (scales) aligned on every rank). For m > 32 with at most 64 projections the exchange
+ * is pipelined: each projection (split along m when its gathered output passes 256 MB) is
+ * computed on `stream` while the previous one's all-gather and scatter run on two streams of the
+ * communicator, which `stream` waits for before the call's later work. Stream-ordered, collective:
+ * every rank makes the same call with the same shapes; a communicator serves one such call at a
+ * time. */
 int iq2_matmul_grouped_sharded(iq2_comm_t comm, const iq2_matmul_problem* problems, uint32_t count,
                                uint32_t m, int x_dtype, void* workspace, size_t workspace_bytes,
                                iq2_stream_t stream);
