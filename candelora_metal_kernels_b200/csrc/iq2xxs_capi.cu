@@ -161,8 +161,8 @@ int matmul_impl(const char* op, const void* x, int x_dtype, uint32_t m, const ui
                           iq2::gemm_path_ok(m, out_dim, in_dim, x, x_dtype, weight_bytes, weight_scales, out) &&
                           workspace != nullptr &&
                           workspace_bytes >= iq2::gemm_workspace_size(m, out_dim, in_dim, x_dtype, sms);
-        // IQ2_XS and IQ2_S with m <= kGemvMaxM: the IQ2_XXS decode GEMV's int8 tensor-core decode,
-        // likewise when the call has its workspace
+        // IQ2_XS, IQ2_S and IQ3_S with m <= kGemvMaxM: the IQ2_XXS decode GEMV's int8 tensor-core
+        // decode, likewise when the call has its workspace
         const bool gemv = iq2::gemv_variant_ok(variant) && m <= iq2::kGemvMaxM &&
                           iq2::gemv_fast_path_ok(m, in_dim, weight_bytes, weight_scales) && workspace != nullptr &&
                           workspace_bytes >= iq2::gemv_variant_workspace_size(variant, m, out_dim, in_dim);
@@ -341,10 +341,10 @@ int iq2_testing_set_gemm_stall(uint64_t wait_limit_ns, uint32_t stall_stage) {
 size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, int x_dtype,
                                  int variant) {
     if (variant < IQ2_VARIANT_IQ2_XXS || variant > IQ2_VARIANT_IQ3_S) return 0;
-    if (variant != IQ2_VARIANT_IQ2_XXS && m <= iq2::kGemvMaxM)  // IQ2_XS, IQ2_S: their decode GEMV's x limbs
+    if (variant != IQ2_VARIANT_IQ2_XXS && m <= iq2::kGemvMaxM)  // the other formats: their decode GEMV's x limbs
         return iq2::gemv_variant_ok(variant) && m > 0 && out_dim > 0 && in_dim > 0
                    ? iq2::gemv_variant_workspace_size(variant, m, out_dim, in_dim)
-                   : 0;  // (IQ3_S: the CUDA-core kernel needs none)
+                   : 0;
     return workspace_for(m, out_dim, in_dim, x_dtype, num_sms_for_current_device());
 }
 

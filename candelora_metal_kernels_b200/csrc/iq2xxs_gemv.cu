@@ -58,6 +58,9 @@ constexpr int LUT_BYTES = 256 * 256;      // 256 rows x (32 lanes grid selectors
 constexpr int LUT_BYTES_XS = 512 * 128 + 128 * 128;
 // IQ2_S: 1024 grid rows x 16 lane copies (64 KB), then 256 sign rows x 16 lane copies
 constexpr int LUT_BYTES_S = 1024 * 64 + 256 * 64;
+// IQ3_S: 512 grid rows x 32 lane copies (64 KB, row `low * 2 + hb` of 128 bytes), then the 16
+// sign-nibble rows x 16 lane copies of {byte mask, its low bits} (8 bytes each)
+constexpr int LUT_BYTES_3S = 512 * 128 + 16 * 128;
 constexpr int MAX_PROBLEMS = 256;         // per grouped launch
 constexpr int MAX_CLUSTERS = 96;          // >= SMs / 2 of the device (74 on B200)
 constexpr int SMEM_LIMIT = 227 * 1024;
@@ -69,13 +72,15 @@ constexpr int SMEM_LIMIT = 227 * 1024;
 // FMT: the weight format, 0 IQ2_XXS, 1 IQ2_XS (its 512-entry grid needs an 80 KB table, its
 // scales a 16-byte slot per row and stage), 2 IQ2_S (1024-entry grid and its 256-entry sign table
 // at 16 copies, 80 KB; per row and stage the 16-byte aligned 80-byte window around the row's
-// 72-byte block, then a 12-byte scale slot).
+// 72-byte block, then a 12-byte scale slot), 3 IQ3_S (512-entry grid of int8 magnitudes at 32
+// copies and a 16-entry sign-nibble table, 66 KB; the 112-byte window around the 104-byte block,
+// then an 8-byte scale slot).
 template <int NT, int LB = 4, int FMT = 0>
 struct GemvShape {
     static constexpr bool SPLIT = LB == 16;
-    static constexpr int LUT = FMT == 2 ? LUT_BYTES_S : (FMT == 1 ? LUT_BYTES_XS : LUT_BYTES);
-    static constexpr int SLOT = FMT == 0 ? 4 : (FMT == 1 ? 16 : 12);  // per row: the scales
-    static constexpr int QROW = FMT == 2 ? 80 : 64;                    // per row: the packed bytes
+    static constexpr int LUT = FMT == 3 ? LUT_BYTES_3S : (FMT == 2 ? LUT_BYTES_S : (FMT == 1 ? LUT_BYTES_XS : LUT_BYTES));
+    static constexpr int SLOT = FMT == 0 ? 4 : (FMT == 1 ? 16 : (FMT == 2 ? 12 : 8));  // per row: the scales
+    static constexpr int QROW = FMT == 2 ? 80 : (FMT == 3 ? 112 : 64);                 // per row: the packed bytes
     static constexpr int T = ((NT <= 2 && LB != 1) || (NT == 1 && LB == 1)) ? 2 : 1;  // 16-row mma tiles per warp
     static constexpr int ROWS = 16 * T;                // rows of a tile
     static constexpr int TPN = SPLIT ? 8 : 8 / LB;     // tokens per n8 tile (SPLIT: per high-byte tile)
@@ -87,7 +92,7 @@ struct GemvShape {
     // fewer stages where the partials (TOK x ROWS per warp slot) are large
     static constexpr int NSTAGES0 = T == 2 ? 3 : ((LB == 4 || (LB == 1 && NT <= 2) || (SPLIT && NT <= 4)) ? 6 : 4);
     static constexpr int PART_BYTES = GEMV_WARPS * 2 * TOK * ROWS * 4;  // [warp][first|last][token][row]
-    // IQ2_XS, IQ2_S: as many as fit beside the larger table (2..5)
+    // IQ2_XS, IQ2_S, IQ3_S: as many as fit beside the larger table (2..5)
     static constexpr int NS_FIT = (SMEM_LIMIT - LUT - PART_BYTES) / ((GEMV_WARPS + 1) * STAGE_BYTES);
     static constexpr int NSTAGES = FMT != 0 ? (NS_FIT < NSTAGES0 ? NS_FIT : NSTAGES0) : NSTAGES0;
     static_assert(NSTAGES >= 2, "stages");
@@ -431,6 +436,10 @@ struct DecodeK {
     uint32_t xsel, gbase, sbase;
     uint32_t gsel2, qsh, qfill, lutw;
     uint32_t two;  // GemvLaunch::two
+    // IQ3_S: xsel = {byte 2t, byte 2t+1} of a sub-block's 8 grid low bytes; qsh = 2t; qfill =
+    // (lane * 4) in bytes 0 and 1 and the table base in bytes 2, 3; sbase = sign table | (lane %
+    // 16) * 8; st8 = 8t
+    uint32_t st8;
 };
 
 // Four signed int8 weights of one 8-weight group (sub-block word {aux_g, aux_s}) for this
@@ -468,6 +477,27 @@ __device__ __forceinline__ void decode_group_s(const DecodeK& k, uint32_t lows, 
     const uint32_t sel = ld_shared_const(ga) | ld_shared_const(sa);
     lo = prmt(KPOS, KNEG, sel);
     hi = prmt(KPOS, KNEG, sel >> 16);
+}
+
+// IQ3_S: eight signed int8 weights of one 8-weight group (lane t of a sub-block): lows = the
+// sub-block's 8 grid low bytes, qw = its qh byte shifted right by 2t (bits j*8 + 0, 1 for
+// j = sb % 4 are the high bits of the group's two grid indices), sw = its 4 sign bytes. The grid
+// row of index low | hb << 8 sits at low * 256 + hb * 128 of the table, so its address is one
+// permute of the low byte and {copy | hb << 7, copy | hb' << 7, base}; a sign nibble's table entry
+// is {0xFF in each negative weight's byte, 0x01 in the same bytes}, and (g ^ mask) + low bits
+// negates those bytes (the magnitudes are 1..15: no carry between bytes).
+__device__ __forceinline__ void decode_group_3s(const DecodeK& k, uint2 lows, uint32_t qw, uint32_t j, uint32_t sw,
+                                                uint32_t& lo, uint32_t& hi) {
+    const uint32_t lw = prmt(lows.x, lows.y, k.xsel);
+    const uint32_t v = (qw >> (8u * j)) & 3u;
+    const uint32_t qa = ((v * 0x4080u) & 0x8080u) | k.qfill;
+    const uint32_t g1 = ld_shared_const(prmt(lw, qa, 0x7604u));
+    const uint32_t g2 = ld_shared_const(prmt(lw, qa, 0x7615u));
+    const uint32_t t1 = sw >> k.st8;
+    const uint2 m1 = ld_shared_v2_const((t1 & 15u) * 128u + k.sbase);
+    const uint2 m2 = ld_shared_v2_const(((t1 >> 4) & 15u) * 128u + k.sbase);
+    lo = (g1 ^ m1.x) + m1.y;
+    hi = (g2 ^ m2.x) + m2.y;
 }
 
 __device__ __forceinline__ uint32_t ld_shared_u8_volatile(uint32_t addr) {
@@ -592,6 +622,75 @@ __device__ __forceinline__ void stage_compute_xs(const DecodeK& dk, uint32_t st_
     }
 }
 
+// IQ3_S stage: as stage_compute (one scale per 32-weight sub-block, one MMA), with the row's
+// 112-byte window at rowbase (+ (r - g) * 112): grid low bytes of sub-block sb at + 8 sb, qh at
+// + 64, sign bytes at + 72 + 4 sb; the scale nibbles at sc_s (row r at + (r - g) * SLOT), two
+// sub-blocks per byte.
+template <int NT, int T, bool PARTIAL, bool SPLIT, int SLOT>
+__device__ __forceinline__ void stage_compute_3s(const DecodeK& dk, uint32_t st_s, const uint8_t* xbp, uint32_t s_lo,
+                                                 uint32_t s_hi, uint32_t rowbase, uint32_t sc_s, int (&I)[T][NT][4]) {
+    uint32_t qx[T][2], qy[T][2];
+#pragma unroll
+    for (int tt = 0; tt < T; ++tt)
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+            const uint2 q = ld_shared_v2_volatile(st_s + rowbase + (uint32_t)((tt * 16 + hr * 8) * 112) + 64u);
+            qx[tt][hr] = q.x >> dk.qsh;
+            qy[tt][hr] = q.y >> dk.qsh;
+        }
+#pragma unroll
+    for (int pair = 0; pair < 4; ++pair) {
+        uint32_t cb[T][2];  // the scale byte of sub-blocks 2 pair, 2 pair + 1 of rows g (+ 8)
+#pragma unroll
+        for (int tt = 0; tt < T; ++tt) {
+            cb[tt][0] = ld_shared_u8_volatile(sc_s + (uint32_t)(tt * 16 * SLOT + pair));
+            cb[tt][1] = ld_shared_u8_volatile(sc_s + (uint32_t)((tt * 16 + 8) * SLOT + pair));
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t sb = pair * 2 + h;
+            uint32_t bf[NT][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const uint2 v = __ldg(reinterpret_cast<const uint2*>(xbp + (sb * NT + nt) * 256));
+                bf[nt][0] = v.x;
+                bf[nt][1] = v.y;
+                if (PARTIAL && (sb < s_lo || sb >= s_hi)) bf[nt][0] = bf[nt][1] = 0u;
+            }
+#pragma unroll
+            for (int tt = 0; tt < T; ++tt) {
+                uint32_t w[4];
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const uint32_t ra = st_s + rowbase + (uint32_t)((tt * 16 + hr * 8) * 112);
+                    const uint2 lows = ld_shared_v2_volatile(ra + 8u * sb);
+                    const uint32_t sw = ld_shared_u32_volatile(ra + 72u + 4u * sb);
+                    decode_group_3s(dk, lows, sb < 4 ? qx[tt][hr] : qy[tt][hr], sb & 3u, sw, w[hr], w[2 + hr]);
+                }
+                const int c0 = (int)(((cb[tt][0] >> (4 * h)) & 15u) * dk.two + 1u);
+                const int c1 = (int)(((cb[tt][1] >> (4 * h)) & 15u) * dk.two + 1u);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    int d[4];
+                    if (SPLIT && nt >= NT / 2) mma_s8u8_16832(d, w[0], w[1], w[2], w[3], bf[nt][0], bf[nt][1]);
+                    else mma_s8_16832(d, w[0], w[1], w[2], w[3], bf[nt][0], bf[nt][1]);
+                    if (sb == 0) {
+                        I[tt][nt][0] = c0 * d[0];
+                        I[tt][nt][1] = c0 * d[1];
+                        I[tt][nt][2] = c1 * d[2];
+                        I[tt][nt][3] = c1 * d[3];
+                    } else {
+                        I[tt][nt][0] += c0 * d[0];
+                        I[tt][nt][1] += c0 * d[1];
+                        I[tt][nt][2] += c1 * d[2];
+                        I[tt][nt][3] += c1 * d[3];
+                    }
+                }
+            }
+        }
+    }
+}
+
 // One stage (a block of ROWS rows) of the decode: s32 sums per 256-block in I. The first
 // sub-block initialises I, so I needs no clearing. PARTIAL: only sub-blocks [s_lo, s_hi) count
 // (the first/last stage of a warp's range); the others see zero x fragments. FUSED: fragments
@@ -661,9 +760,14 @@ __device__ __forceinline__ void stage_compute(const DecodeK& dk, uint32_t st_s, 
 template <int NT, int CAP, int XDT, bool P2P = false, int LB = 4, int FMT = 0>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_constant__ GemvLaunch<CAP> L) {
     using S_ = GemvShape<NT, LB, FMT>;
-    static_assert(FMT == 0 || (!P2P && (LB == 4 || LB == 16)), "IQ2_XS, IQ2_S: the plain decode GEMV only");
-    constexpr uint32_t SC_B = FMT != 0 ? 10u : (uint32_t)SC_BYTES;  // scale bytes per block
-    constexpr uint32_t QB = FMT == 2 ? 72u : (uint32_t)QS_BYTES;   // packed bytes per block
+    static_assert(FMT == 0 || (!P2P && (LB == 4 || LB == 16)), "IQ2_XS, IQ2_S, IQ3_S: the plain decode GEMV only");
+    constexpr uint32_t SC_B = FMT == 3 ? 6u : (FMT != 0 ? 10u : (uint32_t)SC_BYTES);  // scale bytes per block
+    constexpr uint32_t QB = FMT == 3 ? 104u : (FMT == 2 ? 72u : (uint32_t)QS_BYTES);   // packed bytes per block
+    // IQ2_S, IQ3_S: the row's block in 16-byte copies of its aligned window (the last one reads
+    // only the block's 8 bytes when the block starts the window); the aligned scale words
+    constexpr int NCH = FMT == 3 ? 7 : 5;
+    constexpr int WIN = (int)S_::QROW;
+    constexpr uint32_t NSW = FMT == 3 ? 2u : 3u;
     constexpr uint32_t SLOT = (uint32_t)S_::SLOT;
     constexpr bool FUSED = XDT >= 0;
     constexpr int T = S_::T, ROWS = S_::ROWS, TOK = S_::TOK, STAGE_QS = S_::STAGE_QS;
@@ -730,8 +834,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         i_tiles = P.tiles;
         i_full = row0 + ROWS <= P.N;
         i_rstep = P.nb * QB * 8u;
-        // (IQ2_S: the block of row lane % ROWS)
-        iq = FMT == 2 ? P.qs + ((size_t)(row0 + ((uint32_t)lane & (ROWS - 1))) * P.nb + ic.blk) * QB
+        // (IQ2_S, IQ3_S: the block of row lane % ROWS)
+        iq = FMT >= 2 ? P.qs + ((size_t)(row0 + ((uint32_t)lane & (ROWS - 1))) * P.nb + ic.blk) * QB
                       : P.qs + ((size_t)(row0 + g) * P.nb + ic.blk) * QB + t * 16;
         isp = P.sc + ((size_t)(row0 + lane) * P.nb + ic.blk) * SC_B;
         i_scend = P.sc + (size_t)P.N * P.nb * SC_B;
@@ -745,19 +849,18 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
             if (ic.tb >= tbf_lo && ic.tb < tbf_hi && i_full) {
                 // the common case: every sub-block and every row of the stage is needed; chunk t
                 // of row r = 8c + g goes to chunk t ^ ((r >> 1) & 3) of the row's 64 bytes
-                if constexpr (FMT == 2) {
-                    // the 16-byte aligned 80-byte window around the row's 72-byte block (which
-                    // starts at byte 0 or 8 of it) in five 16-byte copies; the last one reads
-                    // only bytes of the block
+                if constexpr (FMT >= 2) {
+                    // the 16-byte aligned window around the row's block (which starts at byte 0
+                    // or 8 of it) in 16-byte copies; the last one reads only bytes of the block
                     const uint32_t odd = (uint32_t)reinterpret_cast<uintptr_t>(iq) & 8u;
                     const uint8_t* win = iq - odd;
                     const uint32_t r = (uint32_t)lane & (ROWS - 1);
 #pragma unroll
-                    for (int i = 0; i < (ROWS * 5 + 31) / 32; ++i) {
+                    for (int i = 0; i < (ROWS * NCH + 31) / 32; ++i) {
                         const uint32_t idx = (uint32_t)lane + 32u * i;
-                        if ((ROWS * 5) % 32 != 0 && idx >= (uint32_t)(ROWS * 5)) break;
+                        if ((ROWS * NCH) % 32 != 0 && idx >= (uint32_t)(ROWS * NCH)) break;
                         const uint32_t ch = idx / ROWS;
-                        cp_async_16(st_s + r * 80 + ch * 16, win + ch * 16, (ch == 4 && !odd) ? 8u : 16u);
+                        cp_async_16(st_s + r * WIN + ch * 16, win + ch * 16, (ch == NCH - 1 && !odd) ? 8u : 16u);
                     }
                 } else {
 #pragma unroll
@@ -772,7 +875,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                     const size_t rem = (size_t)(i_scend - ea);
                     if constexpr (FMT != 0) {
 #pragma unroll
-                        for (uint32_t w = 0; w < 3; ++w) {
+                        for (uint32_t w = 0; w < NSW; ++w) {
                             const size_t r4 = rem > 4 * w ? rem - 4 * w : 0;
                             cp_async_4(st_s + STAGE_QS + lane * SLOT + 4 * w, r4 ? ea + 4 * w : ea,
                                        r4 < 4 ? (uint32_t)r4 : 4u);
@@ -789,7 +892,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 const uint32_t ch_lo = s_lo >> 1, ch_hi = (s_hi + 1) >> 1;        // 16-byte chunks needed
                 const uint8_t* qrow = P.qs + ((size_t)row0 * P.nb + ic.blk) * QB;
                 const size_t row_bytes = (size_t)P.nb * QB;
-                if constexpr (FMT == 2) {
+                if constexpr (FMT >= 2) {
                     // rows that exist: their whole window, as in the common case; others: zeros
                     const uint32_t r = (uint32_t)lane & (ROWS - 1);
                     const bool ok = row0 + r < P.N;
@@ -797,12 +900,12 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                     const uint32_t odd = (uint32_t)reinterpret_cast<uintptr_t>(blkp) & 8u;
                     const uint8_t* win = blkp - odd;
 #pragma unroll
-                    for (int i = 0; i < (ROWS * 5 + 31) / 32; ++i) {
+                    for (int i = 0; i < (ROWS * NCH + 31) / 32; ++i) {
                         const uint32_t idx = (uint32_t)lane + 32u * i;
-                        if ((ROWS * 5) % 32 != 0 && idx >= (uint32_t)(ROWS * 5)) break;
+                        if ((ROWS * NCH) % 32 != 0 && idx >= (uint32_t)(ROWS * NCH)) break;
                         const uint32_t ch = idx / ROWS;
-                        cp_async_16(st_s + r * 80 + ch * 16, ok ? win + ch * 16 : P.qs,
-                                    ok ? ((ch == 4 && !odd) ? 8u : 16u) : 0u);
+                        cp_async_16(st_s + r * WIN + ch * 16, ok ? win + ch * 16 : P.qs,
+                                    ok ? ((ch == NCH - 1 && !odd) ? 8u : 16u) : 0u);
                     }
                 } else {
 #pragma unroll
@@ -822,7 +925,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                     const size_t ea = e & ~(size_t)3, total = (size_t)P.N * P.nb * SC_B;
                     if constexpr (FMT != 0) {
 #pragma unroll
-                        for (uint32_t w = 0; w < 3; ++w) {
+                        for (uint32_t w = 0; w < NSW; ++w) {
                             const size_t at = ea + 4 * w;
                             const uint32_t nbytes = ok && at < total ? (uint32_t)min((size_t)4, total - at) : 0u;
                             cp_async_4(st_s + STAGE_QS + lane * SLOT + 4 * w, P.sc + (nbytes ? at : 0), nbytes);
@@ -858,7 +961,25 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
 
     // ---- the decode table, built from the 1.5 KB compact copy: row e = 32 copies (one per lane)
     // ---- of the grid selector of code e, then (e < 128) 32 copies of the sign selector of index e
-    if constexpr (FMT == 2) {
+    if constexpr (FMT == 3) {
+        // IQ3_S: grid index low | hb << 8 at low * 256 + hb * 128: 32 copies of its four magnitude
+        // bytes; then row n (64 KB + n * 128) = 16 copies of {0xFF in byte j for bit j of n set,
+        // the same bytes' low bits}
+        for (int c = threadIdx.x; c < LUT_BYTES_3S / 16; c += blockDim.x) {
+            uint4 v;
+            if (c < 4096) {
+                const uint32_t gv = IQ3S_GRID[(c >> 4) | (((c >> 3) & 1) << 8)];
+                v = make_uint4(gv, gv, gv, gv);
+            } else {
+                const uint32_t n = (uint32_t)(c - 4096) >> 3;
+                uint32_t mask = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) mask |= ((n >> j) & 1u) * (0xFFu << (8 * j));
+                v = make_uint4(mask, mask & 0x01010101u, mask, mask & 0x01010101u);
+            }
+            *reinterpret_cast<uint4*>(smem + gap + c * 16) = v;
+        }
+    } else if constexpr (FMT == 2) {
         // IQ2_S: 64-byte rows of 16 copies: row 4 * low + qh2 (< 1024) = the grid selector of
         // grid entry low | qh2 << 8 (nibble j: the magnitude code of weight j); then sign row s =
         // the sign selector of sign byte s (nibble j: 4 when bit j is set)
@@ -1031,6 +1152,13 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
         dk.qfill = l16 * 0x01010101u;
         dk.lutw = lut_s;
     }
+    if constexpr (FMT == 3) {
+        dk.xsel = (2u * t) | ((2u * t + 1u) << 4);
+        dk.qsh = 2u * (uint32_t)t;
+        dk.qfill = ((uint32_t)lane * 4u) * 0x0101u | (lut_s & 0xFFFF0000u);
+        dk.sbase = (lut_s + 65536u) | (((uint32_t)lane & 15u) * 8u);
+        dk.st8 = 8u * (uint32_t)t;
+    }
     const uint32_t swz = (uint32_t)((g >> 1) & 3);  // rows g, g+8, g+16, g+24 share it
     const uint32_t rowbase = (uint32_t)g * 64u;     // rows tt*16+g (+8): rowbase + tt*1024 (+512)
 
@@ -1078,13 +1206,20 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
             const uint32_t odd = (cc.blk & 1u) ^ c_dpar;
             const uint32_t so = odd ? 4u : 2u;
             const uint32_t slot_s = st_s + STAGE_QS + (uint32_t)g * SLOT;
-            const uint32_t rb = FMT == 2 ? (uint32_t)g * 80u + odd * 8u : rowbase;
-            if (s_lo == 0 && s_hi == 8)
+            const uint32_t rb = FMT >= 2 ? (uint32_t)g * (uint32_t)WIN + odd * 8u : rowbase;
+            if constexpr (FMT == 3) {
+                // (IQ3_S: one scale per sub-block, one MMA)
+                if (s_lo == 0 && s_hi == 8)
+                    stage_compute_3s<NT, T, false, S_::SPLIT, SLOT>(dk, st_s, xbp, s_lo, s_hi, rb, slot_s + so, I);
+                else
+                    stage_compute_3s<NT, T, true, S_::SPLIT, SLOT>(dk, st_s, xbp, s_lo, s_hi, rb, slot_s + so, I);
+            } else if (s_lo == 0 && s_hi == 8) {
                 stage_compute_xs<NT, T, false, S_::SPLIT, FMT, SLOT>(dk, st_s, xbp, s_lo, s_hi, rb, swz, slot_s, so,
                                                                      t < 2, I);
-            else
+            } else {
                 stage_compute_xs<NT, T, true, S_::SPLIT, FMT, SLOT>(dk, st_s, xbp, s_lo, s_hi, rb, swz, slot_s, so,
                                                                     t < 2, I);
+            }
         } else if (s_lo == 0 && s_hi == 8) {
             stage_compute<NT, T, false, FUSED, S_::SPLIT>(dk, st_s, xbp, xsp, s_lo, s_hi, rowbase, swz, I);
         } else {
@@ -1106,8 +1241,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const __grid_c
                 const uint32_t r0 = tt * 16 + g, r1 = r0 + 8;
                 const uint32_t w0 = ld_shared_u32_volatile(st_s + STAGE_QS + r0 * SLOT);
                 const uint32_t w1 = ld_shared_u32_volatile(st_s + STAGE_QS + r1 * SLOT);
-                const float d0 = half_bits_to_float(prmt(w0, 0u, dsel));
-                const float d1 = half_bits_to_float(prmt(w1, 0u, dsel));
+                // (IQ3_S: its scale d (1 + 2s) has no /8, which the column scales carry)
+                const float d0 = half_bits_to_float(prmt(w0, 0u, dsel)) * (FMT == 3 ? 8.0f : 1.0f);
+                const float d1 = half_bits_to_float(prmt(w1, 0u, dsel)) * (FMT == 3 ? 8.0f : 1.0f);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     F[tt][nt][0] = fmaf((float)I[tt][nt][0], d0 * cs[nt].x, F[tt][nt][0]);
@@ -1363,6 +1499,7 @@ size_t smem_for_variant(int nt, int limbs, uint32_t nb) {
 size_t smem_for_nt(int nt, int limbs, bool fused, uint32_t nb, int fmt = 0) {
     if (fmt == 1) return smem_for_variant<1>(nt, limbs, nb);  // IQ2_XS
     if (fmt == 2) return smem_for_variant<2>(nt, limbs, nb);  // IQ2_S
+    if (fmt == 3) return smem_for_variant<3>(nt, limbs, nb);  // IQ3_S
     if (limbs == 1) {
         switch (nt) {
             case 1: return smem_for<1, 1>(fused, nb);
@@ -1412,7 +1549,8 @@ int max_active_clusters(int num_sms) {
 
 // max_cl: clusters the device can run at once (0 when only the workspace size is wanted).
 // w8a8: the activations as the W8A8 mode's int8 (one limb, m <= 32).
-// fmt: the weight format (0 IQ2_XXS, 1 IQ2_XS, 2 IQ2_S; only IQ2_XXS makes its x limbs in the GEMV).
+// fmt: the weight format (0 IQ2_XXS, 1 IQ2_XS, 2 IQ2_S, 3 IQ3_S; only IQ2_XXS makes its x limbs in
+// the GEMV).
 GroupPlan plan_group(const GemvProblemHost* probs, uint32_t count, uint32_t m, int max_cl, bool w8a8 = false,
                      int fmt = 0) {
     GroupPlan pl;
@@ -1686,7 +1824,7 @@ cudaError_t launch_gemv(const void* x, int x_dtype, uint32_t m, const uint8_t* q
     return launch_gemv_group(&p, 1, m, x_dtype, workspace, num_sms, stream);
 }
 
-bool gemv_variant_ok(int variant) { return variant == 1 || variant == 2; }
+bool gemv_variant_ok(int variant) { return variant >= 1 && variant <= 3; }
 
 size_t gemv_variant_workspace_size(int variant, uint32_t m, uint32_t n, uint32_t k) {
     if (!gemv_variant_ok(variant)) return 0;
@@ -1716,8 +1854,11 @@ cudaError_t launch_gemv_variant(int variant, const void* x, int x_dtype, uint32_
     GemvProblemHost p{x, qs, sc, n, k, out};
     const GroupPlan pl = plan_group(&p, 1, m, max_active_clusters(num_sms), false, variant);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    return variant == 1 ? launch_gemv_fmt<1>(p, m, x_dtype, ws, pl, stream)
-                        : launch_gemv_fmt<2>(p, m, x_dtype, ws, pl, stream);
+    switch (variant) {
+        case 1: return launch_gemv_fmt<1>(p, m, x_dtype, ws, pl, stream);
+        case 2: return launch_gemv_fmt<2>(p, m, x_dtype, ws, pl, stream);
+        default: return launch_gemv_fmt<3>(p, m, x_dtype, ws, pl, stream);
+    }
 }
 
 cudaError_t launch_gemv_generic(const void* x, int x_dtype, uint32_t m, const uint8_t* qs,

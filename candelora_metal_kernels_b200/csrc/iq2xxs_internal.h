@@ -67,8 +67,8 @@ cudaError_t launch_gemv_w8a8(const void* x, int x_dtype, uint32_t m, const uint8
 cudaError_t launch_gemv(const void* x, int x_dtype, uint32_t m, const uint8_t* qs, const uint8_t* sc,
                         uint32_t n, uint32_t k, float* out, void* workspace, int num_sms,
                         cudaStream_t stream);
-// The same decode GEMV for IQ2_XS and IQ2_S weights (variant 1 or 2 as IQ2_VARIANT_*; m <=
-// kGemvMaxM; qs 16-byte and sc 4-byte aligned). gemv_variant_ok: the formats it takes.
+// The same decode GEMV for IQ2_XS, IQ2_S and IQ3_S weights (variant 1, 2 or 3 as IQ2_VARIANT_*;
+// m <= kGemvMaxM; qs 16-byte and sc 4-byte aligned). gemv_variant_ok: the formats it takes.
 bool gemv_variant_ok(int variant);
 size_t gemv_variant_workspace_size(int variant, uint32_t m, uint32_t n, uint32_t k);
 cudaError_t launch_gemv_variant(int variant, const void* x, int x_dtype, uint32_t m, const uint8_t* qs,

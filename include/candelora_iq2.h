@@ -87,7 +87,7 @@ int iq2_abi_version(void);
 int iq2_device_check(void);
 
 /* Bytes of device scratch iq2_matmul needs for this problem. 0 means none: workspace may then be NULL.
- * IQ2_XS, IQ2_S and IQ3_S with m > 32, and IQ2_XS and IQ2_S with m <= 32, report the workspace of their
+ * IQ2_XS, IQ2_S and IQ3_S report the workspace of their
  * tensor-core path (the GEMM; the decode GEMV's x limbs); a call of theirs without it is still
  * valid and runs the f32 CUDA-core kernel instead. */
 size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, int x_dtype,
@@ -103,7 +103,7 @@ size_t iq2_matmul_workspace_size(uint32_t m, uint32_t out_dim, uint32_t in_dim, 
  * decode; x in 28-bit fixed point for m <= 4, rel. error ~1e-6, and 16-bit above, ~4e-5), larger
  * m the tcgen05 GEMM (bf16 operands, f32 accumulate). IQ2_XS, IQ2_S and IQ3_S with m > 32 and a
  * workspace of iq2_matmul_workspace_size bytes run the same tcgen05 GEMM (weights decoded to
- * bf16), IQ2_XS and IQ2_S with m <= 32 and that workspace the decode GEMV (as IQ2_XXS); otherwise an f32
+ * bf16), with m <= 32 and that workspace the decode GEMV (as IQ2_XXS); otherwise an f32
  * CUDA-core kernel (src/iq2_matmul.rs:884-1016 numerics, FMA accumulate).
  */
 int iq2_matmul(const void* x, int x_dtype, uint32_t m, const uint8_t* weight_bytes,

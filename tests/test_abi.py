@@ -80,11 +80,11 @@ def test_workspace_query_needs_no_device(lib):
     assert lib.iq2_matmul_workspace_size(16, 4096, 4096, 0, 0) > 0  # x limbs go through the workspace
     assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 0) == 0  # small K: limbs made in shared memory
     assert lib.iq2_matmul_workspace_size(0, 4096, 4096, 0, 0) == 0
-    # IQ2_XS and IQ2_S at m <= 32: their decode GEMV's x limbs (always through the workspace); IQ3_S
-    # at m <= 32 runs a kernel without scratch; above, every format reports the tensor-core GEMM's
+    # IQ2_XS, IQ2_S and IQ3_S at m <= 32: their decode GEMV's x limbs (always through the
+    # workspace); above, every format reports the tensor-core GEMM's
     assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 1) > 0
     assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 2) > 0
-    assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 3) == 0
+    assert lib.iq2_matmul_workspace_size(1, 4096, 4096, 0, 3) > 0
     assert lib.iq2_matmul_workspace_size(64, 4096, 4096, 0, 3) > 0
 
 

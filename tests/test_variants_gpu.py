@@ -161,12 +161,13 @@ def test_variant_w8a8_gemm(oracle, variant):
     assert rel_l2(y, ref) <= GEMM_ORACLE_TOL
 
 
-@pytest.mark.parametrize("variant", ["iq2_xs", "iq2_s"])
+@pytest.mark.parametrize("variant", ["iq2_xs", "iq2_s", "iq3_s"])
 @pytest.mark.parametrize("m", [1, 3, 8, 16, 32])
 def test_variant_decode_gemv(oracle, variant, m):
-    """IQ2_XS and IQ2_S at m <= 32 on the IQ2_XXS decode GEMV (int8 tensor-core decode; two MMAs
-    per sub-block, one per 16-weight scale), selected when the call has the workspace the size
-    query reports: against the oracle and the CUDA-core kernel (no workspace), f32 x, ragged K."""
+    """IQ2_XS, IQ2_S and IQ3_S at m <= 32 on the IQ2_XXS decode GEMV (int8 tensor-core decode;
+    IQ2_XS / IQ2_S: two MMAs per sub-block, one per 16-weight scale; IQ3_S: magnitudes 1..15 signed
+    by a byte mask), selected when the call has the workspace the size query reports: against the
+    oracle and the CUDA-core kernel (no workspace), f32 x, ragged K."""
     var = VARIANTS[variant][0]
     n, k = 1000, 4096 + 256 + 96
     wb, ws = _blocks(variant, n, k, seed=40 + m)
