@@ -38,6 +38,12 @@
 //   * Grouped launches serve up to 256 projections (e.g. q/k/v or gate/up sharing x) with one
 //     prep and one GEMV launch. Kernels use programmatic dependent launch: before its wait a
 //     GEMV only builds its constant table and prefetches its first weights into L2.
+//   * The other formats (template parameter FMT, single projections, x limbs from the prep
+//     kernel; reference decode_iq2_xs_value / decode_iq2_s_value / decode_iq3_s_value,
+//     iq2_matmul.metal:736-866): IQ2_XS and IQ2_S keep the selector decode with their larger grids
+//     and run two MMAs per sub-block for their 16-weight scales; IQ3_S's grid holds the int8
+//     magnitudes themselves and its signs are applied with a byte mask. Their blocks that are not
+//     16-byte aligned (IQ2_S 72 bytes, IQ3_S 104) are staged as aligned windows around them.
 #include "iq2xxs_common.cuh"
 #include "iq2xxs_codebook.h"
 #include "iq2_variant_grids.h"
